@@ -1,0 +1,360 @@
+"""Benchmark: µs per layer of SeoulKV4 sparse decode at 128K context on B200.
+
+One step = one decode of one query token through one layer (4 KV heads,
+16 query heads, d=256): coarse -> fine -> Stage-1.5 -> Stage-1.6 -> Stage-II
+-> FP8 attention.  Each step uses a fresh Q; L2 is flushed (a 256 MiB write)
+before every timed step, so the index planes are read cold.  With
+``--gpus N`` (torchrun), every rank decodes its own independent layer (weak
+scaling, no collective on the data path); the reported value is the
+whole-job time per layer, max over ranks.
+
+``--impl reference`` times the CPU restatement of the reference pipeline
+(the reference ships no runnable CPU decode; its device path needs a
+Tenstorrent board) on this host's cores, on a bounded sample of steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "µs/layer sparse decode at 128K ctx; top-100 ID parity vs ref; achieved HBM GB/s"
+UNIT = "µs/layer"
+CONFIG_INDEX = 1  # 1xB200 headline profile
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    p.add_argument("--context", type=int, default=131072)
+    p.add_argument("--nprobe", type=int, default=384)
+    p.add_argument("--e2e-steps", type=int, default=200)
+    p.add_argument("--cpu-steps", type=int, default=2)
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler (SM clock + throttle reasons) around the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_layer(context, nprobe, seed, device):
+    from seoulkv_b200 import SeoulKV4Index, synthetic
+
+    k, v, mixes = synthetic.make_kv(context, seed=seed)
+    index = SeoulKV4Index.build(k, v, sink=128, local=256, nprobe=nprobe, build_device=device)
+    return k, v, mixes, index
+
+
+def oracle_cells(k, index):
+    from oracle import oracle as O
+    from seoulkv_b200.index import device_view
+
+    kb = k.contiguous().view(torch.int16).numpy().view(np.uint16)
+    scales, p2, r2, r4 = O.key_codec(kb)
+    cells = []
+    for g, c in enumerate(index.cells()):
+        dv = device_view(c)
+        cells.append(O.CellInputs(
+            nc=dv["nc"], nprobe=dv["nprobe"], lam=dv["lam"], upper=dv["upper"], lower=dv["lower"],
+            coarse_scale4=dv["coarse_scale4"], fine_scale=dv["fine_scale"], resid_bf16=dv["resid_bf16"],
+            offsets=dv["offsets"], values=dv["values"], context=k.shape[1],
+            prefix2=p2[g], residual2=r2[g], residual4=r4[g], key_scale=scales[g]))
+    return cells
+
+
+def oracle_decode(cells, q, k8, v8, context, pool: ThreadPoolExecutor):
+    """CPU restatement of one decode step (4 KV heads in parallel threads)."""
+    from oracle import oracle as O
+
+    qb = q.contiguous().view(torch.int16).numpy().view(np.uint16).reshape(16, 256)
+    res = list(pool.map(lambda g: O.run_cell(cells[g], qb[4 * g:4 * g + 4]), range(4)))
+    out = np.zeros((16, 256), np.uint16)
+    for j in range(16):
+        g, h = divmod(j, 4)
+        keys = O.attention_keys(context, 128, 256, res[g]["final_ids"][h])
+        out[j] = O.attention(qb[j], k8[g], v8[g], keys)
+    return res, out
+
+
+def run_reference(args):
+    """CPU arm: the oracle port of the reference pipeline on host cores."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    cores = os.cpu_count() or 1
+    seed = CONFIG_INDEX * 1000
+    dev = "cuda:0" if torch.cuda.is_available() else "cpu"
+    k, v, mixes, index = make_layer(args.context, args.nprobe, seed, dev)
+    from seoulkv_b200 import synthetic
+
+    cells = oracle_cells(k, index)
+    k8 = O.fp8_e4m3(k.float().numpy())
+    v8 = O.fp8_e4m3(v.float().numpy())
+    steps = max(1, min(args.steps, args.cpu_steps))
+    warm = max(0, min(args.warmup, 1))
+    qs = [synthetic.make_query(args.context, mixes, seed=seed + 1 + i) for i in range(steps + warm)]
+    with ThreadPoolExecutor(max_workers=min(4, cores)) as pool:
+        for i in range(warm):
+            oracle_decode(cells, qs[i], k8, v8, args.context, pool)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            oracle_decode(cells, qs[warm + i], k8, v8, args.context, pool)
+        dt = time.perf_counter() - t0
+    us = dt / steps * 1e6
+    line = {
+        "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f64-exact dots, f32 post-ops, bf16 scores", "data": "synthetic (BASELINE generator, seeded)",
+        "impl": "reference",
+        "config": {"workload": "1 layer, 1 query token, T=131072, 4 KV / 16 Q heads, d=256, nprobe=384",
+                   "context": args.context, "nprobe": args.nprobe},
+        "cpu_baseline": {"value": us, "unit": UNIT, "cores": min(4, cores), "kind": "port",
+                         "sample": f"{steps} decode steps (fresh Q each) of the 128K layer, 4 KV heads on "
+                                   f"{min(4, cores)} threads; C restatement of the reference funnel"},
+        "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world, rank, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    from seoulkv_b200 import SeoulKV4, SeoulKV4Config, synthetic
+
+    seed = CONFIG_INDEX * 1000 + rank
+    k, v, mixes, index = make_layer(args.context, args.nprobe, seed, str(device))
+    n_q = args.warmup + args.steps
+    qs_host = [synthetic.make_query(args.context, mixes, seed=seed * 7919 + i) for i in range(max(n_q, args.e2e_steps + 2))]
+    q_dev = torch.stack([q.reshape(16, 256) for q in qs_host[:n_q]]).to(device)
+    attn = SeoulKV4(device=device, k=k, v=v, index=index, config=SeoulKV4Config(debug=True))
+    attn.run(qs_host[0])
+    attn.synchronize()
+    eng = attn._engine
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    qbits = q_dev.view(torch.int16)
+
+    def step(i):
+        eng.bind_query(qbits[i].data_ptr(), True, stream.cuda_stream)
+        eng.run(stream.cuda_stream)
+
+    for i in range(args.warmup):
+        flush.zero_()
+        step(i)
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = Clocks(local)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    clocks.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step(args.warmup + i)
+        ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    per = np.array([s.elapsed_time(e) for s, e in zip(starts, ends)]) * 1e3  # µs
+    total_us = float(per.sum())
+    if world > 1:
+        t = torch.tensor([total_us], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_us = float(t.item())
+    eng.sync()  # status check of the last step
+    value = total_us / (world * args.steps)
+
+    # per-kernel device times (non-graph launches, L2 flushed before each)
+    prof = {}
+    for _ in range(5):
+        flush.zero_()
+        step(args.warmup)  # same Q as a timed step, then re-run kernel by kernel
+        torch.cuda.synchronize(device)
+        flush.zero_()
+        eng.bind_query(qbits[args.warmup].data_ptr(), True, stream.cuda_stream)
+        for name, ms in eng.profile_step(stream.cuda_stream):
+            prof.setdefault(name, []).append(ms)
+    prof = {n: float(np.mean(v)) * 1e3 for n, v in prof.items()}  # µs
+    traffic = eng.traffic()
+    stage_bytes = {"k_coarse": traffic["coarse"], "k_fine": traffic["fine"], "k_s16": traffic["stage16"],
+                   "k_s2": traffic["stage2"], "k_attn": traffic["attention"]}
+    top = max(prof, key=prof.get)
+    dom = top if top in stage_bytes else max(stage_bytes, key=lambda n: prof.get(n, 0))
+    peak, peak_kind = peaks()
+    achieved = stage_bytes[dom] / (prof[dom] * 1e-6) / 1e9
+    roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+            "traffic": None, "algorithmic_bytes": stage_bytes[dom], "kernel_us": prof[dom]}
+    ncu_note = ROOT / "profiles" / "coarse_128k_traffic.json"
+    if ncu_note.exists():
+        try:
+            roof["traffic"] = json.loads(ncu_note.read_text()).get(dom)
+        except Exception:
+            pass
+
+    # parity of one timed step against the CPU restatement + CPU baseline timing
+    parity, cpu_line = None, None
+    if rank == 0 and world == 1:
+        from oracle import oracle as O
+
+        cells = oracle_cells(k, index)
+        k8 = O.fp8_e4m3(k.float().numpy())
+        v8 = O.fp8_e4m3(v.float().numpy())
+        qi = args.warmup + args.steps - 1
+        step(qi)
+        ids = eng.debug_ids()[0]
+        out = eng.output_host()[0]
+        cores = min(4, os.cpu_count() or 1)
+        with ThreadPoolExecutor(max_workers=cores) as pool:
+            qcpu = q_dev[qi].cpu().reshape(1, 1, 16, 256)
+            t0 = time.perf_counter()
+            res, ref_out = oracle_decode(cells, qcpu, k8, v8, args.context, pool)
+            cpu_us = (time.perf_counter() - t0) * 1e6
+            for i in range(1, args.cpu_steps):
+                t0 = time.perf_counter()
+                oracle_decode(cells, qs_host[i].cpu(), k8, v8, args.context, pool)
+                cpu_us = min(cpu_us, (time.perf_counter() - t0) * 1e6)
+        want = np.stack([r["final_ids"] for r in res])
+        err = np.abs(O.bf16_to_f32(out).astype(np.float64) - O.bf16_to_f32(ref_out).astype(np.float64))
+        parity = {"ids_bit_exact": bool(np.array_equal(ids, want)), "out_max_abs": float(err.max()),
+                  "out_mean_abs": float(err.mean()), "tolerance": [2e-2, 2e-3]}
+        cpu_line = {"value": cpu_us, "unit": UNIT, "cores": cores, "kind": "port",
+                    "sample": f"best of {args.cpu_steps} decode steps of this 128K layer (C restatement, "
+                              f"4 KV heads on {cores} threads)"}
+
+    # end to end through the public API: pinned host Q -> run -> to_torch
+    e2e = None
+    if rank == 0:
+        qp = [q.pin_memory() for q in qs_host[:args.e2e_steps + 2]]
+        for i in range(2):
+            attn.run(qp[i]).to_torch()
+        t0 = time.perf_counter()
+        for i in range(args.e2e_steps):
+            attn.run(qp[i + 2]).to_torch()
+        e2e_us = (time.perf_counter() - t0) / args.e2e_steps * 1e6
+        e2e = {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": 16 * 256 * 2,
+               "d2h_bytes_per_step": 16 * 256 * 2, "timing": "host wall clock incl. sync, L2 warm"}
+
+    if rank == 0:
+        st = eng.status()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": value / 1e3, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64-exact dots, f32 softmax, bf16 scores, fp8 K/V",
+            "data": "synthetic (BASELINE generator, seeded), fresh Q per step",
+            "config": {"workload": "1 layer, 1 query token, T=131072, 4 KV / 16 Q heads, d=256, nprobe=384, "
+                                   "sink=128, local=256, top-100",
+                       "context": args.context, "nprobe": args.nprobe, "l2": "flushed before every step",
+                       "parallelism": f"{world} independent layers (one per GPU)" if world > 1 else "1 GPU"},
+            "p50_us": float(np.percentile(per, 50)), "p99_us": float(np.percentile(per, 99)),
+            "tokens_per_s": 1e6 / value,
+            "roofline": roof, "kernel_us": prof, "algorithmic_bytes_per_step": traffic,
+            "live_counts": {"survivors_max": st.survivors_max, "pool_min": st.pool_min, "pool_max": st.pool_max,
+                            "union15_max": st.union15_max, "union16_max": st.union16_max},
+            "parity": parity, "cpu_baseline": cpu_line, "e2e": e2e, "clocks": clk,
+            "gpu_launches": eng.kernels_per_step() * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    attn.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

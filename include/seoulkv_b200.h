@@ -1,0 +1,157 @@
+/*
+ * seoulkv_b200.h -- C ABI of the B200 SeoulKV4 sparse-decode engine.
+ *
+ * Plain C types only: device and host buffers are raw pointers with sizes,
+ * streams are `void*` (a cudaStream_t; NULL is CUDA's legacy default stream).
+ * Every function returns 0 on success and a negative SKV_E_* code on error;
+ * skv_last_error() then describes the failure (thread-local).
+ *
+ * One engine instance serves `n_slots` independent cache snapshots (a slot
+ * is one request, or one layer of a stack).  Each slot has four KV heads
+ * ("cells") with their own index.  One skv_run() decodes one query token for
+ * every slot.
+ *
+ * Counterparts in the reference (daniel-geon-park/SeoulKV, src/seoulkv4):
+ *   skv_create        SeoulKV4.__init__                       api.py:16-55
+ *   skv_upload_index  index upload inside _runtime.initialize   _runtime.py:36-47
+ *   skv_upload_kv     key planes + FP8 [V|K] record upload       _runtime.py:48-92
+ *   skv_bind_query    SeoulKV4._bind_query / query_prepare.bind api.py:70-73,
+ *                                                            _kernels/query_prepare/host.py:309-319
+ *   skv_run           _runtime.enqueue (4 programs, no sync)     _runtime.py:189-194
+ *   skv_sync          SeoulKV4.synchronize                     api.py:104-107
+ *   skv_status        capacity / live-count checks              _kernels/stage1_fine/seoulkv4_stage1_live.py:72-77,
+ *                                                            _kernels/stage15/seoulkv4_stage15_ingest.py:38-42
+ *   skv_debug_ids     SeoulKV4.debug_snapshot                  api.py:119-126
+ *   skv_output        DecodeResult.to_torch / device_tensors   result.py:25-38
+ *   skv_destroy       SeoulKV4.close                           api.py:128-137
+ */
+#ifndef SEOULKV_B200_H
+#define SEOULKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SKV_OK 0
+#define SKV_E_INVALID (-1)    /* bad argument, shape or state            */
+#define SKV_E_CUDA (-2)       /* a CUDA runtime call failed              */
+#define SKV_E_CAPACITY (-3)   /* a live count left its allowed range     */
+#define SKV_E_STATE (-4)      /* wrong lifecycle order (e.g. run before upload) */
+
+/* Status word bits reported per cell by the device (skv_status). */
+#define SKV_STATUS_POOL_OVER 1u   /* Stage-1.5 pool larger than capacity  */
+#define SKV_STATUS_POOL_UNDER 2u  /* Stage-1.5 pool smaller than 2048     */
+#define SKV_STATUS_FINE_SHORT 4u  /* a head had fewer than nprobe survivors */
+
+typedef struct SkvDesc {
+    int32_t n_slots;          /* independent caches decoded per run        */
+    int32_t context;          /* T, tokens per cache                       */
+    int32_t sink;             /* dense prefix tokens                       */
+    int32_t local;            /* dense suffix tokens                       */
+    int32_t nc;               /* centroids per KV head (multiple of 32)    */
+    int32_t stage15_capacity; /* pool slots per KV head                    */
+    int32_t device;           /* CUDA device ordinal                       */
+    int32_t flags;            /* reserved, 0                               */
+} SkvDesc;
+
+/* One KV head's index in the engine layout (host memory). */
+typedef struct SkvCellView {
+    int32_t nc;
+    int32_t nprobe;               /* multiple of 16 in [16, min(512, nc)] */
+    float lam;                    /* interval lambda                      */
+    int32_t n_postings;           /* offsets[nc]                          */
+    const uint8_t *upper;         /* [nc][64]  code >> 2, 4 codes/byte LE */
+    const uint8_t *lower;         /* [nc][64]  code & 3                   */
+    const float *coarse_scale4;   /* [nc/32]   group scale / 4            */
+    const float *fine_scale;      /* [nc/32]   FP16 group fine scale      */
+    const uint16_t *resid_bf16;   /* [nc]      BF16 residual norm         */
+    const int32_t *offsets;       /* [nc+1]    CSR offsets                */
+    const int32_t *values;        /* [n_postings] token ids               */
+    const int32_t *mates;         /* [n_postings] other list of the token, or -1 */
+} SkvCellView;
+
+typedef struct SkvStatus {
+    uint32_t flags;               /* OR of SKV_STATUS_* over all cells    */
+    int32_t first_bad_cell;       /* -1 when flags == 0                   */
+    int32_t survivors_max;        /* largest coarse survivor count        */
+    int32_t pool_max;             /* largest Stage-1.5 pool               */
+    int32_t pool_min;             /* smallest Stage-1.5 pool              */
+    int32_t union15_max;          /* largest Stage-1.5 union              */
+    int32_t union16_max;          /* largest Stage-II candidate set       */
+    int32_t reserved;
+} SkvStatus;
+
+const char *skv_last_error(void);
+const char *skv_version(void);
+
+int skv_create(const SkvDesc *desc, void **handle);
+void skv_destroy(void *handle);
+
+/* cells[4] for one slot.  Copies everything; the caller keeps ownership. */
+int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells);
+
+/* K and V: BF16 bit patterns [4][T][256] for one slot, host or device memory.
+ * Builds the key code planes and the FP8-e4m3 [K|V] records on the GPU. */
+int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t *v,
+                  int32_t on_device);
+
+/* Q: BF16 bit patterns [n_slots][16][256], host or device memory.  Host
+ * memory is staged through a pinned buffer; the copy is ordered on `stream`. */
+int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *stream);
+
+/* Enqueue the whole funnel for every slot on `stream` (no host sync). */
+int skv_run(void *handle, void *stream);
+
+/* Wait for all work of this engine, then check the device status words:
+ * returns SKV_E_CAPACITY if any cell reported a live count out of range. */
+int skv_sync(void *handle);
+int skv_status(void *handle, SkvStatus *out);
+
+/* Output BF16 bit patterns [n_slots][16][256].  to_host=1 copies to `out`
+ * (synchronising), to_host=0 writes the device pointer into *(void**)out. */
+int skv_output(void *handle, void *out, int32_t to_host);
+
+/* Selected token ids of the last run: int32 [n_slots][4][4][100] (KV head,
+ * query head, rank).  Synchronises. */
+int skv_debug_ids(void *handle, int32_t *out);
+
+/* Intermediate buffers of the last run, for diagnostics and parity tests.
+ * `which` selects one of SKV_STAGE_*; copies at most `bytes` bytes of the
+ * given slot's four cells (cell-major) and returns the byte count in *written. */
+#define SKV_STAGE_COUNTS 0      /* int32 [4][8]: ntags,nsel,npool,nu15,ncand,status,0,0 */
+#define SKV_STAGE_THRESH 1      /* uint16 [4][4] coarse thresholds (BF16 bits) */
+#define SKV_STAGE_TAGS 2        /* uint32 [4][nc] survivor tags                */
+#define SKV_STAGE_SELECTED 3    /* int32 [4][2048] Fine cluster ids            */
+#define SKV_STAGE_POOL 4        /* int32 [4][capacity] pool token ids          */
+#define SKV_STAGE_U15 5         /* int32 [4][6400] pool positions              */
+#define SKV_STAGE_CAND 6        /* int32 [4][1024] Stage-1.5 union positions   */
+#define SKV_STAGE_FINAL_POS 7   /* int32 [4][4][100] Stage-1.5 union positions */
+#define SKV_STAGE_LOHI 8        /* uint16 [4][2][4][nc] coarse lo, hi (BF16)   */
+int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
+                   size_t *written);
+
+/* Bytes the funnel read on the last run (from the live counts): the
+ * algorithmic traffic used for roofline reporting, per stage, summed over slots. */
+typedef struct SkvTraffic {
+    double coarse, fine, stage15, stage16, stage2, attention, total;
+} SkvTraffic;
+int skv_traffic(void *handle, SkvTraffic *out);
+
+/* One decode step launched kernel by kernel (no graph) with a CUDA event
+ * between kernels; writes each kernel's device time in milliseconds to
+ * kernel_ms[0..n) (n = min(max_kernels, kernels per step)) and n to
+ * *n_kernels.  Synchronises.  For profiling; results equal skv_run's. */
+int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_kernels,
+                     int32_t *n_kernels);
+/* Name of kernel i of one step (static string; "" when out of range). */
+const char *skv_kernel_name(int32_t i);
+/* Kernels one skv_run enqueues. */
+int32_t skv_kernels_per_step(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SEOULKV_B200_H */

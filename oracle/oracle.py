@@ -1,0 +1,297 @@
+"""TEST INFRASTRUCTURE ONLY: CPU restatement of the SeoulKV4 decode funnel.
+
+This module is the parity checker for the CUDA engine.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import it;
+the product path (``seoulkv_b200``) never does, and fails loudly when its own
+CUDA library is missing instead of falling back here.
+
+The funnel arithmetic lives in ``skv_oracle.c`` (built into
+``oracle/libskv_oracle.so`` by :func:`build`); this file adds the pieces that
+are plain array work:
+
+* ``key_codec`` restates ``_stage15_key_codec``/``encode_planes``
+  (reference ``src/seoulkv4/_codecs/keys.py:16-44``);
+* ``fp8_e4m3`` is the K/V record conversion of ``src/seoulkv4/_runtime.py:76-92``
+  (canonically ``torch.float8_e4m3fn``: round to nearest even, NaN above 464);
+* ``attention`` restates the sink + local + top-100 softmax of
+  ``src/seoulkv4/_kernels/codegen/attention.py:83-146`` with the score scale
+  ``D**-0.5`` of ``src/seoulkv4/_kernels/stage16/seoulkv4_stage16_fused.py:1607``,
+  in float64.
+
+Parity of the funnel is pinned against the reference's own helper oracles by
+the fixtures under ``tests/golden`` (see ``tests/golden/make_golden.py``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libskv_oracle.so"
+D = 256
+G = 4
+
+# Fixed funnel budgets of the reference profile (src/seoulkv4/config.py:25-40).
+M15 = 2048
+UNION15 = 1600
+M16 = 256
+TOPK = 100
+
+
+def build(force: bool = False) -> Path:
+    """Compile the C restatement (gcc, no FMA contraction)."""
+    src = HERE / "skv_oracle.c"
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.check_call(
+            ["gcc", "-O2", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
+             "-std=c11", "-o", str(LIB_PATH), str(src), "-lm"]
+        )
+    return LIB_PATH
+
+
+class _Cell(ctypes.Structure):
+    _fields_ = [
+        ("nc", ctypes.c_int32),
+        ("nprobe", ctypes.c_int32),
+        ("lam", ctypes.c_float),
+        ("upper", ctypes.c_void_p),
+        ("lower", ctypes.c_void_p),
+        ("coarse_scale4", ctypes.c_void_p),
+        ("fine_scale", ctypes.c_void_p),
+        ("resid_bf16", ctypes.c_void_p),
+        ("offsets", ctypes.c_void_p),
+        ("values", ctypes.c_void_p),
+        ("context", ctypes.c_int32),
+        ("prefix2", ctypes.c_void_p),
+        ("residual2", ctypes.c_void_p),
+        ("residual4", ctypes.c_void_p),
+        ("key_scale", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        _lib = ctypes.CDLL(str(LIB_PATH))
+        _lib.skv_oracle_query_bytes.restype = ctypes.c_size_t
+        _lib.skv_oracle_bf16_rne.restype = ctypes.c_uint16
+        _lib.skv_oracle_bf16_rne.argtypes = [ctypes.c_float]
+        for name in ("skv_oracle_coarse", "skv_oracle_fine", "skv_oracle_pool",
+                     "skv_oracle_stage15", "skv_oracle_stage16"):
+            getattr(_lib, name).restype = ctypes.c_int
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> ctypes.c_void_p:
+    assert a.flags["C_CONTIGUOUS"]
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+# ----------------------------------------------------------- array helpers
+
+
+def bf16_bits(x) -> np.ndarray:
+    """FP32 -> BF16 bit patterns, round to nearest even (NaN kept quiet)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF
+    r = np.where(nan, ((u >> 16) | 0x40) & 0xFFFF, r)
+    return r.astype(np.uint16)
+
+
+def bf16_to_f32(bits) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _pack_low(values: np.ndarray, bits: int) -> np.ndarray:
+    per = 8 // bits
+    v = values.astype(np.uint16).reshape(*values.shape[:-1], -1, per)
+    shifts = (np.arange(per, dtype=np.uint16) * bits)
+    return (v << shifts).sum(axis=-1).astype(np.uint8)
+
+
+def key_codec(k_bf16_bits: np.ndarray):
+    """Per-(head, dim) max-abs 8-bit key codes and their three bit planes.
+
+    ``k_bf16_bits``: uint16 [G, T, 256] BF16 patterns.  Returns
+    ``(scales [G,256] f32, prefix2 [G,T,64], residual2 [G,T,64], residual4 [G,T,128])``.
+    Each FP32 operation is one IEEE operation, as in the reference's torch code.
+    """
+    import torch
+
+    kf = torch.from_numpy(np.ascontiguousarray(k_bf16_bits).view(np.int16)).view(torch.bfloat16).float()
+    scales = kf.abs().amax(dim=1).clamp_min(1e-9)
+    step8 = (2 * scales) / 256
+    code8 = torch.clamp(torch.floor((kf + scales[:, None, :]) / step8[:, None, :]), 0, 255).to(torch.uint8)
+    del kf
+
+    def pack(vals, bits_):
+        per = 8 // bits_
+        v = vals.reshape(*vals.shape[:-1], -1, per).to(torch.int32)
+        acc = v[..., 0]
+        for j in range(1, per):
+            acc = acc | (v[..., j] << (bits_ * j))
+        return acc.to(torch.uint8).numpy()
+
+    return (
+        scales.numpy().astype(np.float32),
+        pack(code8 >> 6, 2),
+        pack((code8 >> 4) & 3, 2),
+        pack(code8 & 15, 4),
+    )
+
+
+def fp8_e4m3(x_f32: np.ndarray) -> np.ndarray:
+    """Decoded FP8-e4m3 values (as float64) of FP32 inputs via torch's cast."""
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(x_f32, dtype=np.float32))
+    return t.to(torch.float8_e4m3fn).to(torch.float64).numpy()
+
+
+# ------------------------------------------------------------ the funnel
+
+
+class CellInputs:
+    """Host arrays of one KV head in the engine's layout."""
+
+    def __init__(self, *, nc, nprobe, lam, upper, lower, coarse_scale4, fine_scale,
+                 resid_bf16, offsets, values, context, prefix2, residual2, residual4,
+                 key_scale):
+        self.arrays = dict(
+            upper=np.ascontiguousarray(upper, dtype=np.uint8),
+            lower=np.ascontiguousarray(lower, dtype=np.uint8),
+            coarse_scale4=np.ascontiguousarray(coarse_scale4, dtype=np.float32),
+            fine_scale=np.ascontiguousarray(fine_scale, dtype=np.float32),
+            resid_bf16=np.ascontiguousarray(resid_bf16, dtype=np.uint16),
+            offsets=np.ascontiguousarray(offsets, dtype=np.int32),
+            values=np.ascontiguousarray(values, dtype=np.int32),
+            prefix2=np.ascontiguousarray(prefix2, dtype=np.uint8),
+            residual2=np.ascontiguousarray(residual2, dtype=np.uint8),
+            residual4=np.ascontiguousarray(residual4, dtype=np.uint8),
+            key_scale=np.ascontiguousarray(key_scale, dtype=np.float32),
+        )
+        self.nc, self.nprobe, self.lam, self.context = int(nc), int(nprobe), float(lam), int(context)
+        a = self.arrays
+        self.struct = _Cell(
+            nc=self.nc, nprobe=self.nprobe, lam=self.lam,
+            upper=_ptr(a["upper"]), lower=_ptr(a["lower"]),
+            coarse_scale4=_ptr(a["coarse_scale4"]), fine_scale=_ptr(a["fine_scale"]),
+            resid_bf16=_ptr(a["resid_bf16"]), offsets=_ptr(a["offsets"]),
+            values=_ptr(a["values"]), context=self.context,
+            prefix2=_ptr(a["prefix2"]), residual2=_ptr(a["residual2"]),
+            residual4=_ptr(a["residual4"]), key_scale=_ptr(a["key_scale"]),
+        )
+
+
+class OracleError(RuntimeError):
+    """A decode the reference would reject (pool outside [2048, capacity])."""
+
+    def __init__(self, message, status):
+        super().__init__(message)
+        self.status = status
+
+
+def run_cell(cell: CellInputs, q_bits: np.ndarray, *, capacity: int = 13056,
+             m15: int = M15, union15: int = UNION15, m16: int = M16, topk: int = TOPK):
+    """Run the funnel for one KV head; ``q_bits``: uint16 [4, 256] BF16 patterns.
+
+    Returns a dict with every intermediate (see skv_oracle.c).
+    """
+    L = lib()
+    q_bits = np.ascontiguousarray(q_bits, dtype=np.uint16).reshape(G, D)
+    qbuf = ctypes.create_string_buffer(L.skv_oracle_query_bytes())
+    L.skv_oracle_prepare_query(_ptr(q_bits), _ptr(cell.arrays["key_scale"]),
+                               ctypes.c_float(cell.lam), qbuf)
+    out = {}
+    # OracleQuery leading fields: qb f32[4][256], q15 u16[4][256], qs u16[4][256], qn, qsum
+    raw = bytes(qbuf)
+    off = 0
+    out["qb"] = np.frombuffer(raw, np.float32, G * D, off).reshape(G, D); off += 4 * G * D
+    out["q15"] = np.frombuffer(raw, np.uint16, G * D, off).reshape(G, D); off += 2 * G * D
+    out["qs"] = np.frombuffer(raw, np.uint16, G * D, off).reshape(G, D); off += 2 * G * D
+    out["qn"] = np.frombuffer(raw, np.float32, G, off).copy(); off += 4 * G
+    out["qsum"] = np.frombuffer(raw, np.float32, G, off).copy()
+
+    nc = cell.nc
+    lo = np.zeros((G, nc), np.uint16)
+    hi = np.zeros((G, nc), np.uint16)
+    th = np.zeros(G, np.uint16)
+    tags = np.zeros(nc, np.uint32)
+    s = ctypes.byref(cell.struct)
+    ntags = L.skv_oracle_coarse(s, qbuf, _ptr(lo), _ptr(hi), _ptr(th), _ptr(tags))
+    out.update(lo=lo, hi=hi, thresh=th, tags=tags[:ntags].copy())
+
+    P = cell.nprobe
+    fscores = np.zeros((G, max(ntags, 1)), np.uint16)
+    ftop = np.zeros((G, P), np.int32)
+    selected = np.zeros(G * P, np.int32)
+    nsel = L.skv_oracle_fine(s, qbuf, _ptr(tags), ntags, _ptr(fscores), _ptr(ftop), _ptr(selected))
+    if nsel < 0:
+        raise OracleError("a query head has fewer than nprobe coarse survivors", 3)
+    out.update(fine_scores=fscores[:, :ntags], fine_top=ftop, selected=selected[:nsel].copy())
+
+    pool = np.zeros(max(capacity, 1), np.int32)
+    npool = L.skv_oracle_pool(s, _ptr(selected), nsel, _ptr(pool), capacity)
+    out["pool_size"] = npool
+    if npool > capacity:
+        raise OracleError(f"Stage-1.5 pool {npool} exceeds capacity {capacity}", 1)
+    if npool < m15:
+        raise OracleError(f"Stage-1.5 pool {npool} below {m15}", 2)
+    pool = pool[:npool].copy()
+    out["pool"] = pool
+
+    s15 = np.zeros((G, npool), np.uint16)
+    top15 = np.full((G, union15), -1, np.int32)
+    u15 = np.zeros(G * union15, np.int32)
+    nu = L.skv_oracle_stage15(s, qbuf, _ptr(pool), npool, union15, _ptr(s15), _ptr(top15), _ptr(u15))
+    u15 = u15[:nu].copy()
+    out.update(s15_scores=s15, s15_top=top15, u15=u15)
+
+    s16 = np.zeros((G, nu), np.uint16)
+    top16 = np.full((G, m16), -1, np.int32)
+    cand = np.zeros(G * m16, np.int32)
+    ncand = L.skv_oracle_stage16(s, qbuf, _ptr(pool), _ptr(u15), nu, m16, _ptr(s16), _ptr(top16), _ptr(cand))
+    cand = cand[:ncand].copy()
+    out.update(s16_scores=s16, s16_top=top16, cand=cand)
+
+    s2 = np.zeros((G, ncand), np.uint16)
+    fpos = np.zeros((G, topk), np.int32)
+    fids = np.zeros((G, topk), np.int32)
+    L.skv_oracle_stage2(s, qbuf, _ptr(pool), _ptr(u15), _ptr(cand), ncand, topk,
+                        _ptr(s2), _ptr(fpos), _ptr(fids))
+    out.update(s2_scores=s2, final_pos=fpos, final_ids=fids)
+    return out
+
+
+def attention_keys(context: int, sink: int, local: int, ids: np.ndarray) -> np.ndarray:
+    """Key order of one query head: sink, local, then top-100 in rank order."""
+    return np.concatenate([
+        np.arange(sink, dtype=np.int64),
+        np.arange(context - local, context, dtype=np.int64),
+        np.asarray(ids, dtype=np.int64),
+    ])
+
+
+def attention(q_bits: np.ndarray, k8: np.ndarray, v8: np.ndarray, keys: np.ndarray) -> np.ndarray:
+    """One query head: softmax(q.k/16) v over FP8-decoded K/V rows, float64.
+
+    ``q_bits`` uint16 [256]; ``k8``/``v8`` float64 [T, 256] decoded FP8.
+    Returns the BF16 output bit patterns [256].
+    """
+    q = bf16_to_f32(q_bits).astype(np.float64)
+    kk = k8[keys]
+    s = (kk @ q) / 16.0
+    s = s - s.max()
+    p = np.exp(s)
+    o = (p[:, None] * v8[keys]).sum(axis=0) / p.sum()
+    return bf16_bits(o.astype(np.float32))

@@ -1,0 +1,221 @@
+"""ctypes binding of ``include/seoulkv_b200.h`` (the engine's C ABI).
+
+There is no CPU fallback: if the sm_100a library cannot be loaded, every
+entry point raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import numpy as np
+
+from seoulkv_b200 import _build
+
+SKV_STATUS_POOL_OVER = 1
+SKV_STATUS_POOL_UNDER = 2
+SKV_STATUS_FINE_SHORT = 4
+SKV_E_CAPACITY = -3
+
+STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8)
+
+EXPORTS = (
+    "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
+    "skv_upload_kv", "skv_bind_query", "skv_run", "skv_sync", "skv_status", "skv_output",
+    "skv_debug_ids", "skv_read_stage", "skv_traffic", "skv_profile_step", "skv_kernel_name",
+    "skv_kernels_per_step",
+)
+
+
+class SkvDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("n_slots", "context", "sink", "local", "nc", "stage15_capacity", "device", "flags")]
+
+
+class SkvCellView(ctypes.Structure):
+    _fields_ = [
+        ("nc", ctypes.c_int32), ("nprobe", ctypes.c_int32), ("lam", ctypes.c_float),
+        ("n_postings", ctypes.c_int32),
+        ("upper", ctypes.c_void_p), ("lower", ctypes.c_void_p), ("coarse_scale4", ctypes.c_void_p),
+        ("fine_scale", ctypes.c_void_p), ("resid_bf16", ctypes.c_void_p), ("offsets", ctypes.c_void_p),
+        ("values", ctypes.c_void_p), ("mates", ctypes.c_void_p),
+    ]
+
+
+class SkvStatus(ctypes.Structure):
+    _fields_ = [("flags", ctypes.c_uint32)] + [(n, ctypes.c_int32) for n in (
+        "first_bad_cell", "survivors_max", "pool_max", "pool_min", "union15_max", "union16_max", "reserved")]
+
+
+class SkvTraffic(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_double) for n in
+                ("coarse", "fine", "stage15", "stage16", "stage2", "attention", "total")]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def library_path() -> Path:
+    return _build.LIB
+
+
+def load() -> ctypes.CDLL:
+    """Load (building first if stale and nvcc exists) the CUDA library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB
+        try:
+            if _build.stale():
+                _build.build()
+        except Exception as exc:  # no nvcc: only an existing library will do
+            if not path.exists():
+                raise RuntimeError(f"seoulkv_b200 CUDA library missing and cannot be built: {exc}") from exc
+        if not path.exists():
+            raise RuntimeError(f"seoulkv_b200 CUDA library missing: {path}")
+        lib = ctypes.CDLL(str(path))
+        for name in EXPORTS:
+            getattr(lib, name)  # raises AttributeError if an export is missing
+        lib.skv_last_error.restype = ctypes.c_char_p
+        lib.skv_version.restype = ctypes.c_char_p
+        lib.skv_create.argtypes = [ctypes.POINTER(SkvDesc), ctypes.POINTER(ctypes.c_void_p)]
+        lib.skv_destroy.argtypes = [ctypes.c_void_p]
+        lib.skv_destroy.restype = None
+        lib.skv_upload_index.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(SkvCellView)]
+        lib.skv_upload_kv.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_int32]
+        lib.skv_bind_query.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        lib.skv_run.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.skv_sync.argtypes = [ctypes.c_void_p]
+        lib.skv_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(SkvStatus)]
+        lib.skv_output.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]
+        lib.skv_debug_ids.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.skv_read_stage.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                       ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]
+        lib.skv_traffic.argtypes = [ctypes.c_void_p, ctypes.POINTER(SkvTraffic)]
+        lib.skv_profile_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                         ctypes.POINTER(ctypes.c_int32)]
+        lib.skv_kernel_name.restype = ctypes.c_char_p
+        lib.skv_kernel_name.argtypes = [ctypes.c_int32]
+        lib.skv_kernels_per_step.restype = ctypes.c_int32
+        _lib = lib
+        return lib
+
+
+class NativeError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().skv_last_error().decode(errors="replace")
+        raise NativeError(rc, f"{what}: {msg}")
+
+
+def _ptr(a: np.ndarray) -> ctypes.c_void_p:
+    assert a.flags["C_CONTIGUOUS"]
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class Engine:
+    """One engine instance: ``n_slots`` caches x 4 KV heads on one CUDA device."""
+
+    def __init__(self, *, n_slots: int, context: int, sink: int, local: int, nc: int,
+                 capacity: int, device: int):
+        self.lib = load()
+        self.n_slots, self.context, self.nc, self.capacity = n_slots, context, nc, capacity
+        self.sink, self.local, self.device = sink, local, device
+        desc = SkvDesc(n_slots=n_slots, context=context, sink=sink, local=local, nc=nc,
+                       stage15_capacity=capacity, device=device, flags=0)
+        h = ctypes.c_void_p()
+        check(self.lib.skv_create(ctypes.byref(desc), ctypes.byref(h)), "skv_create")
+        self.handle = h
+        self._keep = []
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.skv_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def upload_index(self, slot: int, views: list[dict]) -> None:
+        arrs = []
+        cells = (SkvCellView * 4)()
+        for g, v in enumerate(views):
+            a = {k: np.ascontiguousarray(v[k]) for k in
+                 ("upper", "lower", "coarse_scale4", "fine_scale", "resid_bf16", "offsets", "values", "mates")}
+            arrs.append(a)
+            cells[g] = SkvCellView(
+                nc=int(v["nc"]), nprobe=int(v["nprobe"]), lam=float(v["lam"]),
+                n_postings=int(len(a["values"])),
+                **{k: _ptr(x) for k, x in a.items()},
+            )
+        check(self.lib.skv_upload_index(self.handle, slot, cells), "skv_upload_index")
+
+    def upload_kv(self, slot: int, k_ptr: int, v_ptr: int, on_device: bool) -> None:
+        check(self.lib.skv_upload_kv(self.handle, slot, ctypes.c_void_p(k_ptr), ctypes.c_void_p(v_ptr),
+                                     int(on_device)), "skv_upload_kv")
+
+    def bind_query(self, q_ptr: int, on_device: bool, stream: int = 0) -> None:
+        check(self.lib.skv_bind_query(self.handle, ctypes.c_void_p(q_ptr), int(on_device),
+                                      ctypes.c_void_p(stream or None)), "skv_bind_query")
+
+    def run(self, stream: int = 0) -> None:
+        check(self.lib.skv_run(self.handle, ctypes.c_void_p(stream or None)), "skv_run")
+
+    def sync(self) -> None:
+        check(self.lib.skv_sync(self.handle), "skv_sync")
+
+    def status(self) -> SkvStatus:
+        s = SkvStatus()
+        check(self.lib.skv_status(self.handle, ctypes.byref(s)), "skv_status")
+        return s
+
+    def output_host(self) -> np.ndarray:
+        out = np.empty((self.n_slots, 16, 256), dtype=np.uint16)
+        check(self.lib.skv_output(self.handle, _ptr(out), 1), "skv_output")
+        return out
+
+    def output_device_ptr(self) -> int:
+        p = ctypes.c_void_p()
+        check(self.lib.skv_output(self.handle, ctypes.byref(p), 0), "skv_output")
+        return int(p.value)
+
+    def debug_ids(self) -> np.ndarray:
+        out = np.empty((self.n_slots, 4, 4, 100), dtype=np.int32)
+        check(self.lib.skv_debug_ids(self.handle, _ptr(out)), "skv_debug_ids")
+        return out
+
+    def read_stage(self, slot: int, which: str, dtype, shape) -> np.ndarray:
+        out = np.zeros(shape, dtype=dtype)
+        written = ctypes.c_size_t()
+        check(self.lib.skv_read_stage(self.handle, slot, STAGE[which], _ptr(out), out.nbytes,
+                                      ctypes.byref(written)), "skv_read_stage")
+        return out
+
+    def profile_step(self, stream: int = 0) -> list[tuple[str, float]]:
+        """One non-graph step with per-kernel device times (ms)."""
+        ms = np.zeros(64, dtype=np.float32)
+        n = ctypes.c_int32()
+        check(self.lib.skv_profile_step(self.handle, ctypes.c_void_p(stream or None), _ptr(ms), 64,
+                                        ctypes.byref(n)), "skv_profile_step")
+        return [(self.lib.skv_kernel_name(i).decode(), float(ms[i])) for i in range(n.value)]
+
+    def kernels_per_step(self) -> int:
+        return int(self.lib.skv_kernels_per_step())
+
+    def traffic(self) -> dict:
+        t = SkvTraffic()
+        check(self.lib.skv_traffic(self.handle, ctypes.byref(t)), "skv_traffic")
+        return {n: getattr(t, n) for n, _ in SkvTraffic._fields_}

@@ -1,0 +1,204 @@
+"""Public SeoulKV4 lifecycle on a B200 (mirrors ``src/seoulkv4/api.py:14-145``).
+
+``SeoulKV4(device=..., k=..., v=..., index=..., config=...)`` validates and
+keeps the inputs; the first ``run(q)`` uploads the index, key planes and FP8
+records, captures the decode step as a CUDA graph and runs it; later calls
+only copy Q and replay the graph on the current PyTorch stream.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from seoulkv_b200 import _native
+from seoulkv_b200.config import (
+    MAX_CONTEXT, MIN_CONTEXT, N_HEADS, N_KV_HEADS, STAGE15_M, SeoulKV4Config, validate_nprobe,
+)
+from seoulkv_b200.index import SeoulKV4Index, device_view
+from seoulkv_b200.result import DecodeResult
+
+
+def _cuda_index(device) -> int:
+    if device is None:
+        raise ValueError("supply a caller-owned CUDA device")
+    dev = torch.device(device if not isinstance(device, int) else f"cuda:{device}")
+    if dev.type != "cuda":
+        raise ValueError("SeoulKV4 runs on a CUDA device")
+    return dev.index if dev.index is not None else torch.cuda.current_device()
+
+
+def _bits(t: torch.Tensor) -> torch.Tensor:
+    return t.contiguous().view(torch.int16)
+
+
+class SeoulKV4:
+    """Static-cache sparse decode: one request, one query token per run."""
+
+    def __init__(self, *, device, k: torch.Tensor, v: torch.Tensor, index: SeoulKV4Index,
+                 config: SeoulKV4Config | None = None):
+        self._config = SeoulKV4Config() if config is None else config
+        if not isinstance(self._config, SeoulKV4Config) or not isinstance(index, SeoulKV4Index):
+            raise TypeError("expected SeoulKV4Config and SeoulKV4Index")
+        self._device_index = _cuda_index(device)
+        context = index.zones.context
+        if not MIN_CONTEXT <= context <= MAX_CONTEXT or context % 4:
+            raise ValueError("unsupported context for the fixed SeoulKV4 candidate/tag profile")
+        for name, value in (("K", k), ("V", v)):
+            if (not isinstance(value, torch.Tensor) or value.dtype != torch.bfloat16
+                    or value.device.type not in ("cpu", "cuda")
+                    or tuple(value.shape) != (N_KV_HEADS, context, 256)):
+                raise ValueError(f"expected BF16 {name} [4,{context},256]")
+        index._check_keys(k.cpu() if k.device.type != "cpu" else k)
+        nc = min(int(c["centroids"].shape[0]) for c in index.cells())
+        self._nprobe = (validate_nprobe(self._config.nprobe, nc) if self._config.nprobe is not None
+                        else index.nprobe)
+        self._index = index
+        self._host_kv = (k, v)
+        self._engine: _native.Engine | None = None
+        self._generation = 0
+        self._closed = False
+
+    # -------------------------------------------------------------- state
+
+    def _require_open(self):
+        if self._closed:
+            raise RuntimeError("SeoulKV4 is closed")
+
+    def _require_initialized(self):
+        self._require_open()
+        if self._engine is None:
+            raise RuntimeError("run(q) must initialize SeoulKV4 first")
+        return self._engine
+
+    @property
+    def initialized(self) -> bool:
+        return self._engine is not None
+
+    @staticmethod
+    def _validate_query(q):
+        if (not isinstance(q, torch.Tensor) or q.dtype != torch.bfloat16
+                or q.device.type not in ("cpu", "cuda") or tuple(q.shape) != (1, 1, N_HEADS, 256)):
+            raise ValueError("expected BF16 Q [1,1,16,256]")
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self._device_index).cuda_stream
+
+    def _initialize(self):
+        zones = self._index.zones
+        cells = self._index.cells()
+        nc = int(cells[0]["centroids"].shape[0])
+        if any(int(c["centroids"].shape[0]) != nc for c in cells):
+            raise ValueError("all four index cells must have the same centroid count")
+        eng = _native.Engine(n_slots=1, context=zones.context, sink=zones.sink, local=zones.local,
+                             nc=nc, capacity=self._config.stage15_capacity, device=self._device_index)
+        try:
+            eng.upload_index(0, [device_view(c, p) for c, p in zip(cells, self._nprobe)])
+            k, v = self._host_kv
+            if k.device.type == "cuda":
+                kb, vb = _bits(k.to(f"cuda:{self._device_index}")), _bits(v.to(f"cuda:{self._device_index}"))
+                eng.upload_kv(0, kb.data_ptr(), vb.data_ptr(), True)
+            else:
+                kb, vb = _bits(k), _bits(v)
+                eng.upload_kv(0, kb.data_ptr(), vb.data_ptr(), False)
+        except Exception:
+            eng.close()
+            raise
+        return eng
+
+    # -------------------------------------------------------------- public
+
+    def run(self, q: torch.Tensor) -> DecodeResult:
+        """Initialise on the first call, then bind Q and enqueue the decode step."""
+        self._require_open()
+        self._validate_query(q)
+        first = self._engine is None
+        if first:
+            self._engine = self._initialize()
+            self._host_kv = None
+        self._bind_query(q)
+        self._engine.run(self._stream())
+        self._generation += 1
+        if first:
+            # the reference's first run checks the live pool against capacity
+            st = self._engine.status()
+            if st.flags:
+                raise ValueError(
+                    f"live Stage-I key counts [{st.pool_min}, {st.pool_max}] outside "
+                    f"[{STAGE15_M},{self._config.stage15_capacity}] (status {st.flags:#x}); "
+                    "change capacity, never truncate")
+        return DecodeResult(self, self._generation)
+
+    def _bind_query(self, q: torch.Tensor) -> None:
+        self._validate_query(q)
+        eng = self._require_initialized()
+        if q.device.type == "cuda":
+            qd = _bits(q.to(f"cuda:{self._device_index}"))
+            eng.bind_query(qd.data_ptr(), True, self._stream())
+        else:
+            qh = _bits(q)
+            eng.bind_query(qh.data_ptr(), False, self._stream())
+
+    def synchronize(self) -> None:
+        """Wait for the last run; raises RuntimeError if a live count left its range."""
+        self._require_open()
+        if self._engine is not None:
+            try:
+                self._engine.sync()
+            except _native.NativeError as exc:
+                raise RuntimeError(str(exc)) from exc
+
+    def metadata(self) -> dict:
+        """Host-only configuration; never reads device tensors."""
+        self._require_open()
+        zones = self._index.zones
+        meta = {
+            "initialized": self.initialized,
+            "cache_layout": "flat",
+            "index": self._index.metadata(),
+            "nprobe": list(self._nprobe),
+        }
+        if self.initialized:
+            meta.update(
+                implementation="coarse 2-bit intervals -> fine 4-bit top-nprobe -> spill-2 pool -> "
+                               "2-bit top-1600 union -> 4-bit top-256 union -> 8-bit exact top-100 -> "
+                               "FP8 sink+local+top-100 attention",
+                device=torch.cuda.get_device_name(self._device_index),
+                attention_zones=zones.metadata(),
+                attention_kv_dtype="FP8_E4M3",
+                kernels_per_step=16,
+                stage15_capacity=self._config.stage15_capacity,
+                graph_replay=True,
+            )
+        return meta
+
+    def debug_snapshot(self) -> dict:
+        """Selected token ids of the latest run: LongTensor [4, 4, 100] (KV group, head, rank)."""
+        eng = self._require_initialized()
+        if not self._config.debug:
+            raise RuntimeError("debug_snapshot requires SeoulKV4Config(debug=True)")
+        self.synchronize()
+        return {"selected_ids": torch.from_numpy(eng.debug_ids()[0]).long()}
+
+    def close(self) -> None:
+        """Release this instance's device buffers after pending work (idempotent)."""
+        if self._closed:
+            return
+        try:
+            if self._engine is not None:
+                try:
+                    self._engine.sync()
+                except _native.NativeError:
+                    pass
+        finally:
+            self._closed = True
+            if self._engine is not None:
+                self._engine.close()
+            self._engine = None
+            self._host_kv = self._index = None
+
+    def __enter__(self):
+        self._require_open()
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        self.close()

@@ -1,0 +1,60 @@
+"""Runtime settings (mirrors ``src/seoulkv4/config.py:1-40`` of the reference)."""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+DEFAULT_NPROBE = 256
+
+# Fixed funnel budgets of the validated profile (reference config.py:25-40).
+N_KV_HEADS = 4
+N_HEADS = 16
+HEAD_DIM = 256
+TOPK = 100
+STAGE15_M = 2048          # per-head frontier; the first 1600 enter the union
+STAGE15_UNION_M = 1600
+STAGE16_M = 256
+MIN_CONTEXT = 6400
+MAX_CONTEXT = 524288      # reference limit (index.py:114); the engine itself takes up to 2^20
+MAX_CENTROIDS = 65536     # Fine's 16-bit survivor positions (index.py:126)
+
+
+def validate_nprobe(nprobe, nc: int) -> tuple[int, ...]:
+    """One value for all heads or four per-head values; multiples of 16 in [16, min(512, nc)]."""
+    if type(nprobe) is int:
+        probes = (nprobe,) * N_KV_HEADS
+    elif isinstance(nprobe, Sequence) and not isinstance(nprobe, (str, bytes)):
+        probes = tuple(nprobe)
+    else:
+        raise ValueError("nprobe must be an integer or four per-head integers")
+    hi = min(512, nc)
+    if len(probes) != N_KV_HEADS or any(type(p) is not int or not 16 <= p <= hi or p % 16 for p in probes):
+        raise ValueError(f"each nprobe must be a multiple of 16 in [16, {hi}]")
+    return probes
+
+
+@dataclass(frozen=True)
+class SeoulKV4Config:
+    """Stage-1.5 key capacity per KV head, diagnostics, optional nprobe override.
+
+    ``stage15_capacity`` must be a multiple of 768 in [12288, 24576]; a live
+    pool above it is reported as an error, never truncated.  ``nprobe``
+    (None = keep the index's value) overrides the index's probe budget for this
+    instance without rebuilding the index.
+    """
+
+    stage15_capacity: int = 13056
+    debug: bool = False
+    nprobe: int | tuple[int, ...] | None = None
+
+    def __post_init__(self):
+        n = self.stage15_capacity
+        if type(n) is not int or not 12288 <= n <= 24576 or n % (6 * 4 * 32):
+            raise ValueError("stage15_capacity must be a multiple of 768 in [12288, 24576]")
+        if type(self.debug) is not bool:
+            raise TypeError("debug must be a bool")
+        if self.nprobe is not None:
+            validate_nprobe(self.nprobe if type(self.nprobe) is int else tuple(self.nprobe), 512)
+            if not isinstance(self.nprobe, int):
+                object.__setattr__(self, "nprobe", tuple(self.nprobe))

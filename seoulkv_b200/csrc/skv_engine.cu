@@ -1,0 +1,570 @@
+// skv_engine.cu -- the C ABI of include/seoulkv_b200.h.
+//
+// The engine owns every device buffer it uses (allocated in skv_create and
+// the upload calls, never in skv_run).  The decode step is captured once into
+// a CUDA graph and replayed on the caller's stream by skv_run.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/seoulkv_b200.h"
+#include "skv_device.cuh"
+#include "skv_kernels.cuh"
+
+using namespace skv;
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string &msg) {
+  g_error = msg;
+  return code;
+}
+
+#define CK(call)                                                                          \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return fail(SKV_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));       \
+  } while (0)
+
+struct CellBufs {
+  uint8_t *upper = nullptr, *lower = nullptr;
+  float *coarse_scale4 = nullptr, *fine_scale = nullptr;
+  uint16_t *resid = nullptr;
+  int32_t *offsets = nullptr, *values = nullptr, *mates = nullptr;
+  uint8_t *prefix2 = nullptr, *residual2 = nullptr, *residual4 = nullptr, *kv8 = nullptr;
+  float *key_scale = nullptr;
+  int32_t n_postings = 0;
+};
+
+struct Engine {
+  SkvDesc desc{};
+  int n_cells = 0;
+  cudaStream_t stream = nullptr;  // internal stream (uploads, capture)
+  std::vector<CellBufs> bufs;
+  std::vector<CellDev> hcells;
+  std::vector<int> index_ok, kv_ok;
+  CellDev *dcells = nullptr;
+  Work work{};
+  std::vector<void *> allocs;     // workspace allocations
+  uint16_t *q_pinned = nullptr;
+  cudaEvent_t q_copied = nullptr, done = nullptr;
+  bool q_pending = false, ran = false;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+template <class T>
+int dalloc(Engine *e, T **p, size_t count) {
+  CK(cudaMalloc(reinterpret_cast<void **>(p), count * sizeof(T) + 16));
+  CK(cudaMemset(*p, 0, count * sizeof(T) + 16));
+  e->allocs.push_back(*p);
+  return SKV_OK;
+}
+
+void free_cell(CellBufs &b, bool index, bool kv) {
+  if (index) {
+    for (void *p : {(void *)b.upper, (void *)b.lower, (void *)b.coarse_scale4, (void *)b.fine_scale,
+                    (void *)b.resid, (void *)b.offsets, (void *)b.values, (void *)b.mates})
+      if (p) cudaFree(p);
+    b.upper = b.lower = nullptr;
+    b.coarse_scale4 = b.fine_scale = nullptr;
+    b.resid = nullptr;
+    b.offsets = b.values = b.mates = nullptr;
+  }
+  if (kv) {
+    for (void *p : {(void *)b.prefix2, (void *)b.residual2, (void *)b.residual4, (void *)b.kv8,
+                    (void *)b.key_scale})
+      if (p) cudaFree(p);
+    b.prefix2 = b.residual2 = b.residual4 = b.kv8 = nullptr;
+    b.key_scale = nullptr;
+  }
+}
+
+template <class T>
+int upload(T **dst, const T *src, size_t count) {
+  CK(cudaMalloc(reinterpret_cast<void **>(dst), count * sizeof(T) + 16));
+  CK(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+  return SKV_OK;
+}
+
+Engine *as_engine(void *h) { return static_cast<Engine *>(h); }
+
+int ready(Engine *e) {
+  for (int i = 0; i < e->n_cells; ++i)
+    if (!e->index_ok[i] || !e->kv_ok[i])
+      return fail(SKV_E_STATE, "cell " + std::to_string(i) + " has no index or K/V uploaded");
+  return SKV_OK;
+}
+
+int sync_done(Engine *e) {
+  CK(cudaSetDevice(e->desc.device));
+  if (e->ran) CK(cudaEventSynchronize(e->done));
+  CK(cudaStreamSynchronize(e->stream));
+  return SKV_OK;
+}
+
+int read_counts(Engine *e, std::vector<int32_t> &c) {
+  c.assign((size_t)e->n_cells * NCOUNT, 0);
+  CK(cudaMemcpy(c.data(), e->work.counts, c.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+  return SKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *skv_last_error(void) { return g_error.c_str(); }
+
+const char *skv_version(void) { return "seoulkv_b200 0.1 (sm_100a)"; }
+
+int skv_create(const SkvDesc *d, void **handle) {
+  if (!d || !handle) return fail(SKV_E_INVALID, "null descriptor or handle");
+  *handle = nullptr;
+  if (d->n_slots < 1 || d->n_slots > 4096) return fail(SKV_E_INVALID, "n_slots must be in [1, 4096]");
+  if (d->context < 1 || d->context > (1 << 20)) return fail(SKV_E_INVALID, "context must be in [1, 2^20]");
+  if (d->sink < 0 || d->local < 0 || d->sink + d->local > d->context)
+    return fail(SKV_E_INVALID, "sink/local must be disjoint and inside the context");
+  if (d->nc < 32 || d->nc % 32 || d->nc > 65536)
+    return fail(SKV_E_INVALID, "nc must be a multiple of 32 in [32, 65536]");
+  if (d->stage15_capacity < M15_MIN || d->stage15_capacity > 65536)
+    return fail(SKV_E_INVALID, "stage15_capacity must be in [2048, 65536]");
+  auto *e = new Engine();
+  e->desc = *d;
+  e->n_cells = d->n_slots * G;
+  int rc;
+#define TRY(x)             \
+  do {                     \
+    rc = (x);              \
+    if (rc) {              \
+      skv_destroy(e);      \
+      return rc;           \
+    }                      \
+  } while (0)
+  {
+    cudaError_t ce = cudaSetDevice(d->device);
+    if (ce != cudaSuccess) {
+      delete e;
+      return fail(SKV_E_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(ce));
+    }
+  }
+  TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) ? fail(SKV_E_CUDA, "stream") : 0);
+  TRY(cudaEventCreateWithFlags(&e->q_copied, cudaEventDisableTiming) ? fail(SKV_E_CUDA, "event") : 0);
+  TRY(cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming) ? fail(SKV_E_CUDA, "event") : 0);
+  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->q_pinned), (size_t)d->n_slots * 16 * D * 2,
+                    cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned query buffer") : 0);
+  TRY(prepare_funnel_attributes() ? fail(SKV_E_CUDA, "kernel attributes") : 0);
+  e->bufs.resize(e->n_cells);
+  e->hcells.assign(e->n_cells, CellDev{});
+  e->index_ok.assign(e->n_cells, 0);
+  e->kv_ok.assign(e->n_cells, 0);
+  Work &w = e->work;
+  const size_t C = e->n_cells, nc = d->nc, cap = d->stage15_capacity;
+  w.n_cells = e->n_cells;
+  w.n_slots = d->n_slots;
+  w.T = d->context;
+  w.sink = d->sink;
+  w.local = d->local;
+  w.nc = d->nc;
+  w.cap = d->stage15_capacity;
+  TRY(dalloc(e, &e->dcells, C));
+  w.cells = e->dcells;
+  uint16_t *q = nullptr;
+  TRY(dalloc(e, &q, (size_t)d->n_slots * 16 * D));
+  w.q = q;
+  TRY(dalloc(e, &w.ops, C * 3 * D * G));
+  TRY(dalloc(e, &w.qscal, C * 8));
+  TRY(dalloc(e, &w.lo, C * G * nc));
+  TRY(dalloc(e, &w.hi, C * G * nc));
+  TRY(dalloc(e, &w.chist, C * G * 256));
+  TRY(dalloc(e, &w.thr, C * 16));
+  TRY(dalloc(e, &w.tags, C * nc));
+  TRY(dalloc(e, &w.fkeys, C * G * nc));
+  TRY(dalloc(e, &w.sel, C * SEL_MAX));
+  TRY(dalloc(e, &w.selbits, C * (nc / 32)));
+  TRY(dalloc(e, &w.pool, C * cap));
+  TRY(dalloc(e, &w.k15, C * G * cap));
+  TRY(dalloc(e, &w.u15pos, C * U15_MAX));
+  TRY(dalloc(e, &w.u15tok, C * U15_MAX));
+  TRY(dalloc(e, &w.k16, C * G * U15_MAX));
+  TRY(dalloc(e, &w.cand, C * CAND_MAX));
+  TRY(dalloc(e, &w.final_pos, C * G * TOPK));
+  TRY(dalloc(e, &w.final_ids, C * G * TOPK));
+  TRY(dalloc(e, &w.counts, C * NCOUNT));
+  TRY(dalloc(e, &w.attn_part, C * G * ATTN_SPLIT * 260));
+  TRY(dalloc(e, &w.out, (size_t)d->n_slots * 16 * D));
+#undef TRY
+  *handle = e;
+  return SKV_OK;
+}
+
+void skv_destroy(void *handle) {
+  Engine *e = as_engine(handle);
+  if (!e) return;
+  cudaSetDevice(e->desc.device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->ran && e->done) cudaEventSynchronize(e->done);
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->graph) cudaGraphDestroy(e->graph);
+  for (auto &b : e->bufs) free_cell(b, true, true);
+  for (void *p : e->allocs) cudaFree(p);
+  if (e->q_pinned) cudaFreeHost(e->q_pinned);
+  if (e->q_copied) cudaEventDestroy(e->q_copied);
+  if (e->done) cudaEventDestroy(e->done);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+static int refresh_cells(Engine *e) {
+  CK(cudaMemcpy(e->dcells, e->hcells.data(), e->hcells.size() * sizeof(CellDev), cudaMemcpyHostToDevice));
+  return SKV_OK;
+}
+
+int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells) {
+  Engine *e = as_engine(handle);
+  if (!e || !cells) return fail(SKV_E_INVALID, "null engine or cells");
+  if (slot < 0 || slot >= e->desc.n_slots) return fail(SKV_E_INVALID, "slot out of range");
+  CK(cudaSetDevice(e->desc.device));
+  CK(cudaStreamSynchronize(e->stream));
+  const int nc = e->desc.nc, T = e->desc.context;
+  for (int g = 0; g < G; ++g) {
+    const SkvCellView &v = cells[g];
+    if (v.nc != nc) return fail(SKV_E_INVALID, "cell nc differs from the engine's nc");
+    if (v.nprobe < 16 || v.nprobe > 512 || v.nprobe % 16 || v.nprobe > nc)
+      return fail(SKV_E_INVALID, "nprobe must be a multiple of 16 in [16, min(512, nc)]");
+    if (!(v.lam >= 0.0f) || v.lam > 3.0e38f) return fail(SKV_E_INVALID, "lam must be finite and >= 0");
+    if (!v.upper || !v.lower || !v.coarse_scale4 || !v.fine_scale || !v.resid_bf16 || !v.offsets ||
+        !v.values || !v.mates)
+      return fail(SKV_E_INVALID, "null index array");
+    if (v.offsets[0] != 0 || v.offsets[nc] != v.n_postings || v.n_postings < 0)
+      return fail(SKV_E_INVALID, "CSR offsets must start at 0 and end at n_postings");
+    for (int i = 0; i < nc; ++i)
+      if (v.offsets[i + 1] < v.offsets[i]) return fail(SKV_E_INVALID, "CSR offsets must be non-decreasing");
+    for (int j = 0; j < v.n_postings; ++j) {
+      if (v.values[j] < 0 || v.values[j] >= T) return fail(SKV_E_INVALID, "CSR token id out of range");
+      if (v.mates[j] < -1 || v.mates[j] >= nc) return fail(SKV_E_INVALID, "posting mate out of range");
+    }
+  }
+  for (int g = 0; g < G; ++g) {
+    const SkvCellView &v = cells[g];
+    const int cell = slot * G + g;
+    CellBufs &b = e->bufs[cell];
+    free_cell(b, true, false);
+    int rc;
+    if ((rc = upload(&b.upper, v.upper, (size_t)nc * 64))) return rc;
+    if ((rc = upload(&b.lower, v.lower, (size_t)nc * 64))) return rc;
+    if ((rc = upload(&b.coarse_scale4, v.coarse_scale4, (size_t)nc / 32))) return rc;
+    if ((rc = upload(&b.fine_scale, v.fine_scale, (size_t)nc / 32))) return rc;
+    if ((rc = upload(&b.resid, v.resid_bf16, (size_t)nc))) return rc;
+    if ((rc = upload(&b.offsets, v.offsets, (size_t)nc + 1))) return rc;
+    if ((rc = upload(&b.values, v.values, (size_t)(v.n_postings > 0 ? v.n_postings : 1)))) return rc;
+    if ((rc = upload(&b.mates, v.mates, (size_t)(v.n_postings > 0 ? v.n_postings : 1)))) return rc;
+    b.n_postings = v.n_postings;
+    CellDev &c = e->hcells[cell];
+    c.upper = b.upper;
+    c.lower = b.lower;
+    c.coarse_scale4 = b.coarse_scale4;
+    c.fine_scale = b.fine_scale;
+    c.resid = b.resid;
+    c.offsets = b.offsets;
+    c.values = b.values;
+    c.mates = b.mates;
+    c.nc = nc;
+    c.nprobe = v.nprobe;
+    c.lam = v.lam;
+    e->index_ok[cell] = 1;
+  }
+  return refresh_cells(e);
+}
+
+int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t *v, int32_t on_device) {
+  Engine *e = as_engine(handle);
+  if (!e || !k || !v) return fail(SKV_E_INVALID, "null engine or K/V");
+  if (slot < 0 || slot >= e->desc.n_slots) return fail(SKV_E_INVALID, "slot out of range");
+  CK(cudaSetDevice(e->desc.device));
+  CK(cudaStreamSynchronize(e->stream));
+  const size_t T = e->desc.context, elems = (size_t)G * T * D;
+  const uint16_t *dk = k, *dv = v;
+  uint16_t *stage = nullptr;
+  if (!on_device) {
+    CK(cudaMalloc(reinterpret_cast<void **>(&stage), 2 * elems * sizeof(uint16_t)));
+    cudaError_t c1 = cudaMemcpy(stage, k, elems * 2, cudaMemcpyHostToDevice);
+    cudaError_t c2 = c1 == cudaSuccess ? cudaMemcpy(stage + elems, v, elems * 2, cudaMemcpyHostToDevice) : c1;
+    if (c2 != cudaSuccess) {
+      cudaFree(stage);
+      return fail(SKV_E_CUDA, std::string("K/V upload: ") + cudaGetErrorString(c2));
+    }
+    dk = stage;
+    dv = stage + elems;
+  }
+  float *scale[G];
+  uint8_t *p2[G], *r2[G], *r4[G], *kv8[G];
+  uint32_t *smax = nullptr;
+  int rc = SKV_OK;
+  for (int g = 0; g < G && rc == SKV_OK; ++g) {
+    CellBufs &b = e->bufs[slot * G + g];
+    free_cell(b, false, true);
+    if (cudaMalloc(reinterpret_cast<void **>(&b.prefix2), T * 64) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.residual2), T * 64) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.residual4), T * 128) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.kv8), T * REC) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.key_scale), D * sizeof(float)) != cudaSuccess)
+      rc = fail(SKV_E_CUDA, "out of device memory for key planes / FP8 records");
+    scale[g] = b.key_scale;
+    p2[g] = b.prefix2;
+    r2[g] = b.residual2;
+    r4[g] = b.residual4;
+    kv8[g] = b.kv8;
+  }
+  if (rc == SKV_OK && cudaMalloc(reinterpret_cast<void **>(&smax), G * D * sizeof(uint32_t)) != cudaSuccess)
+    rc = fail(SKV_E_CUDA, "out of device memory");
+  if (rc == SKV_OK) {
+    cudaError_t ce = launch_key_codec(dk, dv, (int)T, smax, scale, p2, r2, r4, kv8, e->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+    if (ce != cudaSuccess) rc = fail(SKV_E_CUDA, std::string("key codec: ") + cudaGetErrorString(ce));
+  }
+  if (smax) cudaFree(smax);
+  if (stage) cudaFree(stage);
+  if (rc) return rc;
+  for (int g = 0; g < G; ++g) {
+    const int cell = slot * G + g;
+    CellDev &c = e->hcells[cell];
+    c.prefix2 = p2[g];
+    c.residual2 = r2[g];
+    c.residual4 = r4[g];
+    c.kv8 = kv8[g];
+    c.key_scale = scale[g];
+    e->kv_ok[cell] = 1;
+  }
+  return refresh_cells(e);
+}
+
+int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *stream) {
+  Engine *e = as_engine(handle);
+  if (!e || !q) return fail(SKV_E_INVALID, "null engine or query");
+  CK(cudaSetDevice(e->desc.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: legacy default stream
+  const size_t bytes = (size_t)e->desc.n_slots * 16 * D * sizeof(uint16_t);
+  uint16_t *dq = const_cast<uint16_t *>(e->work.q);
+  if (on_device) {
+    CK(cudaMemcpyAsync(dq, q, bytes, cudaMemcpyDeviceToDevice, st));
+    return SKV_OK;
+  }
+  // the pinned staging buffer may still feed the previous copy
+  if (e->q_pending) CK(cudaEventSynchronize(e->q_copied));
+  std::memcpy(e->q_pinned, q, bytes);
+  CK(cudaMemcpyAsync(dq, e->q_pinned, bytes, cudaMemcpyHostToDevice, st));
+  CK(cudaEventRecord(e->q_copied, st));
+  e->q_pending = true;
+  return SKV_OK;
+}
+
+int skv_run(void *handle, void *stream) {
+  Engine *e = as_engine(handle);
+  if (!e) return fail(SKV_E_INVALID, "null engine");
+  int rc = ready(e);
+  if (rc) return rc;
+  CK(cudaSetDevice(e->desc.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: legacy default stream
+  if (!e->exec) {
+    CK(cudaStreamSynchronize(e->stream));
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t le = launch_funnel(e->work, e->stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (le != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return fail(SKV_E_CUDA, std::string("funnel launch: ") + cudaGetErrorString(le));
+    }
+    if (ce != cudaSuccess) return fail(SKV_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    e->graph = g;
+    CK(cudaGraphInstantiate(&e->exec, g, 0));
+  }
+  CK(cudaGraphLaunch(e->exec, st));
+  CK(cudaEventRecord(e->done, st));
+  e->ran = true;
+  return SKV_OK;
+}
+
+int skv_status(void *handle, SkvStatus *out) {
+  Engine *e = as_engine(handle);
+  if (!e || !out) return fail(SKV_E_INVALID, "null engine or output");
+  int rc = sync_done(e);
+  if (rc) return rc;
+  std::vector<int32_t> c;
+  if ((rc = read_counts(e, c))) return rc;
+  SkvStatus s{};
+  s.first_bad_cell = -1;
+  s.pool_min = 1 << 30;
+  for (int i = 0; i < e->n_cells; ++i) {
+    const int32_t *k = &c[(size_t)i * NCOUNT];
+    const uint32_t st = (uint32_t)k[C_STATUS];
+    if (st && s.first_bad_cell < 0) s.first_bad_cell = i;
+    s.flags |= st;
+    s.survivors_max = std::max(s.survivors_max, k[C_TAGS]);
+    s.pool_max = std::max(s.pool_max, k[C_POOL]);
+    s.pool_min = std::min(s.pool_min, k[C_POOL]);
+    s.union15_max = std::max(s.union15_max, k[C_U15]);
+    s.union16_max = std::max(s.union16_max, k[C_CAND]);
+  }
+  *out = s;
+  return SKV_OK;
+}
+
+int skv_sync(void *handle) {
+  Engine *e = as_engine(handle);
+  if (!e) return fail(SKV_E_INVALID, "null engine");
+  if (!e->ran) return sync_done(e);
+  SkvStatus s;
+  int rc = skv_status(handle, &s);
+  if (rc) return rc;
+  if (s.flags) {
+    char msg[256];
+    std::snprintf(msg, sizeof msg,
+                  "live count out of range at cell %d (status 0x%x: %s%s%s); pool range [%d, %d], capacity %d",
+                  s.first_bad_cell, s.flags, (s.flags & SKV_STATUS_POOL_OVER) ? "pool above capacity " : "",
+                  (s.flags & SKV_STATUS_POOL_UNDER) ? "pool below 2048 " : "",
+                  (s.flags & SKV_STATUS_FINE_SHORT) ? "fewer than nprobe survivors" : "", s.pool_min,
+                  s.pool_max, e->desc.stage15_capacity);
+    return fail(SKV_E_CAPACITY, msg);
+  }
+  return SKV_OK;
+}
+
+int skv_output(void *handle, void *out, int32_t to_host) {
+  Engine *e = as_engine(handle);
+  if (!e || !out) return fail(SKV_E_INVALID, "null engine or output");
+  if (!to_host) {
+    *static_cast<void **>(out) = e->work.out;
+    return SKV_OK;
+  }
+  int rc = sync_done(e);
+  if (rc) return rc;
+  CK(cudaMemcpy(out, e->work.out, (size_t)e->desc.n_slots * 16 * D * 2, cudaMemcpyDeviceToHost));
+  return SKV_OK;
+}
+
+int skv_debug_ids(void *handle, int32_t *out) {
+  Engine *e = as_engine(handle);
+  if (!e || !out) return fail(SKV_E_INVALID, "null engine or output");
+  int rc = sync_done(e);
+  if (rc) return rc;
+  CK(cudaMemcpy(out, e->work.final_ids, (size_t)e->n_cells * G * TOPK * sizeof(int32_t),
+                cudaMemcpyDeviceToHost));
+  return SKV_OK;
+}
+
+int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes, size_t *written) {
+  Engine *e = as_engine(handle);
+  if (!e || !dst) return fail(SKV_E_INVALID, "null engine or destination");
+  if (slot < 0 || slot >= e->desc.n_slots) return fail(SKV_E_INVALID, "slot out of range");
+  int rc = sync_done(e);
+  if (rc) return rc;
+  const size_t nc = e->desc.nc, cap = e->desc.stage15_capacity, c0 = (size_t)slot * G;
+  const Work &w = e->work;
+  const void *src = nullptr;
+  size_t n = 0;
+  switch (which) {
+    case SKV_STAGE_COUNTS: src = w.counts + c0 * NCOUNT; n = G * NCOUNT * 4; break;
+    case SKV_STAGE_THRESH: {
+      std::vector<uint32_t> t((size_t)G * 16);
+      CK(cudaMemcpy(t.data(), w.thr + c0 * 16, t.size() * 4, cudaMemcpyDeviceToHost));
+      std::vector<uint16_t> o(G * G);
+      for (int g = 0; g < G; ++g)
+        for (int h = 0; h < G; ++h) {
+          const uint32_t ordv = t[(size_t)g * 16 + T_COARSE * G + h];
+          o[g * G + h] = (uint16_t)((ordv & 0x8000u) ? (ordv ^ 0x8000u) : (~ordv & 0xffffu));
+        }
+      n = std::min(bytes, o.size() * 2);
+      std::memcpy(dst, o.data(), n);
+      if (written) *written = n;
+      return SKV_OK;
+    }
+    case SKV_STAGE_TAGS: src = w.tags + c0 * nc; n = G * nc * 4; break;
+    case SKV_STAGE_SELECTED: src = w.sel + c0 * SEL_MAX; n = (size_t)G * SEL_MAX * 4; break;
+    case SKV_STAGE_POOL: src = w.pool + c0 * cap; n = G * cap * 4; break;
+    case SKV_STAGE_U15: src = w.u15pos + c0 * U15_MAX; n = (size_t)G * U15_MAX * 4; break;
+    case SKV_STAGE_CAND: src = w.cand + c0 * CAND_MAX; n = (size_t)G * CAND_MAX * 4; break;
+    case SKV_STAGE_FINAL_POS: src = w.final_pos + c0 * G * TOPK; n = (size_t)G * G * TOPK * 4; break;
+    case SKV_STAGE_LOHI: {
+      // ordered keys back to BF16 patterns, [cell][lo/hi][head][nc]
+      std::vector<uint16_t> lo(G * G * nc), hi(G * G * nc);
+      CK(cudaMemcpy(lo.data(), w.lo + c0 * G * nc, lo.size() * 2, cudaMemcpyDeviceToHost));
+      CK(cudaMemcpy(hi.data(), w.hi + c0 * G * nc, hi.size() * 2, cudaMemcpyDeviceToHost));
+      std::vector<uint16_t> o(2 * lo.size());
+      auto un = [](uint16_t v) -> uint16_t { return (v & 0x8000u) ? (v ^ 0x8000u) : (uint16_t)~v; };
+      for (int g = 0; g < G; ++g)
+        for (size_t i = 0; i < G * nc; ++i) {
+          o[((size_t)g * 2 + 0) * G * nc + i] = un(lo[(size_t)g * G * nc + i]);
+          o[((size_t)g * 2 + 1) * G * nc + i] = un(hi[(size_t)g * G * nc + i]);
+        }
+      n = std::min(bytes, o.size() * 2);
+      std::memcpy(dst, o.data(), n);
+      if (written) *written = n;
+      return SKV_OK;
+    }
+    default: return fail(SKV_E_INVALID, "unknown stage selector");
+  }
+  n = std::min(n, bytes);
+  CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost));
+  if (written) *written = n;
+  return SKV_OK;
+}
+
+int skv_traffic(void *handle, SkvTraffic *out) {
+  Engine *e = as_engine(handle);
+  if (!e || !out) return fail(SKV_E_INVALID, "null engine or output");
+  int rc = sync_done(e);
+  if (rc) return rc;
+  std::vector<int32_t> c;
+  if ((rc = read_counts(e, c))) return rc;
+  const double nc = e->desc.nc;
+  SkvTraffic t{};
+  for (int i = 0; i < e->n_cells; ++i) {
+    const int32_t *k = &c[(size_t)i * NCOUNT];
+    t.coarse += nc * 64 + nc * 2 + nc / 32 * 4;           // upper plane, residual norm, scales
+    t.fine += (double)k[C_TAGS] * (64 + 64 + 4);          // upper + lower rows of survivors, tags
+    t.stage15 += (double)k[C_POSTINGS] * 8 + (double)std::min(k[C_POOL], e->desc.stage15_capacity) * 64 +
+                 (double)k[C_SEL] * 8;                    // ids + mates, prefixes, offsets
+    t.stage16 += (double)k[C_U15] * (64 + 64);            // prefix2 + residual2
+    t.stage2 += (double)k[C_CAND] * (64 + 64 + 128);      // + residual4
+    t.attention += (double)(e->desc.sink + e->desc.local + G * TOPK) * REC + G * D * 2;
+  }
+  t.total = t.coarse + t.fine + t.stage15 + t.stage16 + t.stage2 + t.attention;
+  *out = t;
+  return SKV_OK;
+}
+
+int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_kernels, int32_t *n_kernels) {
+  Engine *e = as_engine(handle);
+  if (!e || !kernel_ms || !n_kernels) return fail(SKV_E_INVALID, "null engine or output");
+  int rc = ready(e);
+  if (rc) return rc;
+  CK(cudaSetDevice(e->desc.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: legacy default stream
+  const int nk = funnel_kernel_count();
+  std::vector<cudaEvent_t> ev(nk + 1, nullptr);
+  for (auto &x : ev) CK(cudaEventCreate(&x));
+  cudaError_t le = launch_funnel(e->work, st, ev.data());
+  cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(ev[nk]) : le;
+  const int n = std::min<int>(nk, max_kernels);
+  for (int i = 0; i < n && se == cudaSuccess; ++i) se = cudaEventElapsedTime(&kernel_ms[i], ev[i], ev[i + 1]);
+  for (auto &x : ev) cudaEventDestroy(x);
+  if (se != cudaSuccess) return fail(SKV_E_CUDA, std::string("profile step: ") + cudaGetErrorString(se));
+  CK(cudaEventRecord(e->done, st));
+  e->ran = true;
+  *n_kernels = n;
+  return SKV_OK;
+}
+
+const char *skv_kernel_name(int32_t i) { return funnel_kernel_name(i); }
+
+int32_t skv_kernels_per_step(void) { return funnel_kernel_count(); }
+
+}  // extern "C"

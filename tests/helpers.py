@@ -1,0 +1,57 @@
+"""Shared test helpers: seeded cases and oracle runs (test infrastructure)."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import oracle as O
+from seoulkv_b200 import synthetic
+from seoulkv_b200.index import SeoulKV4Index, device_view
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+class Case:
+    """A seeded synthetic cache + index + queries, with oracle results per query."""
+
+    def __init__(self, context=8192, nprobe=128, seed=11, components=256, index=None, sink=128, local=256):
+        self.context, self.sink, self.local = context, sink, local
+        self.k, self.v, self.mixes = synthetic.make_kv(context, seed=seed, components=components)
+        self.index = index or SeoulKV4Index.build(self.k, self.v, sink=sink, local=local, nprobe=nprobe)
+        self.planes = O.key_codec(bits(self.k))
+        self._k8 = self._v8 = None
+
+    def cells(self, nprobe=None):
+        scales, p2, r2, r4 = self.planes
+        out = []
+        for g, c in enumerate(self.index.cells()):
+            dv = device_view(c, None if nprobe is None else nprobe[g])
+            out.append(O.CellInputs(
+                nc=dv["nc"], nprobe=dv["nprobe"], lam=dv["lam"], upper=dv["upper"], lower=dv["lower"],
+                coarse_scale4=dv["coarse_scale4"], fine_scale=dv["fine_scale"], resid_bf16=dv["resid_bf16"],
+                offsets=dv["offsets"], values=dv["values"], context=self.context,
+                prefix2=p2[g], residual2=r2[g], residual4=r4[g], key_scale=scales[g]))
+        return out
+
+    def query(self, seed):
+        return synthetic.make_query(self.context, self.mixes, seed=seed)
+
+    def kv8(self):
+        if self._k8 is None:
+            self._k8 = O.fp8_e4m3(self.k.float().numpy())
+            self._v8 = O.fp8_e4m3(self.v.float().numpy())
+        return self._k8, self._v8
+
+    def oracle(self, q, capacity=13056, nprobe=None):
+        qb = bits(q).reshape(16, 256)
+        res = [O.run_cell(c, qb[4 * g:4 * g + 4], capacity=capacity) for g, c in enumerate(self.cells(nprobe))]
+        k8, v8 = self.kv8()
+        out = np.zeros((16, 256), np.uint16)
+        for j in range(16):
+            g, h = divmod(j, 4)
+            keys = O.attention_keys(self.context, self.sink, self.local, res[g]["final_ids"][h])
+            out[j] = O.attention(qb[j], k8[g], v8[g], keys)
+        return res, out

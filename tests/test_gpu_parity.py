@@ -1,0 +1,77 @@
+"""CUDA engine vs the CPU oracle, stage by stage (bit-exact) and output (tolerance)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from seoulkv_b200 import SeoulKV4, SeoulKV4Config
+from tests.helpers import Case, bits
+
+pytestmark = pytest.mark.gpu
+
+# north_star tolerance for the BF16 attention output
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+@pytest.fixture(scope="module")
+def case():
+    return Case(context=8192, nprobe=128, seed=11)
+
+
+def _compare(eng, res, nc, capacity):
+    counts = eng.read_stage(0, "counts", np.int32, (4, 8))
+    lohi = eng.read_stage(0, "lohi", np.uint16, (4, 2, 4, nc))
+    thresh = eng.read_stage(0, "thresh", np.uint16, (4, 4))
+    tags = eng.read_stage(0, "tags", np.uint32, (4, nc))
+    sel = eng.read_stage(0, "selected", np.int32, (4, 2048))
+    pool = eng.read_stage(0, "pool", np.int32, (4, capacity))
+    u15 = eng.read_stage(0, "u15", np.int32, (4, 6400))
+    cand = eng.read_stage(0, "cand", np.int32, (4, 1024))
+    fpos = eng.read_stage(0, "final_pos", np.int32, (4, 4, 100))
+    for g, r in enumerate(res):
+        assert np.array_equal(lohi[g, 0], r["lo"]), f"cell {g}: coarse lower bounds"
+        assert np.array_equal(lohi[g, 1], r["hi"]), f"cell {g}: coarse upper bounds"
+        assert np.array_equal(thresh[g], r["thresh"]), f"cell {g}: coarse thresholds"
+        n = counts[g, 0]
+        assert n == len(r["tags"]) and np.array_equal(tags[g, :n], r["tags"]), f"cell {g}: survivors"
+        n = counts[g, 1]
+        assert n == len(r["selected"]) and np.array_equal(sel[g, :n], r["selected"]), f"cell {g}: fine union"
+        n = counts[g, 2]
+        assert n == len(r["pool"]) and np.array_equal(pool[g, :n], r["pool"]), f"cell {g}: pool"
+        n = counts[g, 3]
+        assert n == len(r["u15"]) and np.array_equal(u15[g, :n], r["u15"]), f"cell {g}: stage-1.5 union"
+        n = counts[g, 4]
+        assert n == len(r["cand"]) and np.array_equal(cand[g, :n], r["cand"]), f"cell {g}: stage-1.6 union"
+        assert np.array_equal(fpos[g], r["final_pos"]), f"cell {g}: stage-II ranks"
+        assert counts[g, 5] == 0, f"cell {g}: status"
+
+
+def test_funnel_parity_and_output(case, cuda):
+    cfg = SeoulKV4Config(debug=True)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
+        for qseed in (101, 102, 103):
+            q = case.query(qseed)
+            y = attn.run(q).to_torch()
+            res, ref_out = case.oracle(q)
+            eng = attn._engine
+            _compare(eng, res, case.index.cells()[0]["centroids"].shape[0], 13056)
+            ids = attn.debug_snapshot()["selected_ids"].numpy()
+            want = np.stack([r["final_ids"] for r in res])
+            assert np.array_equal(ids, want), "selected token ids"
+            got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
+            ref = O.bf16_to_f32(ref_out).astype(np.float64)
+            err = np.abs(got - ref)
+            assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
+
+
+def test_device_query_and_replay(case, cuda):
+    q = case.query(201)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
+        a = attn.run(q).to_torch()
+        b = attn.run(q.to(cuda)).to_torch()
+        assert torch.equal(a, b)
+        ids1 = attn.debug_snapshot()["selected_ids"]
+        attn.run(case.query(202))
+        attn.run(q)
+        assert torch.equal(attn.debug_snapshot()["selected_ids"], ids1)
