@@ -29,7 +29,7 @@
  * (TT FPU accumulation order, TopK-XL tie order):
  *   - every scoring dot product is the EXACT sum of (operand x small integer)
  *     products, rounded once to FP32 (RNE).  Operand rows are first flushed:
- *     an element whose magnitude is below 2^(E-24), E = floor(log2 max|x|)
+ *     an element whose magnitude is below 2^(E-22), E = floor(log2 max|x|)
  *     of that row, becomes zero.  The exact sum is formed here with 64-bit
  *     integers on a 2^(E-31) grid.
  *   - FP32 post-operations are single IEEE operations, each rounded to
@@ -121,7 +121,7 @@ static void exact_row(const float *x, int64_t *X, int32_t *shift) {
     for (int d = 0; d < D; ++d)
         if (x[d] != 0.0f) { int e = ilogbf(x[d]); if (e > E) E = e; }
     if (E == INT32_MIN) { memset(X, 0, sizeof(int64_t) * D); *shift = 0; return; }
-    const double floor_mag = ldexp(1.0, E - 24);
+    const double floor_mag = ldexp(1.0, E - 22);
     for (int d = 0; d < D; ++d) {
         double v = (double)x[d];
         X[d] = fabs(v) < floor_mag ? 0 : (int64_t)ldexp(v, 31 - E);

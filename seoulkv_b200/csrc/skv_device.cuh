@@ -1,12 +1,17 @@
 // skv_device.cuh -- shared device helpers and the engine's device layout.
 //
 // Arithmetic conventions (identical in the CPU oracle):
-//   * scoring dot products are exact sums of (operand x small integer) in
-//     FP64 on operand rows flushed below 2^(E-24) (E = top exponent of the
-//     row), rounded once to FP32;
+//   * a scoring dot product is the EXACT sum of (query operand x small
+//     integer code weight), rounded once to FP32.  Each operand row is first
+//     flushed below 2^(E-22) (E = top exponent of the row), which puts every
+//     kept element on the integer grid 2^(E-29) with |X| < 2^30.  X is split
+//     into four signed base-256 digits and the code weights are int8, so the
+//     sum runs on int8 tensor cores (mma.sync m16n8k32, int32 accumulate)
+//     without any rounding, and the digit sums recombine exactly in int64;
 //   * FP32 post-operations use __f*_rn intrinsics so nothing is contracted;
 //   * FP32 -> BF16 rounds to nearest even.
 #pragma once
+#include <climits>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -21,14 +26,20 @@ constexpr int M15_MIN = 2048;   // smallest legal Stage-1.5 pool
 constexpr int U15_MAX = G * UNION15;
 constexpr int CAND_MAX = G * M16;
 constexpr int SEL_MAX = G * 512;   // Fine union bound (nprobe <= 512)
-constexpr int ATTN_SPLIT = 16;     // attention partitions per KV head
+constexpr int ATTN_SPLIT = 32;     // attention partitions per KV head
 constexpr int REC = 512;           // FP8 [K | V] record bytes
 constexpr int NCOUNT = 8;          // per-cell counters
+constexpr int CHUNK = 1024;        // centroid / pool positions per chunk CTA
+constexpr int SCHUNK = 256;        // survivors per pool-kernel CTA
+constexpr int FRAG_ROW = 8 * 2 * 32 * 2;  // u32 per operand row set (ks, n-tile, lane, reg)
+constexpr int PART = 260;          // floats per attention partial (m, l, pad, pad, o[256])
 
 // Per-cell counters (Work::counts[cell][*]).
 enum Count { C_TAGS = 0, C_SEL = 1, C_POOL = 2, C_U15 = 3, C_CAND = 4, C_STATUS = 5, C_POSTINGS = 6 };
 // Threshold slots (Work::thr[cell][stage][head]).
 enum Stage { T_COARSE = 0, T_FINE = 1, T_S15 = 2, T_S16 = 3 };
+// Operand rows (Work::frag / Work::shift).
+enum Row { R_Q = 0, R_Q15 = 1, R_QS = 2 };
 
 constexpr uint32_t ST_POOL_OVER = 1u, ST_POOL_UNDER = 2u, ST_FINE_SHORT = 4u;
 
@@ -51,29 +62,46 @@ struct CellDev {
 };
 
 // Workspace: one base pointer per buffer, indexed by cell inside kernels.
+// Buffers marked (step) must be zero when a step starts; the last kernel of
+// a step clears them again for the next one.
 struct Work {
   int n_cells, n_slots, T, sink, local, nc, cap;
+  int chunks_nc;            // ceil(nc / CHUNK)
+  int chunks_surv;          // ceil(nc / SCHUNK)
+  int chunks_pool;          // ceil(cap / CHUNK)
   const CellDev *cells;
   const uint16_t *q;        // [n_slots][16][256] BF16
-  double *ops;              // [cell][3][256][4]  A=q, B=16*q15, Dq=qs (d-major)
-  float *qscal;             // [cell][8]  qn[4], 3*sum(q)[4]
+  uint32_t *frag;           // [cell][3][FRAG_ROW] int8 digit fragments of the operand rows
+  int32_t *shift;           // [cell][3][4] value = digits-sum * 2^shift
+  float *qscal;             // [cell][8]  lambda*|q| [4], 3*sum(q) [4]
   uint16_t *lo, *hi;        // [cell][4][nc] ordered BF16 coarse bounds
-  uint32_t *chist;          // [cell][4][256]
   uint32_t *thr;            // [cell][4 stages][4 heads]
+  uint8_t *smask;           // [cell][nc] coarse head masks
+  int32_t *chunk_cnt;       // [cell][chunks_nc] survivors per centroid chunk
   uint32_t *tags;           // [cell][nc]
   uint32_t *fkeys;          // [cell][4][nc]
+  uint32_t *selbits;        // [cell][nc/32] selected clusters (step)
+  uint16_t *kept;           // [cell][nc] kept postings per survivor
+  unsigned long long *keptmask;  // [cell][nc] kept postings of lists <= 64 long
+  int32_t *chunk_kept;      // [cell][chunks_surv]
+  int32_t *chunk_sel;       // [cell][chunks_surv]
+  int32_t *chunk_post;      // [cell][chunks_surv]
   int32_t *sel;             // [cell][SEL_MAX]
-  uint32_t *selbits;        // [cell][nc/32]
   int32_t *pool;            // [cell][cap]
   uint32_t *k15;            // [cell][4][cap]
+  uint32_t *u15bits;        // [cell][cap/32] (step)
   int32_t *u15pos;          // [cell][U15_MAX]
   int32_t *u15tok;          // [cell][U15_MAX]
   uint32_t *k16;            // [cell][4][U15_MAX]
+  uint32_t *candbits;       // [cell][U15_MAX/32] (step)
   int32_t *cand;            // [cell][CAND_MAX]
+  uint32_t *k2;             // [cell][4][CAND_MAX] Stage-II keys
   int32_t *final_pos;       // [cell][4][TOPK]
   int32_t *final_ids;       // [cell][4][TOPK]
   int32_t *counts;          // [cell][NCOUNT]
-  float *attn_part;         // [cell][4][ATTN_SPLIT][260]
+  float *attn_part;         // [cell][4][ATTN_SPLIT][PART]
+  uint32_t *arrive;         // [cell] attention partitions finished (step)
+  uint32_t *hist;           // [cell][4 stages][4 heads][4096] first-pass histograms (step)
   uint16_t *out;            // [n_slots][16][256] BF16
 };
 
@@ -97,15 +125,88 @@ __device__ __forceinline__ uint32_t ord_fused(uint32_t score, uint32_t pos) {
   return (x & 0x80000000u) ? ~x : (x | 0x80000000u);
 }
 
-// Exact conversion of a small signed integer to double without I2F.
-__device__ __forceinline__ double small2d(int v) {
-  return __hiloint2double(0x43300000, v ^ (int)0x80000000) - 4503601774854144.0;
+// First-pass histogram (top 12 key bits) of one selection.
+__device__ __forceinline__ uint32_t *hist_of(const Work &w, int cell, int stage, int head) {
+  return w.hist + (((size_t)cell * 4 + stage) * G + head) * 4096;
+}
+
+// 2^e as a double, e in the normal range.
+__device__ __forceinline__ double pow2d(int e) { return __hiloint2double((e + 1023) << 20, 0); }
+
+// Exact digit sum -> FP32 score input (one rounding).
+__device__ __forceinline__ float exact_to_float(long long dsum, double scale) {
+  return __double2float_rn(__ll2double_rn(dsum) * scale);
+}
+
+// ------------------------------------------------------ tensor-core dots
+
+// B operand fragments of one operand row set: 8 k-steps x 2 n-tiles x 2 regs.
+// Column n of n-tile nt is (head 2*nt + n/4, digit n%4).  Virtual k of
+// k-step ks maps to dimension 32*ks + (k >= 16 ? 16 : 0) + 4*(k%4... see
+// k_qprep), matching the byte order the A-side unpacking produces.
+struct BFrag {
+  uint32_t b[8][2][2];
+};
+
+__device__ __forceinline__ void load_bfrag(const Work &w, int cell, int row, int lane, BFrag &f) {
+  const uint2 *p = reinterpret_cast<const uint2 *>(w.frag + ((size_t)cell * 3 + row) * FRAG_ROW);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint2 v = p[(ks * 2 + nt) * 32 + lane];
+      f.b[ks][nt][0] = v.x;
+      f.b[ks][nt][1] = v.y;
+    }
+}
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Recombine the four digit accumulators.  Thread t of a quad ends with the
+// exact sum for row (t odd ? g + 8 : g) and heads t/2 (d[0]) and 2 + t/2 (d[1]).
+__device__ __forceinline__ void combine_digits(const int (&acc)[2][4], int t, long long (&d)[2]) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    long long pg = (long long)acc[nt][0] + 256LL * acc[nt][1];
+    long long p8 = (long long)acc[nt][2] + 256LL * acc[nt][3];
+    if (t & 1) { pg *= 65536LL; p8 *= 65536LL; }
+    pg += __shfl_xor_sync(0xffffffffu, pg, 1);
+    p8 += __shfl_xor_sync(0xffffffffu, p8, 1);
+    d[nt] = (t & 1) ? p8 : pg;
+  }
+}
+
+// Weight unpacking: byte i of the result is the weight of dimension
+// 16*word + 4*i + t for a 2-bit-per-dimension plane word.
+__device__ __forceinline__ uint32_t w2(uint32_t word, int t) { return (word >> (2 * t)) & 0x03030303u; }
+// 2p - 3 for p in 0..3 (Stage-1.5 prefix codes).
+__device__ __forceinline__ uint32_t w_odd2(uint32_t p) { return __vsub4(p << 1, 0x03030303u); }
+// 2(4u + l) - 15 for the 4-bit code (u, l) (Fine centroid codes, Stage-1.6 keys).
+__device__ __forceinline__ uint32_t w_odd4(uint32_t u, uint32_t l) {
+  return __vsub4((u << 3) | (l << 1), 0x0f0f0f0fu);
+}
+// 2n - 15 for the residual4 nibbles of dimensions 16*word + 4*i + t, from the
+// two residual4 words covering those 16 dimensions.
+__device__ __forceinline__ uint32_t w_nib(uint32_t lo_word, uint32_t hi_word, int t) {
+  const uint32_t x = (lo_word >> (4 * t)) & 0x000f000fu, y = (hi_word >> (4 * t)) & 0x000f000fu;
+  return __vsub4(__byte_perm(x, y, 0x6420) << 1, 0x0f0f0f0fu);
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 (&r)[4], int i) {
+  const uint4 v = r[i >> 2];
+  return (i & 3) == 0 ? v.x : (i & 3) == 1 ? v.y : (i & 3) == 2 ? v.z : v.w;
 }
 
 // ------------------------------------------------------------ block scans
 
 // Exclusive prefix sum over the block (blockDim.x a multiple of 32, <= 1024).
-// Returns this thread's exclusive prefix; *total receives the block sum.
 __device__ __forceinline__ int block_exclusive_scan(int v, int *total) {
   __shared__ int s_warp[32];
   __shared__ int s_total;
@@ -120,14 +221,14 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *total) {
   if (lane == 31) s_warp[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = lane < nwarps ? s_warp[lane] : 0;
-    int t = w;
+    int wv = lane < nwarps ? s_warp[lane] : 0;
+    int t = wv;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       int y = __shfl_up_sync(0xffffffffu, t, o);
       if (lane >= o) t += y;
     }
-    if (lane < nwarps) s_warp[lane] = t - w;
+    if (lane < nwarps) s_warp[lane] = t - wv;
     if (lane == 31) s_total = t;
   }
   __syncthreads();
@@ -137,13 +238,21 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *total) {
   return r;
 }
 
+// Sum of src[0..n) computed by the whole block (result in every thread).
+__device__ __forceinline__ int block_sum_prefix(const int32_t *src, int n) {
+  int s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += src[i];
+  int total;
+  block_exclusive_scan(s, &total);
+  return total;
+}
+
 // Given a 256-bin histogram in shared memory, find the bin holding the k-th
 // largest element (1-based k) scanning from bin 255 down.  Executed by warp 0;
 // results are written to *bin and *above (count strictly above that bin).
 __device__ __forceinline__ void find_bin_desc(const uint32_t *hist, uint32_t k, int *bin,
                                               uint32_t *above) {
   const int lane = threadIdx.x & 31;
-  // lane l owns bins [255-8l-7, 255-8l], i.e. the l-th block from the top
   uint32_t c[8];
   uint32_t s = 0;
 #pragma unroll

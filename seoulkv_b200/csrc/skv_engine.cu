@@ -133,8 +133,8 @@ int skv_create(const SkvDesc *d, void **handle) {
     return fail(SKV_E_INVALID, "sink/local must be disjoint and inside the context");
   if (d->nc < 32 || d->nc % 32 || d->nc > 65536)
     return fail(SKV_E_INVALID, "nc must be a multiple of 32 in [32, 65536]");
-  if (d->stage15_capacity < M15_MIN || d->stage15_capacity > 65536)
-    return fail(SKV_E_INVALID, "stage15_capacity must be in [2048, 65536]");
+  if (d->stage15_capacity < M15_MIN || d->stage15_capacity > 65536 || d->stage15_capacity % 32)
+    return fail(SKV_E_INVALID, "stage15_capacity must be a multiple of 32 in [2048, 65536]");
   auto *e = new Engine();
   e->desc = *d;
   e->n_cells = d->n_slots * G;
@@ -178,26 +178,41 @@ int skv_create(const SkvDesc *d, void **handle) {
   uint16_t *q = nullptr;
   TRY(dalloc(e, &q, (size_t)d->n_slots * 16 * D));
   w.q = q;
-  TRY(dalloc(e, &w.ops, C * 3 * D * G));
+  w.chunks_nc = (d->nc + CHUNK - 1) / CHUNK;
+  w.chunks_surv = (d->nc + SCHUNK - 1) / SCHUNK;
+  w.chunks_pool = (d->stage15_capacity + CHUNK - 1) / CHUNK;
+  TRY(dalloc(e, &w.frag, C * 3 * FRAG_ROW));
+  TRY(dalloc(e, &w.shift, C * 3 * G));
   TRY(dalloc(e, &w.qscal, C * 8));
   TRY(dalloc(e, &w.lo, C * G * nc));
   TRY(dalloc(e, &w.hi, C * G * nc));
-  TRY(dalloc(e, &w.chist, C * G * 256));
   TRY(dalloc(e, &w.thr, C * 16));
+  TRY(dalloc(e, &w.smask, C * nc));
+  TRY(dalloc(e, &w.chunk_cnt, C * w.chunks_nc));
   TRY(dalloc(e, &w.tags, C * nc));
   TRY(dalloc(e, &w.fkeys, C * G * nc));
-  TRY(dalloc(e, &w.sel, C * SEL_MAX));
   TRY(dalloc(e, &w.selbits, C * (nc / 32)));
+  TRY(dalloc(e, &w.kept, C * nc));
+  TRY(dalloc(e, &w.keptmask, C * nc));
+  TRY(dalloc(e, &w.chunk_kept, C * w.chunks_surv));
+  TRY(dalloc(e, &w.chunk_sel, C * w.chunks_surv));
+  TRY(dalloc(e, &w.chunk_post, C * w.chunks_surv));
+  TRY(dalloc(e, &w.sel, C * SEL_MAX));
   TRY(dalloc(e, &w.pool, C * cap));
   TRY(dalloc(e, &w.k15, C * G * cap));
+  TRY(dalloc(e, &w.u15bits, C * (cap / 32)));
   TRY(dalloc(e, &w.u15pos, C * U15_MAX));
   TRY(dalloc(e, &w.u15tok, C * U15_MAX));
   TRY(dalloc(e, &w.k16, C * G * U15_MAX));
+  TRY(dalloc(e, &w.candbits, C * (U15_MAX / 32)));
   TRY(dalloc(e, &w.cand, C * CAND_MAX));
+  TRY(dalloc(e, &w.k2, C * G * CAND_MAX));
   TRY(dalloc(e, &w.final_pos, C * G * TOPK));
   TRY(dalloc(e, &w.final_ids, C * G * TOPK));
   TRY(dalloc(e, &w.counts, C * NCOUNT));
-  TRY(dalloc(e, &w.attn_part, C * G * ATTN_SPLIT * 260));
+  TRY(dalloc(e, &w.attn_part, C * G * ATTN_SPLIT * PART));
+  TRY(dalloc(e, &w.arrive, C));
+  TRY(dalloc(e, &w.hist, C * 4 * G * 4096));
   TRY(dalloc(e, &w.out, (size_t)d->n_slots * 16 * D));
 #undef TRY
   *handle = e;
