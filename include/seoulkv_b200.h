@@ -130,6 +130,11 @@ int skv_debug_ids(void *handle, int32_t *out);
 #define SKV_STAGE_CAND 6        /* int32 [4][1024] Stage-1.5 union positions   */
 #define SKV_STAGE_FINAL_POS 7   /* int32 [4][4][100] Stage-1.5 union positions */
 #define SKV_STAGE_LOHI 8        /* uint16 [4][2][4][nc] coarse lo, hi (BF16)   */
+#define SKV_STAGE_PREFIX2 9     /* uint8 [4][T][64]  key codes >> 6            */
+#define SKV_STAGE_RESIDUAL2 10  /* uint8 [4][T][64]  (key codes >> 4) & 3      */
+#define SKV_STAGE_RESIDUAL4 11  /* uint8 [4][T][128] key codes & 15            */
+#define SKV_STAGE_KV8 12        /* uint8 [4][T][512] FP8-e4m3 [K | V] records  */
+#define SKV_STAGE_KEY_SCALE 13  /* float [4][256] per-dimension max |k|        */
 int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
                    size_t *written);
 

@@ -19,7 +19,8 @@ SKV_STATUS_POOL_UNDER = 2
 SKV_STATUS_FINE_SHORT = 4
 SKV_E_CAPACITY = -3
 
-STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8)
+STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8,
+             prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13)
 
 EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",

@@ -524,6 +524,30 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
       if (written) *written = n;
       return SKV_OK;
     }
+    case SKV_STAGE_PREFIX2:
+    case SKV_STAGE_RESIDUAL2:
+    case SKV_STAGE_RESIDUAL4:
+    case SKV_STAGE_KV8:
+    case SKV_STAGE_KEY_SCALE: {
+      const size_t T = e->desc.context;
+      const size_t row = which == SKV_STAGE_RESIDUAL4 ? 128 : which == SKV_STAGE_KV8 ? REC
+                       : which == SKV_STAGE_KEY_SCALE ? 0 : 64;
+      const size_t per = which == SKV_STAGE_KEY_SCALE ? D * sizeof(float) : T * row;
+      size_t done = 0;
+      for (int g = 0; g < G && done < bytes; ++g) {
+        const CellBufs &b = e->bufs[c0 + g];
+        const void *p = which == SKV_STAGE_PREFIX2 ? (const void *)b.prefix2
+                      : which == SKV_STAGE_RESIDUAL2 ? (const void *)b.residual2
+                      : which == SKV_STAGE_RESIDUAL4 ? (const void *)b.residual4
+                      : which == SKV_STAGE_KV8 ? (const void *)b.kv8 : (const void *)b.key_scale;
+        if (!p) return fail(SKV_E_STATE, "K/V not uploaded for this slot");
+        const size_t m = std::min(per, bytes - done);
+        CK(cudaMemcpy(static_cast<char *>(dst) + done, p, m, cudaMemcpyDeviceToHost));
+        done += m;
+      }
+      if (written) *written = done;
+      return SKV_OK;
+    }
     default: return fail(SKV_E_INVALID, "unknown stage selector");
   }
   n = std::min(n, bytes);

@@ -55,3 +55,51 @@ class Case:
             keys = O.attention_keys(self.context, self.sink, self.local, res[g]["final_ids"][h])
             out[j] = O.attention(qb[j], k8[g], v8[g], keys)
         return res, out
+
+
+# ------------------------------------------------------------ golden data
+
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "golden_t8192.npz"
+
+
+class Golden:
+    """The reference-built fixture (tests/golden/make_golden.py) + regenerated K/V."""
+
+    def __init__(self):
+        import json
+
+        z = np.load(GOLDEN, allow_pickle=False)
+        self.z = {k: z[k] for k in z.files}
+        self.meta = json.loads(str(self.z["metadata"]))
+        self.context = self.meta["context"]
+        self.k, self.v, self.mixes = synthetic.make_kv(self.context, seed=self.meta["kv_seed"])
+        self.queries = [synthetic.make_query(self.context, self.mixes, seed=s) for s in self.meta["q_seeds"]]
+
+    def views(self):
+        """Engine/oracle cell views of the reference-built index."""
+        from seoulkv_b200.index import posting_mates
+
+        out = []
+        for g, info in enumerate(self.meta["cells"]):
+            z = self.z
+            upper, lower = z[f"{g}_upper"], z[f"{g}_lower"]
+            nc = upper.shape[0]
+            scale = z[f"{g}_scale"].astype(np.float32).reshape(-1, 32)
+            gfs = z[f"{g}_group_fine_scale"].view(np.float16).astype(np.float32)
+            resid = torch.from_numpy(z[f"{g}_coarse_residual_norm"].view(np.float16).copy()).bfloat16()
+            offsets = z[f"{g}_offsets"].astype(np.int32)
+            values = z[f"{g}_values"].astype(np.int32)
+            out.append(dict(
+                nc=nc, nprobe=int(info["p"]), lam=float(info["lam"]), upper=upper, lower=lower,
+                coarse_scale4=(scale[:, 0] / np.float32(4)).astype(np.float32), fine_scale=gfs,
+                resid_bf16=resid.view(torch.int16).numpy().view(np.uint16), offsets=offsets, values=values,
+                mates=posting_mates(offsets, values)))
+        return out
+
+    def oracle_cells(self):
+        scales, p2, r2, r4 = O.key_codec(bits(self.k))
+        return [O.CellInputs(nc=v["nc"], nprobe=v["nprobe"], lam=v["lam"], upper=v["upper"], lower=v["lower"],
+                             coarse_scale4=v["coarse_scale4"], fine_scale=v["fine_scale"],
+                             resid_bf16=v["resid_bf16"], offsets=v["offsets"], values=v["values"],
+                             context=self.context, prefix2=p2[g], residual2=r2[g], residual4=r4[g],
+                             key_scale=scales[g]) for g, v in enumerate(self.views())]

@@ -1,0 +1,52 @@
+"""The C-ABI library loads and exports every function include/seoulkv_b200.h declares."""
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from seoulkv_b200 import _native
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "seoulkv_b200.h"
+
+
+def declared():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(skv_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_core_entry_points():
+    names = declared()
+    for must in ("skv_create", "skv_destroy", "skv_upload_index", "skv_upload_kv", "skv_bind_query",
+                 "skv_run", "skv_sync", "skv_status", "skv_output", "skv_debug_ids", "skv_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert lib.skv_version().startswith(b"seoulkv_b200")
+    assert lib.skv_kernels_per_step() > 0
+    assert lib.skv_kernel_name(0) != b""
+
+
+def test_create_rejects_bad_descriptors():
+    lib = _native.load()
+    import ctypes
+
+    h = ctypes.c_void_p()
+    for kw in (dict(n_slots=0), dict(nc=33), dict(context=0), dict(sink=9000), dict(stage15_capacity=100)):
+        d = dict(n_slots=1, context=8192, sink=128, local=256, nc=1952, stage15_capacity=13056, device=0)
+        d.update(kw)
+        rc = lib.skv_create(ctypes.byref(_native.SkvDesc(**d)), ctypes.byref(h))
+        assert rc == -1, kw
+        assert lib.skv_last_error()
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path")
+def test_no_gpu_fails_loudly():
+    with pytest.raises(_native.NativeError) as exc:
+        _native.Engine(n_slots=1, context=8192, sink=128, local=256, nc=1952, capacity=13056, device=0)
+    assert exc.value.code == -2
