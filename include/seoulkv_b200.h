@@ -156,6 +156,28 @@ const char *skv_kernel_name(int32_t i);
 /* Kernels one skv_run enqueues. */
 int32_t skv_kernels_per_step(void);
 
+/* Sparse attention that allocates nothing -- no counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory while running (for example
+ * a server that commits its whole HBM budget at start-up and treats a later
+ * cudaMalloc as a failure, since cudaMalloc also synchronises the device).
+ * Computes what the last stage of skv_run computes, from caller buffers:
+ *   q    device BF16 [n_slots][16][256]
+ *   kv8  host array of n_slots*4 device pointers, each FP8-e4m3 records
+ *        [context][512] = K (256 B) | V (256 B) of one KV head
+ *   ids  device int32 [n_slots][4][4][100] selected token ids (KV head,
+ *        query head, rank); ids outside [0, context) are skipped
+ *   out  device BF16 [n_slots][16][256]
+ * Scratch is a fixed file-scope device array sized for SKV_NOALLOC_MAX_SLOTS
+ * slots (about 1 MiB, held by every GPU that loads the library until the
+ * process exits); larger n_slots is rejected with SKV_E_INVALID.  The first
+ * call on a device looks up the scratch address (make that first call before
+ * any stream capture).  All calls share the scratch: calls that overlap on the
+ * GPU (e.g. on two streams) race and must be serialised by the caller. */
+#define SKV_NOALLOC_MAX_SLOTS 2
+int skv_attention_noalloc(int32_t n_slots, const uint16_t *q, const uint8_t *const *kv8, const int32_t *ids,
+                          int32_t context, int32_t sink, int32_t local, uint16_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -118,6 +118,11 @@ int read_counts(Engine *e, std::vector<int32_t> &c) {
 
 }  // namespace
 
+namespace skv {
+// Lets other translation units of the library report through skv_last_error.
+void set_last_error(const std::string &msg) { g_error = msg; }
+}  // namespace skv
+
 extern "C" {
 
 const char *skv_last_error(void) { return g_error.c_str(); }
