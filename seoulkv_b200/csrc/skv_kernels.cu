@@ -1024,26 +1024,36 @@ __global__ void __launch_bounds__(256) k_attn(Work w) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  __shared__ __align__(16) float s_part[ATTN_SPLIT][PART];
-  for (int h = 0; h < G; ++h) {
-    const float4 *ph = reinterpret_cast<const float4 *>(part + (size_t)h * ATTN_SPLIT * PART);
-    float4 *dst = reinterpret_cast<float4 *>(&s_part[0][0]);
-    for (int i = tid; i < ATTN_SPLIT * PART / 4; i += 256) dst[i] = __ldcg(ph + i);
-    __syncthreads();
-    float M = -INFINITY;
-#pragma unroll
-    for (int sp = 0; sp < ATTN_SPLIT; ++sp) M = fmaxf(M, s_part[sp][0]);
-    float L = 0.0f, O = 0.0f;
+  {
+    // thread (head, quarter): output dims 4*q .. 4*q+3 of one head; all
+    // partials of that head are read at once (independent loads)
+    const int h = tid >> 6, q4 = tid & 63;
+    const float *ph = part + (size_t)h * ATTN_SPLIT * PART;
+    float ms[ATTN_SPLIT], ls[ATTN_SPLIT];
+    float4 os[ATTN_SPLIT];
 #pragma unroll
     for (int sp = 0; sp < ATTN_SPLIT; ++sp) {
-      const float ms = s_part[sp][0];
-      if (ms == -INFINITY) continue;
-      const float e = exp2f(ms - M);
-      L += s_part[sp][1] * e;
-      O += s_part[sp][4 + tid] * e;
+      ms[sp] = __ldcg(ph + sp * PART);
+      ls[sp] = __ldcg(ph + sp * PART + 1);
+      os[sp] = __ldcg(reinterpret_cast<const float4 *>(ph + sp * PART + 4) + q4);
     }
-    w.out[((size_t)slot * 16 + g * 4 + h) * D + tid] = bf16_rne(O / L);
-    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < ATTN_SPLIT; ++sp) M = fmaxf(M, ms[sp]);
+    float L = 0.0f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int sp = 0; sp < ATTN_SPLIT; ++sp) {
+      if (ms[sp] == -INFINITY) continue;
+      const float e = exp2f(ms[sp] - M);
+      L += ls[sp] * e;
+      O.x += os[sp].x * e; O.y += os[sp].y * e; O.z += os[sp].z * e; O.w += os[sp].w * e;
+    }
+    uint16_t *dst = w.out + ((size_t)slot * 16 + g * 4 + h) * D + 4 * q4;
+    dst[0] = bf16_rne(O.x / L);
+    dst[1] = bf16_rne(O.y / L);
+    dst[2] = bf16_rne(O.z / L);
+    dst[3] = bf16_rne(O.w / L);
   }
   if (tid == 0) w.arrive[cell] = 0;
   clear_step_state(w, cell);
