@@ -271,21 +271,40 @@ def main():
             prof.setdefault(name, []).append(ms)
     prof = {n: float(np.mean(v)) * 1e3 for n, v in prof.items()}  # µs
     traffic = eng.traffic()
-    stage_bytes = {"k_coarse": traffic["coarse"], "k_fine": traffic["fine"], "k_s16": traffic["stage16"],
-                   "k_s2": traffic["stage2"], "k_attn": traffic["attention"]}
-    top = max(prof, key=prof.get)
-    dom = top if top in stage_bytes else max(stage_bytes, key=lambda n: prof.get(n, 0))
+    if "k_funnel" in prof:
+        # fused path: one kernel carries the whole step
+        dom, dom_bytes = "k_funnel", traffic["total"]
+    else:
+        stage_bytes = {"k_coarse": traffic["coarse"], "k_fine": traffic["fine"], "k_pool_s15": traffic["stage15"],
+                       "k_s16": traffic["stage16"], "k_s2_score": traffic["stage2"], "k_attn": traffic["attention"]}
+        dom = max(stage_bytes, key=lambda n: prof.get(n, 0.0))
+        dom_bytes = stage_bytes[dom]
     peak, peak_kind = peaks()
-    achieved = stage_bytes[dom] / (prof[dom] * 1e-6) / 1e9
+    achieved = dom_bytes / (prof[dom] * 1e-6) / 1e9
     roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-            "traffic": None, "algorithmic_bytes": stage_bytes[dom], "kernel_us": prof[dom]}
-    ncu_note = ROOT / "profiles" / "coarse_128k_traffic.json"
+            "traffic": None, "algorithmic_bytes": dom_bytes, "kernel_us": prof[dom],
+            "timing": "CUDA events around one non-graph launch, L2 flushed"}
+    ncu_note = ROOT / "profiles" / "traffic_128k.json"
     if ncu_note.exists():
         try:
             roof["traffic"] = json.loads(ncu_note.read_text()).get(dom)
         except Exception:
             pass
+    # fused path: SM cycles per phase (CTA 0 of KV head 0), summed over repeats
+    phases = None
+    if eng.fused:
+        mhz = (clk or {}).get("sm_mhz") or 1965.0
+        acc = {}
+        for _ in range(3):
+            flush.zero_()
+            torch.cuda.synchronize(device)
+            for name, cyc in eng.profile_phases(stream.cuda_stream):
+                acc.setdefault(name, [0.0, 0])
+                acc[name][0] += cyc
+            for name in acc:
+                acc[name][1] += 1
+        phases = {n: round(v[0] / v[1] / mhz, 2) for n, v in acc.items()}
 
     # parity of one timed step against the CPU restatement + CPU baseline timing
     parity, cpu_line = None, None
@@ -343,7 +362,7 @@ def main():
                        "parallelism": f"{world} independent layers (one per GPU)" if world > 1 else "1 GPU"},
             "p50_us": float(np.percentile(per, 50)), "p99_us": float(np.percentile(per, 99)),
             "tokens_per_s": 1e6 / value,
-            "roofline": roof, "kernel_us": prof, "algorithmic_bytes_per_step": traffic,
+            "roofline": roof, "kernel_us": prof, "phase_us": phases, "algorithmic_bytes_per_step": traffic,
             "live_counts": {"survivors_max": st.survivors_max, "pool_min": st.pool_min, "pool_max": st.pool_max,
                             "union15_max": st.union15_max, "union16_max": st.union16_max},
             "parity": parity, "cpu_baseline": cpu_line, "e2e": e2e, "clocks": clk,

@@ -45,6 +45,11 @@ extern "C" {
 #define SKV_STATUS_POOL_OVER 1u   /* Stage-1.5 pool larger than capacity  */
 #define SKV_STATUS_POOL_UNDER 2u  /* Stage-1.5 pool smaller than 2048     */
 #define SKV_STATUS_FINE_SHORT 4u  /* a head had fewer than nprobe survivors */
+#define SKV_STATUS_TIMEOUT 8u     /* a bounded device wait gave up (results invalid) */
+
+/* SkvDesc.flags */
+#define SKV_FLAG_STAGED 1         /* run the 14-kernel staged path even where the
+                                     single-kernel cluster path applies      */
 
 typedef struct SkvDesc {
     int32_t n_slots;          /* independent caches decoded per run        */
@@ -54,7 +59,7 @@ typedef struct SkvDesc {
     int32_t nc;               /* centroids per KV head (multiple of 32)    */
     int32_t stage15_capacity; /* pool slots per KV head                    */
     int32_t device;           /* CUDA device ordinal                       */
-    int32_t flags;            /* reserved, 0                               */
+    int32_t flags;            /* SKV_FLAG_* (0: fused path where it applies) */
 } SkvDesc;
 
 /* One KV head's index in the engine layout (host memory). */
@@ -151,10 +156,20 @@ int skv_traffic(void *handle, SkvTraffic *out);
  * *n_kernels.  Synchronises.  For profiling; results equal skv_run's. */
 int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_kernels,
                      int32_t *n_kernels);
-/* Name of kernel i of one step (static string; "" when out of range). */
+/* Name of kernel i of the STAGED path (static string; "" when out of range). */
 const char *skv_kernel_name(int32_t i);
-/* Kernels one skv_run enqueues. */
+/* Kernels one step of the STAGED path enqueues. */
 int32_t skv_kernels_per_step(void);
+/* Name of kernel i of this engine's step: "k_funnel" (one kernel) on the
+ * fused path, the staged names otherwise. */
+const char *skv_step_kernel_name(void *handle, int32_t i);
+/* One fused step with SM-clock marks between its phases (CTA 0 of cell 0):
+ * segment i ends at mark tags[i] and took cycles[i] SM cycles; n =
+ * min(max_marks, marks).  Synchronises.  SKV_E_STATE on the staged path. */
+int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles, int32_t max_marks,
+                       int32_t *n_marks);
+/* Name of a phase mark tag (static string). */
+const char *skv_phase_name(int32_t tag);
 
 /* Sparse attention that allocates nothing -- no counterpart in the reference.
  *

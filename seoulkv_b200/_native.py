@@ -26,8 +26,13 @@ EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
     "skv_upload_kv", "skv_bind_query", "skv_run", "skv_sync", "skv_status", "skv_output",
     "skv_debug_ids", "skv_read_stage", "skv_traffic", "skv_profile_step", "skv_kernel_name",
-    "skv_kernels_per_step",
+    "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name",
 )
+
+SKV_FLAG_STAGED = 1
+# Engines created without an explicit ``staged=`` use the staged (14-kernel)
+# path when this is true; tests flip it to run both paths through the API.
+FORCE_STAGED = False
 
 
 class SkvDesc(ctypes.Structure):
@@ -103,6 +108,12 @@ def load() -> ctypes.CDLL:
         lib.skv_kernel_name.restype = ctypes.c_char_p
         lib.skv_kernel_name.argtypes = [ctypes.c_int32]
         lib.skv_kernels_per_step.restype = ctypes.c_int32
+        lib.skv_step_kernel_name.restype = ctypes.c_char_p
+        lib.skv_step_kernel_name.argtypes = [ctypes.c_void_p, ctypes.c_int32]
+        lib.skv_profile_phases.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
+        lib.skv_phase_name.restype = ctypes.c_char_p
+        lib.skv_phase_name.argtypes = [ctypes.c_int32]
         _lib = lib
         return lib
 
@@ -128,12 +139,13 @@ class Engine:
     """One engine instance: ``n_slots`` caches x 4 KV heads on one CUDA device."""
 
     def __init__(self, *, n_slots: int, context: int, sink: int, local: int, nc: int,
-                 capacity: int, device: int):
+                 capacity: int, device: int, staged: bool | None = None):
         self.lib = load()
         self.n_slots, self.context, self.nc, self.capacity = n_slots, context, nc, capacity
         self.sink, self.local, self.device = sink, local, device
+        staged = FORCE_STAGED if staged is None else staged
         desc = SkvDesc(n_slots=n_slots, context=context, sink=sink, local=local, nc=nc,
-                       stage15_capacity=capacity, device=device, flags=0)
+                       stage15_capacity=capacity, device=device, flags=SKV_FLAG_STAGED if staged else 0)
         h = ctypes.c_void_p()
         check(self.lib.skv_create(ctypes.byref(desc), ctypes.byref(h)), "skv_create")
         self.handle = h
@@ -211,10 +223,27 @@ class Engine:
         n = ctypes.c_int32()
         check(self.lib.skv_profile_step(self.handle, ctypes.c_void_p(stream or None), _ptr(ms), 64,
                                         ctypes.byref(n)), "skv_profile_step")
-        return [(self.lib.skv_kernel_name(i).decode(), float(ms[i])) for i in range(n.value)]
+        return [(self.lib.skv_step_kernel_name(self.handle, i).decode(), float(ms[i])) for i in range(n.value)]
 
     def kernels_per_step(self) -> int:
-        return int(self.lib.skv_kernels_per_step())
+        """Kernels one step of this engine launches (1 on the fused path)."""
+        n = 0
+        while self.lib.skv_step_kernel_name(self.handle, n):
+            n += 1
+        return n
+
+    @property
+    def fused(self) -> bool:
+        return self.lib.skv_step_kernel_name(self.handle, 0) == b"k_funnel"
+
+    def profile_phases(self, stream: int = 0) -> list[tuple[str, float]]:
+        """One fused step: (segment name, SM cycles) in order (CTA 0 of cell 0)."""
+        tags = np.zeros(128, dtype=np.int32)
+        cyc = np.zeros(128, dtype=np.float64)
+        n = ctypes.c_int32()
+        check(self.lib.skv_profile_phases(self.handle, ctypes.c_void_p(stream or None), _ptr(tags), _ptr(cyc),
+                                          128, ctypes.byref(n)), "skv_profile_phases")
+        return [(self.lib.skv_phase_name(int(tags[i])).decode(), float(cyc[i])) for i in range(n.value)]
 
     def traffic(self) -> dict:
         t = SkvTraffic()

@@ -34,6 +34,8 @@ constexpr int SCHUNK = 256;        // survivors per pool-kernel CTA
 constexpr int FRAG_ROW = 8 * 2 * 32 * 2;  // u32 per operand row set (ks, n-tile, lane, reg)
 constexpr int PART = 260;          // floats per attention partial (m, l, pad, pad, o[256])
 
+constexpr int FUSED_MARKS = 96;  // (tag, clock) profiling marks of the fused kernel
+
 // Per-cell counters (Work::counts[cell][*]).
 enum Count { C_TAGS = 0, C_SEL = 1, C_POOL = 2, C_U15 = 3, C_CAND = 4, C_STATUS = 5, C_POSTINGS = 6 };
 // Threshold slots (Work::thr[cell][stage][head]).
@@ -41,7 +43,7 @@ enum Stage { T_COARSE = 0, T_FINE = 1, T_S15 = 2, T_S16 = 3 };
 // Operand rows (Work::frag / Work::shift).
 enum Row { R_Q = 0, R_Q15 = 1, R_QS = 2 };
 
-constexpr uint32_t ST_POOL_OVER = 1u, ST_POOL_UNDER = 2u, ST_FINE_SHORT = 4u;
+constexpr uint32_t ST_POOL_OVER = 1u, ST_POOL_UNDER = 2u, ST_FINE_SHORT = 4u, ST_TIMEOUT = 8u;
 
 struct CellDev {
   const uint8_t *upper, *lower;      // [nc][64]
@@ -103,6 +105,7 @@ struct Work {
   uint32_t *arrive;         // [cell] attention partitions finished (step)
   uint32_t *hist;           // [cell][4 stages][4 heads][4096] first-pass histograms (step)
   uint16_t *out;            // [n_slots][16][256] BF16
+  long long *phase_ts;      // [FUSED_MARKS][2] (tag, SM clock) marks of cell 0, or null
 };
 
 __device__ __forceinline__ uint16_t bf16_rne(float f) {
@@ -141,9 +144,10 @@ __device__ __forceinline__ float exact_to_float(long long dsum, double scale) {
 // ------------------------------------------------------ tensor-core dots
 
 // B operand fragments of one operand row set: 8 k-steps x 2 n-tiles x 2 regs.
-// Column n of n-tile nt is (head 2*nt + n/4, digit n%4).  Virtual k of
-// k-step ks maps to dimension 32*ks + (k >= 16 ? 16 : 0) + 4*(k%4... see
-// k_qprep), matching the byte order the A-side unpacking produces.
+// Column n of n-tile nt is (head 2*nt + n/4, digit n%4).  Within k-step ks,
+// register reg, byte b of lane-in-quad tq holds dimension
+// 32*ks + 16*reg + 4*b + tq: the order in which w2()/w_nib() place the
+// weights of a plane word into the bytes of an A register.
 struct BFrag {
   uint32_t b[8][2][2];
 };
@@ -202,6 +206,34 @@ __device__ __forceinline__ uint32_t w_nib(uint32_t lo_word, uint32_t hi_word, in
 __device__ __forceinline__ uint32_t word_of(const uint4 (&r)[4], int i) {
   const uint4 v = r[i >> 2];
   return (i & 3) == 0 ? v.x : (i & 3) == 1 ? v.y : (i & 3) == 2 ? v.z : v.w;
+}
+
+// --------------------------------------------------- warp-aggregated atomics
+
+// hist[bin] += 1 for every lane whose bin != 0xffffffff.  The lanes that
+// share lane 0's bin are added with one atomic (selection keys crowd into a
+// few bins, where per-lane atomics on one address serialise); the others
+// add individually.  All 32 lanes of the warp must call it.
+__device__ __forceinline__ void hist_add_warp(uint32_t *hist, uint32_t bin) {
+  const uint32_t b0 = __shfl_sync(0xffffffffu, bin, 0);
+  const unsigned same = __ballot_sync(0xffffffffu, bin == b0);
+  if ((threadIdx.x & 31) == 0) {
+    if (b0 != 0xffffffffu) atomicAdd(&hist[b0], (uint32_t)__popc(same));
+  } else if (bin != b0 && bin != 0xffffffffu) {
+    atomicAdd(&hist[bin], 1u);
+  }
+}
+
+// One slot of *counter for every lane with `want` (one atomic per warp);
+// returns the lane's slot, or -1.  All 32 lanes of the warp must call it.
+__device__ __forceinline__ int warp_claim(int *counter, bool want) {
+  const unsigned m = __ballot_sync(0xffffffffu, want);
+  if (!m) return -1;
+  const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(counter, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  return want ? base + __popc(m & ((1u << lane) - 1u)) : -1;
 }
 
 // ------------------------------------------------------------ block scans

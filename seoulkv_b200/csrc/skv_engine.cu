@@ -13,6 +13,7 @@
 
 #include "../../include/seoulkv_b200.h"
 #include "skv_device.cuh"
+#include "skv_fused.cuh"
 #include "skv_kernels.cuh"
 
 using namespace skv;
@@ -58,7 +59,14 @@ struct Engine {
   bool q_pending = false, ran = false;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  bool fused = false;             // one cluster kernel per step (else the staged kernels)
+  long long *phase_ts = nullptr;  // fused phase timestamps (skv_profile_phases)
 };
+
+// Enqueue one decode step of the engine's path.
+cudaError_t launch_step(const Engine *e, const Work &w, cudaStream_t st) {
+  return e->fused ? launch_fused(w, st) : launch_funnel(w, st);
+}
 
 template <class T>
 int dalloc(Engine *e, T **p, size_t count) {
@@ -219,6 +227,10 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(dalloc(e, &w.arrive, C));
   TRY(dalloc(e, &w.hist, C * 4 * G * 4096));
   TRY(dalloc(e, &w.out, (size_t)d->n_slots * 16 * D));
+  TRY(dalloc(e, &e->phase_ts, 2 * FUSED_MARKS));
+  w.phase_ts = nullptr;
+  e->fused = !(d->flags & SKV_FLAG_STAGED) && fused_supported(w);
+  if (e->fused) TRY(prepare_fused_attributes() ? fail(SKV_E_CUDA, "fused kernel attributes") : 0);
 #undef TRY
   *handle = e;
   return SKV_OK;
@@ -395,7 +407,7 @@ int skv_run(void *handle, void *stream) {
   if (!e->exec) {
     CK(cudaStreamSynchronize(e->stream));
     CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t le = launch_funnel(e->work, e->stream);
+    cudaError_t le = launch_step(e, e->work, e->stream);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (le != cudaSuccess) {
@@ -592,10 +604,17 @@ int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_k
   if (rc) return rc;
   CK(cudaSetDevice(e->desc.device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: legacy default stream
-  const int nk = funnel_kernel_count();
+  const int nk = e->fused ? 1 : funnel_kernel_count();
   std::vector<cudaEvent_t> ev(nk + 1, nullptr);
   for (auto &x : ev) CK(cudaEventCreate(&x));
-  cudaError_t le = launch_funnel(e->work, st, ev.data());
+  cudaError_t le;
+  if (e->fused) {
+    cudaEventRecord(ev[0], st);
+    le = launch_fused(e->work, st);
+    cudaEventRecord(ev[1], st);
+  } else {
+    le = launch_funnel(e->work, st, ev.data());
+  }
   cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(ev[nk]) : le;
   const int n = std::min<int>(nk, max_kernels);
   for (int i = 0; i < n && se == cudaSuccess; ++i) se = cudaEventElapsedTime(&kernel_ms[i], ev[i], ev[i + 1]);
@@ -606,6 +625,44 @@ int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_k
   *n_kernels = n;
   return SKV_OK;
 }
+
+const char *skv_step_kernel_name(void *handle, int32_t i) {
+  Engine *e = as_engine(handle);
+  if (!e) return "";
+  if (e->fused) return i == 0 ? "k_funnel" : "";
+  return funnel_kernel_name(i);
+}
+
+int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles, int32_t max_marks,
+                       int32_t *n_marks) {
+  Engine *e = as_engine(handle);
+  if (!e || !tags || !cycles || !n_marks) return fail(SKV_E_INVALID, "null engine or output");
+  if (!e->fused) return fail(SKV_E_STATE, "phase timing needs the fused path");
+  int rc = ready(e);
+  if (rc) return rc;
+  CK(cudaSetDevice(e->desc.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<long long> ts(2 * FUSED_MARKS, -1);
+  CK(cudaMemcpyAsync(e->phase_ts, ts.data(), ts.size() * sizeof(long long), cudaMemcpyHostToDevice, st));
+  Work w = e->work;
+  w.phase_ts = e->phase_ts;
+  CK(launch_fused(w, st));
+  CK(cudaMemcpyAsync(ts.data(), e->phase_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  CK(cudaEventRecord(e->done, st));
+  e->ran = true;
+  int n = 0;
+  for (int i = 1; i < FUSED_MARKS && n < max_marks; ++i) {
+    if (ts[2 * i] < 0) break;
+    tags[n] = (int32_t)ts[2 * i];
+    cycles[n] = (double)(ts[2 * i + 1] - ts[2 * i - 1]);
+    ++n;
+  }
+  *n_marks = n;
+  return SKV_OK;
+}
+
+const char *skv_phase_name(int32_t tag) { return fused_mark_name(tag); }
 
 const char *skv_kernel_name(int32_t i) { return funnel_kernel_name(i); }
 

@@ -1,0 +1,1324 @@
+// skv_fused.cu -- the whole decode funnel of one cell as ONE thread-block
+// cluster.
+//
+// A cell (slot x KV head) is decoded by a cluster of CL = 16 CTAs, one CTA
+// per SM; one launch covers every cell of the step.  The stages of the
+// staged path (skv_kernels.cu) become phases of a single kernel separated by
+// hardware cluster barriers (barrier.cluster, ~0.25 us) instead of kernel
+// boundaries, and the data a phase hands to the next stays in shared memory:
+//
+//   P0  query operands: every CTA derives the 12 operand rows itself
+//   P1  coarse: the CTA's contiguous slice of the upper plane arrives by TMA
+//       bulk copies (8 KB each, one mbarrier each) and is scored on int8
+//       tensor cores; lo/hi stay in shared memory
+//   P2  coarse threshold: cluster radix select, two 8-bit rounds
+//   P3  survivors: head masks, cluster prefix scan -> global positions
+//   P4  fine: upper+lower rows of the survivors gathered with cp.async
+//   P5  fine top-nprobe per head (cluster radix select), selected bitmap
+//   P6  pool: postings of the selected clusters, spill-2 mate rule, cluster
+//       prefix scan -> pool positions
+//   P7  Stage-1.5 scores over a balanced share of the pool positions
+//   P8  top-1600 per head, ascending union (cluster scan)
+//   P9  Stage-1.6 scores of this CTA's union members
+//   P10 top-256 per head, candidates (cluster scan)
+//   P11 Stage-II scores of this CTA's candidates
+//   P12 exact top-100 per head (CTA h of the cluster), rank order
+//   P13 attention: sink + local + top-100 partials per CTA, combined across
+//       the cluster through distributed shared memory
+//
+// Cluster radix select (P2, P5, P8, P10): every CTA histograms its own keys
+// with shared-memory atomics, adds the non-zero bins into the owning CTA's
+// bins (bin b of head h belongs to CTA (256 h + b) / 64) with
+// red.shared::cluster, and after one cluster barrier every CTA reads the
+// 1024 reduced bins back and derives the same boundary bin.  The owners'
+// bins rotate over three buffers, which makes one barrier per round enough:
+// a buffer is cleared two rounds after it was read and one round before it
+// is added to again.
+//
+// Every intermediate the staged path exposes (lo/hi, thresholds, survivor
+// tags, selected clusters, pool, unions, final ranks and ids, counters) is
+// written to the same Work buffers in the same format, so both paths are
+// checked by the same stage-by-stage parity tests.
+//
+// Waits: the only waits are cluster barriers (all threads of all CTAs reach
+// each one: control flow is uniform by construction) and the coarse-slice
+// mbarriers, which poll a bounded number of times and then record
+// ST_TIMEOUT in the cell's status instead of waiting on.
+#include <cuda_fp8.h>
+
+#include "skv_device.cuh"
+#include "skv_fused.cuh"
+
+namespace skv {
+namespace {
+
+constexpr int CL = 16;                            // CTAs per cluster (per cell)
+constexpr int FT = 512;                           // threads per CTA
+constexpr int FW = FT / 32;                       // warps per CTA
+constexpr int PER_MAX = 2048;                     // centroid rows per CTA
+constexpr int SLICE_CHUNK = 128;                  // rows per bulk copy (8 KB)
+constexpr int NCHUNK = PER_MAX / SLICE_CHUNK;     // mbarriers
+constexpr int POS_MAX = 1024;                     // pool positions per CTA
+constexpr int BIG = PER_MAX * 64;                 // staging area (128 KB)
+constexpr int NPUB = 8;                           // exchange slots
+constexpr long long WAIT_POLLS = 1 << 20;         // mbarrier polls before giving up
+
+// Row strides (bytes) of gathered rows in the staging area: 16 bytes of
+// padding keep the 8-byte fragment loads of a warp on distinct banks.
+constexpr int STRIDE_FINE = 144;   // upper | lower
+constexpr int STRIDE_S2 = 272;     // prefix2 | residual2 | residual4
+constexpr int BATCH_FINE = (BIG / STRIDE_FINE) & ~15;
+constexpr int BATCH_S2 = (BIG / STRIDE_S2) & ~15;
+
+enum Pub { P_SURV = 0, P_SEL = 1, P_POOL = 2, P_U15 = 3, P_CAND = 4 };
+
+struct SelCtl {
+  uint32_t prefix[4], mask[4], krem[4], th[4];
+  int done[4];
+};
+
+struct FusedSmem {
+  uint32_t frag[3 * FRAG_ROW];     // int8 digit fragments of the three operand rows
+  uint32_t hist[4 * 256];          // local histograms / reduced bins read back
+  uint32_t red[3][64];             // bins this CTA owns (three rotating buffers)
+  unsigned long long mbar[NCHUNK];
+  int pub[NPUB][4];                // values published to the cluster
+  int all[CL][4];                  // the cluster's values of the latest exchange
+  SelCtl ctl;
+  int shift[3][4];
+  float qscal[8];
+  int sE[12][8];
+  long long sXp[12][8];            // partial sums of X over 32 dimensions
+  long long sxsum[3][4];           // sum over d of X_d per operand row and head
+  int round, status, n_win, pad_;
+  CellDev cell;                    // this cell's descriptor (read once from global)
+  union {
+    struct { uint16_t lo[4][PER_MAX]; uint16_t hi[4][PER_MAX]; } c;   // P1-P3
+    uint32_t fkey[4][PER_MAX];                                        // P4-P5
+    struct { uint16_t slist[PER_MAX]; int soff[PER_MAX]; int ppre[PER_MAX + 1]; } s;  // P5-P6
+    struct {
+      uint16_t sc15[4][POS_MAX], sc16[4][POS_MAX], sc2[4][POS_MAX];   // ordered BF16 scores
+      int tok[POS_MAX];
+      uint16_t urank[POS_MAX];     // rank among this CTA's union members
+      uint16_t clist[POS_MAX];     // candidates (local positions)
+      uint8_t flag[POS_MAX];       // union member
+    } p;                                                              // P7-P11
+  } b;
+  float sx[4 * D];                 // the cell's four query rows (FP32 of BF16)
+  float kscale[D];                 // per-dimension key scales
+  int offs[PER_MAX + 1];           // CSR offsets of the slice's clusters
+  uint16_t resid[PER_MAX];         // residual norms of the slice (BF16)
+  float scale4[PER_MAX / 32];
+  float fscale[PER_MAX / 32];
+  uint16_t sidx[PER_MAX];          // survivors: slice row
+  uint8_t smask[PER_MAX];          // survivors: head mask (bits 0-3), selected (bit 4)
+  uint32_t selw[PER_MAX / 32];
+  alignas(128) uint8_t big[BIG];
+};
+
+constexpr size_t kSmemBytes = sizeof(FusedSmem) + 128;
+static_assert(kSmemBytes <= 227 * 1024, "fused shared memory exceeds 227 KB");
+
+// Profiling marks: (tag, SM clock) pairs written by one thread when
+// Work::phase_ts is set; each tag names the segment that ends at it.
+enum MarkTag {
+  M_START, M_ISSUE, M_QEXP, M_QPREP, M_STARTED, M_SLICE, M_COARSE, M_HIST, M_SYNC, M_READ, M_CSEL,
+  M_SURV, M_FGATHER, M_FINE, M_FSEL, M_SELLIST, M_SELX, M_KEEP, M_POOL, M_S15G, M_S15, M_S15SEL,
+  M_U15, M_S16, M_S16SEL, M_CAND, M_S2, M_S2SEL, M_ATTN_ITEMS, M_ATTN_CTA, M_ATTN, M_NTAGS
+};
+
+struct Marker {
+  long long *ts;
+  int n;
+  __device__ __forceinline__ void operator()(int tag) {
+    if (ts && n < FUSED_MARKS) {
+      ts[2 * n] = tag;
+      ts[2 * n + 1] = clock64();
+      ++n;
+    }
+  }
+};
+
+// ------------------------------------------------------------ primitives
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Cluster-wide barrier that orders all prior memory operations of every
+// thread (shared, distributed shared and global) before all later ones: the
+// CTA barrier gathers the CTA's operations behind thread 0, whose cluster-
+// scope fence releases them; the arrive itself is relaxed and the wait
+// acquires.  (One fence per CTA instead of one per thread.)
+__device__ __forceinline__ void cluster_sync() {
+  __syncthreads();
+  if (threadIdx.x == 0) asm volatile("fence.acq_rel.cluster;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of cluster_sync(), for overlapping independent work.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Warm L2 with data a later phase gathers (no effect on results).
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+__device__ __forceinline__ uint32_t remote(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_remote(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ float ld_remote_f(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_remote(uint32_t a, uint32_t v) {
+  asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_init(void *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(void *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// Contiguous global -> own shared memory copy on the TMA engine (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, void *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try(void *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase: false after WAIT_POLLS polls.
+__device__ __noinline__ bool mbar_wait(void *bar, uint32_t parity) {
+  for (long long i = 0; i < WAIT_POLLS; ++i)
+    if (mbar_try(bar, parity)) return true;
+  return false;
+}
+// Orders this thread's earlier generic shared-memory accesses before later
+// async-proxy (bulk copy) writes to the same memory.
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ void load_frag(const FusedSmem &S, int row, int lane, BFrag &f) {
+  const uint2 *p = reinterpret_cast<const uint2 *>(S.frag + row * FRAG_ROW);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint2 v = p[(ks * 2 + nt) * 32 + lane];
+      f.b[ks][nt][0] = v.x;
+      f.b[ks][nt][1] = v.y;
+    }
+}
+
+// Every CTA publishes four ints; afterwards S.all[r][k] holds CTA r's values
+// in every CTA.  Contains a cluster barrier.
+__device__ __noinline__ void exchange(FusedSmem &S, int slot, int v0, int v1, int v2, int v3) {
+  if (threadIdx.x == 0) {
+    S.pub[slot][0] = v0;
+    S.pub[slot][1] = v1;
+    S.pub[slot][2] = v2;
+    S.pub[slot][3] = v3;
+  }
+  cluster_sync();
+  if (threadIdx.x < CL * 4) {
+    const int r = threadIdx.x >> 2, k = threadIdx.x & 3;
+    S.all[r][k] = (int)ld_remote(remote(&S.pub[slot][k], r));
+  }
+  __syncthreads();
+}
+__device__ __forceinline__ int before(const FusedSmem &S, int k, int rank) {
+  int s = 0;
+  for (int r = 0; r < rank; ++r) s += S.all[r][k];
+  return s;
+}
+__device__ __forceinline__ int total(const FusedSmem &S, int k) { return before(S, k, CL); }
+
+// Warp-level: bin of the k-th largest element of a 256-bin histogram
+// (bins counted from the top) and the count strictly above it.
+__device__ __forceinline__ bool warp_find_desc(const uint32_t *hist, uint32_t k, int lane, int &bin,
+                                               uint32_t &above) {
+  uint32_t c[8], s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * lane - j]; s += c[j]; }
+  uint32_t incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t excl = incl - s;
+  const bool mine = excl < k && k <= incl;
+  const unsigned bal = __ballot_sync(0xffffffffu, mine);
+  int b = 0;
+  uint32_t ab = 0;
+  if (mine) {
+    uint32_t acc = excl;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (acc + c[j] >= k) { b = 255 - 8 * lane - j; ab = acc; break; }
+      acc += c[j];
+    }
+  }
+  const int src = bal ? __ffs(bal) - 1 : 0;
+  bin = __shfl_sync(0xffffffffu, b, src);
+  above = __shfl_sync(0xffffffffu, ab, src);
+  return bal != 0;
+}
+
+enum KeyKind { KEY_COARSE = 0, KEY_FINE = 1, KEY_S15 = 2, KEY_S16 = 3 };
+
+// This CTA's selection key i of head h.
+//   KEY_COARSE: ordered BF16 lower bound (top 16 bits)
+//   KEY_FINE:   fused IEEE key [bf16 score | u16 survivor position]
+//   KEY_S15:    [ordered score | 0xffff - pool position]
+//   KEY_S16:    as KEY_S15 for union members, 0 for the others
+__device__ __forceinline__ uint32_t select_key(const FusedSmem &S, int kind, int h, int i, int q0) {
+  switch (kind) {
+    case KEY_COARSE: return (uint32_t)S.b.c.lo[h][i] << 16;
+    case KEY_FINE: return S.b.fkey[h][i];
+    case KEY_S15: return ((uint32_t)S.b.p.sc15[h][i] << 16) | (0xffffu - (uint32_t)(q0 + i));
+    default:
+      return S.b.p.flag[i] ? ((uint32_t)S.b.p.sc16[h][i] << 16) | (0xffffu - (uint32_t)(q0 + i)) : 0u;
+  }
+}
+
+// K-th largest of the cluster's keys (select_key of `kind`) for each of
+// the four heads; the top `nbits` bits of the 32-bit keys are significant.  On return S.ctl.th[h] holds, per head:
+//   exact:  the K-th largest key (all nbits resolved);
+//   !exact: a threshold t with exactly K keys >= t when keys are distinct
+//           (the K-th largest key, or the floor of its bin when the whole
+//           bin is taken), 0 when K exceeds the number of keys or the
+//           K-th largest key is 0; 0xffffffff when K == 0.
+// Contains one cluster barrier per 8-bit round (at most nbits / 8).
+__device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, int nbits, bool exact, int kind,
+                                            int q0, Marker &mark) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < 4) {
+    S.ctl.prefix[tid] = 0;
+    S.ctl.mask[tid] = 0;
+    S.ctl.krem[tid] = K;
+    S.ctl.done[tid] = K == 0;
+    S.ctl.th[tid] = K == 0 ? 0xffffffffu : 0u;
+  }
+  __syncthreads();
+  for (int sh = 24; sh >= 32 - nbits; sh -= 8) {
+    if (S.ctl.done[0] && S.ctl.done[1] && S.ctl.done[2] && S.ctl.done[3]) break;
+    const int buf = S.round % 3, nbuf = (S.round + 1) % 3;
+    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
+    __syncthreads();
+    // the four heads in one pass (independent chains per thread); a
+    // finished head matches no key
+    uint32_t pf[4], mk[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const bool live = !S.ctl.done[h];
+      pf[h] = live ? S.ctl.prefix[h] : 1u;
+      mk[h] = live ? S.ctl.mask[h] : 0u;
+    }
+    // run-length counting: a thread counts its current bin per head in a
+    // register and adds it when the bin changes and at the end (the warp's
+    // lanes on lane 0's bin in one atomic); selection keys crowd into few
+    // bins, where per-key shared atomics from all warps serialise
+    uint32_t cur[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu}, run[4] = {0u, 0u, 0u, 0u};
+#pragma unroll 1
+    for (int i = tid; i < nloc; i += FT) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint32_t v = select_key(S, kind, h, i, q0);
+        if ((v & mk[h]) != pf[h]) continue;
+        const uint32_t bin = h * 256 + ((v >> sh) & 255u);
+        if (bin != cur[h]) {
+          if (run[h]) atomicAdd(&S.hist[cur[h]], run[h]);
+          cur[h] = bin;
+          run[h] = 0u;
+        }
+        ++run[h];
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint32_t b0 = __shfl_sync(0xffffffffu, cur[h], 0);
+      const uint32_t on0 = cur[h] == b0 ? run[h] : 0u;
+      const uint32_t tot0 = __reduce_add_sync(0xffffffffu, on0);
+      if (lane == 0) {
+        if (b0 != 0xffffffffu && tot0) atomicAdd(&S.hist[b0], tot0);
+      } else if (cur[h] != b0 && run[h]) {
+        atomicAdd(&S.hist[cur[h]], run[h]);
+      }
+    }
+    if (tid < 64) S.red[nbuf][tid] = 0;
+    __syncthreads();
+    mark(M_HIST);
+    for (int e = tid; e < 4 * 256; e += FT) {
+      const uint32_t c = S.hist[e];
+      if (c) red_remote(remote(&S.red[buf][e & 63], (uint32_t)(e >> 6)), c);
+    }
+    cluster_sync();
+    mark(M_SYNC);
+    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = ld_remote(remote(&S.red[buf][e & 63], (uint32_t)(e >> 6)));
+    __syncthreads();
+    if (warp < 4 && !S.ctl.done[warp]) {
+      const int h = warp;
+      int bin;
+      uint32_t above;
+      const bool found = warp_find_desc(S.hist + h * 256, S.ctl.krem[h], lane, bin, above);
+      if (lane == 0) {
+        if (!found) {
+          S.ctl.done[h] = 1;
+          S.ctl.th[h] = 0u;
+        } else {
+          const uint32_t pf = S.ctl.prefix[h] | ((uint32_t)bin << sh);
+          const uint32_t kr = S.ctl.krem[h] - above;
+          const uint32_t cnt = S.hist[h * 256 + bin];
+          S.ctl.prefix[h] = pf;
+          S.ctl.mask[h] |= 255u << sh;
+          S.ctl.krem[h] = kr;
+          if (sh == 32 - nbits || (!exact && cnt == kr && pf != 0u)) {
+            S.ctl.done[h] = 1;
+            S.ctl.th[h] = pf;
+          }
+        }
+      }
+    }
+    if (tid == 0) S.round++;
+    __syncthreads();
+    mark(M_READ);
+  }
+}
+
+// ----------------------------------------------------- tensor-core dots
+
+// Exact digit sums of 16 rows x 4 heads on int8 tensor cores; rows g and
+// g+8 of the tile are given as shared-memory row pointers.  The weights are
+// the raw codes; the odd-integer weights of the scores (2c - (2^b - 1)) are
+// applied afterwards as 2 * dot - (2^b - 1) * sum(X), exactly, in int64.
+//   KIND 0: 2-bit codes (0..3) of one 64-byte plane (coarse u, Stage-1.5 p)
+//   KIND 1: 4-bit codes 4u + l from two 64-byte planes at +0, +64
+template <int KIND>
+__device__ __forceinline__ void tile_dots(const uint8_t *rg, const uint8_t *r8, int t, const BFrag &F,
+                                          long long (&d)[2]) {
+  int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  if (KIND == 0) {
+    const uint4 *pg = reinterpret_cast<const uint4 *>(rg), *p8 = reinterpret_cast<const uint4 *>(r8);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 x = pg[q], y = p8[q];
+      const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int ks = 2 * q + h2;
+        const uint32_t a0 = w2(xs[2 * h2], t), a1 = w2(ys[2 * h2], t);
+        const uint32_t a2 = w2(xs[2 * h2 + 1], t), a3 = w2(ys[2 * h2 + 1], t);
+        mma_s8(acc[0], a0, a1, a2, a3, F.b[ks][0][0], F.b[ks][0][1]);
+        mma_s8(acc[1], a0, a1, a2, a3, F.b[ks][1][0], F.b[ks][1][1]);
+      }
+    }
+    combine_digits(acc, t, d);
+  } else {
+    const uint2 *ug = reinterpret_cast<const uint2 *>(rg), *lg = reinterpret_cast<const uint2 *>(rg + 64);
+    const uint2 *u8 = reinterpret_cast<const uint2 *>(r8), *l8 = reinterpret_cast<const uint2 *>(r8 + 64);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint2 a = ug[ks], b = lg[ks], e = u8[ks], f = l8[ks];
+      const uint32_t a0 = (w2(a.x, t) << 2) | w2(b.x, t), a1 = (w2(e.x, t) << 2) | w2(f.x, t);
+      const uint32_t a2 = (w2(a.y, t) << 2) | w2(b.y, t), a3 = (w2(e.y, t) << 2) | w2(f.y, t);
+      mma_s8(acc[0], a0, a1, a2, a3, F.b[ks][0][0], F.b[ks][0][1]);
+      mma_s8(acc[1], a0, a1, a2, a3, F.b[ks][1][0], F.b[ks][1][1]);
+    }
+    combine_digits(acc, t, d);
+  }
+}
+
+// Residual4 nibbles of dimensions 16*word + 4*i + t (bytes i) from the two
+// residual4 words covering those 16 dimensions.
+__device__ __forceinline__ uint32_t nib(uint32_t lo_word, uint32_t hi_word, int t) {
+  return __byte_perm((lo_word >> (4 * t)) & 0x000f000fu, (hi_word >> (4 * t)) & 0x000f000fu, 0x6420);
+}
+
+// The Stage-1.6 and Stage-II raw-code sums of one tile at once: dh over the
+// 4-bit codes c4 (prefix2 | residual2 at +0, +64), dl over the residual4
+// nibbles r4 (+128).
+__device__ __forceinline__ void tile_dots_8bit(const uint8_t *rg, const uint8_t *r8, int t, const BFrag &F,
+                                               long long (&dh)[2], long long (&dl)[2]) {
+  int hi[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, lo[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  const uint2 *pg = reinterpret_cast<const uint2 *>(rg), *qg = reinterpret_cast<const uint2 *>(rg + 64);
+  const uint4 *ng = reinterpret_cast<const uint4 *>(rg + 128);
+  const uint2 *p8 = reinterpret_cast<const uint2 *>(r8), *q8 = reinterpret_cast<const uint2 *>(r8 + 64);
+  const uint4 *n8 = reinterpret_cast<const uint4 *>(r8 + 128);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint2 vpg = pg[ks], vqg = qg[ks], vp8 = p8[ks], vq8 = q8[ks];
+    const uint4 vng = ng[ks], vn8 = n8[ks];
+    const uint32_t a0 = (w2(vpg.x, t) << 2) | w2(vqg.x, t), a1 = (w2(vp8.x, t) << 2) | w2(vq8.x, t);
+    const uint32_t a2 = (w2(vpg.y, t) << 2) | w2(vqg.y, t), a3 = (w2(vp8.y, t) << 2) | w2(vq8.y, t);
+    mma_s8(hi[0], a0, a1, a2, a3, F.b[ks][0][0], F.b[ks][0][1]);
+    mma_s8(hi[1], a0, a1, a2, a3, F.b[ks][1][0], F.b[ks][1][1]);
+    const uint32_t b0 = nib(vng.x, vng.y, t), b1 = nib(vn8.x, vn8.y, t);
+    const uint32_t b2 = nib(vng.z, vng.w, t), b3 = nib(vn8.z, vn8.w, t);
+    mma_s8(lo[0], b0, b1, b2, b3, F.b[ks][0][0], F.b[ks][0][1]);
+    mma_s8(lo[1], b0, b1, b2, b3, F.b[ks][1][0], F.b[ks][1][1]);
+  }
+  combine_digits(hi, t, dh);
+  combine_digits(lo, t, dl);
+}
+
+__device__ __forceinline__ void fp8x8(uint2 v, float *o) {
+  const uint32_t ws[2] = {v.x, v.y};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const __half2_raw a = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(ws[k] & 0xffffu), __NV_E4M3);
+    const __half2_raw b = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(ws[k] >> 16), __NV_E4M3);
+    const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&a));
+    const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&b));
+    o[4 * k + 0] = fa.x; o[4 * k + 1] = fa.y; o[4 * k + 2] = fb.x; o[4 * k + 3] = fb.y;
+  }
+}
+
+// ------------------------------------------------------------ the kernel
+
+__global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, t = lane & 3;
+  const int hA = t >> 1, hB = 2 + hA;
+  const int rank = (int)cluster_rank();
+  const int cell = blockIdx.y, slot = cell >> 2, g = cell & 3;
+  if (tid < (int)(sizeof(CellDev) / 4))
+    reinterpret_cast<uint32_t *>(&S.cell)[tid] = reinterpret_cast<const uint32_t *>(w.cells + cell)[tid];
+  __syncthreads();
+  const CellDev &c = S.cell;
+  const int nc = w.nc, cap = w.cap;
+  const int per = ((nc + CL * 32 - 1) / (CL * 32)) * 32;
+  const int r0 = min(nc, rank * per), r1 = min(nc, r0 + per), nrows = r1 - r0;
+  const uint32_t P = (uint32_t)c.nprobe;
+  Marker mark{(w.phase_ts && cell == 0 && rank == 0 && tid == 0) ? w.phase_ts : nullptr, 0};
+  int *counts = w.counts + cell * NCOUNT;
+  mark(M_START);
+
+  // ---------------------------------------------------------------- P0
+  // the small inputs first, so that they do not queue behind the slice
+  for (int i = tid; i < 4 * D; i += FT) S.sx[i] = bf16f(w.q[((size_t)slot * 16 + g * 4) * D + i]);
+  for (int i = tid; i < D; i += FT) S.kscale[i] = c.key_scale[i];
+  for (int i = tid; i < nrows; i += FT) S.resid[i] = c.resid[r0 + i];
+  for (int i = tid; i <= nrows; i += FT) S.offs[i] = c.offsets[r0 + i];
+  for (int i = tid; i < (nrows >> 5); i += FT) {
+    S.scale4[i] = c.coarse_scale4[(r0 >> 5) + i];
+    S.fscale[i] = c.fine_scale[(r0 >> 5) + i];
+  }
+  for (int i = tid; i < 3 * 64; i += FT) (&S.red[0][0])[i] = 0;
+  if (tid == 0) {
+    for (int k = 0; k < NCHUNK; ++k) mbar_init(&S.mbar[k], 1);
+    mbar_fence_init();
+    for (int k = 0; k * SLICE_CHUNK < nrows; ++k) {
+      const int rows = min(SLICE_CHUNK, nrows - k * SLICE_CHUNK);
+      mbar_expect_tx(&S.mbar[k], (uint32_t)rows * 64u);
+      bulk_g2s(S.big + k * SLICE_CHUNK * 64, c.upper + (size_t)(r0 + k * SLICE_CHUNK) * 64, (uint32_t)rows * 64u,
+               &S.mbar[k]);
+    }
+    S.round = 0;
+    S.status = 0;
+  }
+  __syncthreads();
+  mark(M_ISSUE);
+  {
+    // 12 operand rows (row r, head h); thread (half, d) takes rows half + 2k
+    const int d = tid & 255, half = tid >> 8;
+    // operand row r of head h at dimension d
+    auto operand = [&](int r, int h) {
+      const float xa = S.sx[h * D + d];
+      if (r == R_Q) return xa;
+      const float prod = __fmul_rn(xa, S.kscale[d]);
+      return r == R_Q15 ? __fmul_rn(bf16f(bf16_rne(__fmul_rn(prod, 0.015625f))), 16.0f)
+                        : bf16f(bf16_rne(__fmul_rn(prod, 0.00390625f)));
+    };
+#pragma unroll 1
+    for (int k = 0; k < 6; ++k) {
+      const int p = half + 2 * k, r = p >> 2, h = p & 3;
+      const float x = operand(r, h);
+      int e = x != 0.0f ? ilogbf(x) : INT_MIN;
+      e = __reduce_max_sync(0xffffffffu, e);
+      if (lane == 0) S.sE[p][warp & 7] = e;
+    }
+    __syncthreads();
+    mark(M_QEXP);
+    uint8_t *fb = reinterpret_cast<uint8_t *>(S.frag);
+#pragma unroll 1
+    for (int k = 0; k < 6; ++k) {
+      const int p = half + 2 * k, r = p >> 2, h = p & 3;
+      int E = INT_MIN;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) E = max(E, S.sE[p][j]);
+      int X = 0;
+      if (E != INT_MIN) {
+        const double v = (double)operand(r, h);
+        if (!(fabs(v) < pow2d(E - 22))) X = __double2int_rn(v * pow2d(29 - E));
+      }
+      int dg[4];
+      dg[0] = (int)(int8_t)(X & 0xff);
+      int rest = (X - dg[0]) >> 8;
+      dg[1] = (int)(int8_t)(rest & 0xff);
+      rest = (rest - dg[1]) >> 8;
+      dg[2] = (int)(int8_t)(rest & 0xff);
+      dg[3] = (rest - dg[2]) >> 8;
+      const int ks = d >> 5, reg = (d >> 4) & 1, byte = (d >> 2) & 3, tq = d & 3, nt = h >> 1;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int lane_b = 4 * (4 * (h & 1) + j) + tq;
+        fb[r * FRAG_ROW * 4 + (((ks * 2 + nt) * 32 + lane_b) * 2 + reg) * 4 + byte] = (uint8_t)(int8_t)dg[j];
+      }
+      if (d == 0) S.shift[r][h] = E == INT_MIN ? 0 : E - 29;
+      long long xsum = X;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) xsum += __shfl_xor_sync(0xffffffffu, xsum, o);
+      if (lane == 0) S.sXp[p][warp & 7] = xsum;
+    }
+    if (warp < 4) {
+      // lambda*|q| and 3*sum(q): pairwise FP64 sums in dimension order
+      const int h = warp;
+      double v[8], sq[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { v[j] = (double)S.sx[h * D + 8 * lane + j]; sq[j] = v[j] * v[j]; }
+      double a = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+      double b = ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        a = a + __shfl_xor_sync(0xffffffffu, a, o);
+        b = b + __shfl_xor_sync(0xffffffffu, b, o);
+      }
+      if (lane == 0) {
+        S.qscal[h] = __fmul_rn(__double2float_rn(__dsqrt_rn(b)), c.lam);
+        S.qscal[4 + h] = __fmul_rn(3.0f, __double2float_rn(a));
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < 12) {
+    long long x = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x += S.sXp[tid][j];
+    S.sxsum[tid >> 2][tid & 3] = x;
+  }
+  mark(M_QPREP);
+  // this CTA has started and its owner bins are zero; the matching wait
+  // precedes the first distributed-shared-memory access (P2)
+  cluster_arrive();
+  __syncthreads();
+  mark(M_STARTED);
+
+  // ---------------------------------------------------------------- P1
+  {
+    BFrag F;
+    load_frag(S, R_Q, lane, F);
+    const double scA = pow2d(S.shift[R_Q][hA]), scB = pow2d(S.shift[R_Q][hB]);
+    const float qnA = S.qscal[hA], qnB = S.qscal[hB], c3A = S.qscal[4 + hA], c3B = S.qscal[4 + hB];
+    const int tiles = nrows >> 4;
+    if (mark.ts && tiles > 0) {
+      mbar_wait(&S.mbar[(tiles * 16 - 1) / SLICE_CHUNK], 0);
+      mark(M_SLICE);
+    }
+    uint16_t *glo = w.lo + (size_t)cell * G * nc, *ghi = w.hi + (size_t)cell * G * nc;
+    for (int tile = warp; tile < tiles; tile += FW) {
+      if (!mbar_wait(&S.mbar[(tile * 16) / SLICE_CHUNK], 0)) atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
+      long long dsum[2];
+      tile_dots<0>(S.big + (tile * 16 + gq) * 64, S.big + (tile * 16 + gq + 8) * 64, t, F, dsum);
+      const int lr = tile * 16 + gq + ((t & 1) << 3), row = r0 + lr;
+      const float sc4 = S.scale4[lr >> 5];
+      const float rr = bf16f(S.resid[lr]);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int h = k ? hB : hA;
+        const float dot = exact_to_float(dsum[k], k ? scB : scA);
+        const float centered = __fsub_rn(__fmul_rn(2.0f, dot), k ? c3B : c3A);
+        const float v = __fmul_rn(centered, sc4);
+        const float margin = __fmul_rn(k ? qnB : qnA, rr);
+        const uint16_t lo = (uint16_t)ord16(bf16_rne(__fsub_rn(v, margin)));
+        const uint16_t hi = (uint16_t)ord16(bf16_rne(__fadd_rn(v, margin)));
+        S.b.c.lo[h][lr] = lo;
+        S.b.c.hi[h][lr] = hi;
+        glo[(size_t)h * nc + row] = lo;
+        ghi[(size_t)h * nc + row] = hi;
+      }
+    }
+  }
+  __syncthreads();
+  mark(M_COARSE);
+
+  // ---------------------------------------------------------------- P2
+  cluster_wait();
+  {
+    cluster_select(S, nrows, P, 16, true, KEY_COARSE, 0, mark);
+  }
+  uint32_t tco[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) tco[h] = S.ctl.th[h] >> 16;
+  if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_COARSE * G + tid] = S.ctl.th[tid] >> 16;
+  mark(M_CSEL);
+
+  // ---------------------------------------------------------------- P3
+  int nsurv;
+  {
+    const int i0 = tid * 4;
+    uint32_t m[4];
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + j;
+      m[j] = 0;
+      if (i < nrows) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) m[j] |= (uint32_t)(S.b.c.hi[h][i] >= tco[h]) << h;
+      }
+      cnt += m[j] != 0;
+    }
+    int r = block_exclusive_scan(cnt, &nsurv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (m[j]) {
+        S.sidx[r] = (uint16_t)(i0 + j);
+        S.smask[r] = (uint8_t)m[j];
+        ++r;
+      }
+  }
+  exchange(S, P_SURV, nsurv, 0, 0, 0);
+  const int surv_base = before(S, 0, rank);
+  for (int k = tid; k < nsurv; k += FT) {
+    const int lr = S.sidx[k];
+    w.tags[(size_t)cell * nc + surv_base + k] = (uint32_t)(r0 + lr) | ((uint32_t)S.smask[k] << 28);
+    // posting lists a survivor would bring into the pool
+    const int b = S.offs[lr], e = S.offs[lr + 1];
+    if (e > b) {
+      prefetch_l2(c.values + b);
+      prefetch_l2(c.mates + b);
+      if (((b * 4) >> 7) != (((e - 1) * 4) >> 7)) {
+        prefetch_l2(c.values + e - 1);
+        prefetch_l2(c.mates + e - 1);
+      }
+    }
+  }
+  if (rank == 0 && tid == 0) counts[C_TAGS] = total(S, 0);
+  mark(M_SURV);
+
+  // ---------------------------------------------------------------- P4
+  {
+    BFrag F;
+    load_frag(S, R_Q, lane, F);
+    const double scA = pow2d(S.shift[R_Q][hA]), scB = pow2d(S.shift[R_Q][hB]);
+    for (int b0 = 0; b0 < nsurv; b0 += BATCH_FINE) {
+      const int nb = min(BATCH_FINE, nsurv - b0);
+      __syncthreads();
+      for (int q = tid; q < nb * 8; q += FT) {
+        const int rr = q >> 3, part = q & 7, cid = r0 + S.sidx[b0 + rr];
+        const uint8_t *src = (part < 4 ? c.upper : c.lower) + (size_t)cid * 64 + (part & 3) * 16;
+        cp16(S.big + rr * STRIDE_FINE + part * 16, src);
+      }
+      cp_wait_all();
+      __syncthreads();
+      if (b0 == 0) mark(M_FGATHER);
+      const int tiles = (nb + 15) >> 4;
+      for (int tile = warp; tile < tiles; tile += FW) {
+        const int rg = tile * 16 + gq, r8 = rg + 8;
+        long long dsum[2];
+        tile_dots<1>(S.big + min(rg, nb - 1) * STRIDE_FINE, S.big + min(r8, nb - 1) * STRIDE_FINE, t, F, dsum);
+        dsum[0] = 2 * dsum[0] - 15 * S.sxsum[R_Q][hA];  // weights 2*c4 - 15
+        dsum[1] = 2 * dsum[1] - 15 * S.sxsum[R_Q][hB];
+        const int row = (t & 1) ? r8 : rg;
+        if (row < nb) {
+          const int k = b0 + row, lr = S.sidx[k], mk = S.smask[k], pos = surv_base + k;
+          const float fs = S.fscale[lr >> 5];
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const int h = kk ? hB : hA;
+            uint32_t key = 0;
+            if ((mk >> h) & 1)
+              key = ord_fused(bf16_rne(__fmul_rn(exact_to_float(dsum[kk], kk ? scB : scA), fs)), (uint32_t)pos);
+            S.b.fkey[h][k] = key;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  mark(M_FINE);
+
+  // ---------------------------------------------------------------- P5
+  {
+    cluster_select(S, nsurv, P, 32, false, KEY_FINE, 0, mark);
+  }
+  mark(M_FSEL);
+  uint32_t st = 0;
+  {
+    uint32_t tf[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      tf[h] = S.ctl.th[h];
+      if (tf[h] == 0u) { tf[h] = 0xffffffffu; st |= ST_FINE_SHORT; }
+    }
+    if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_FINE * G + tid] = tf[tid];
+    for (int k = tid; k < nsurv; k += FT) {
+      bool s = false;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) s |= S.b.fkey[h][k] >= tf[h];
+      if (s) S.smask[k] |= 0x10;
+    }
+    for (int i = tid; i < PER_MAX / 32; i += FT) S.selw[i] = 0;
+    __syncthreads();
+    for (int k = tid; k < nsurv; k += FT)
+      if (S.smask[k] & 0x10) atomicOr(&S.selw[S.sidx[k] >> 5], 1u << (S.sidx[k] & 31));
+    __syncthreads();
+    for (int i = tid; i < (nrows >> 5); i += FT) w.selbits[(size_t)cell * (nc >> 5) + (r0 >> 5) + i] = S.selw[i];
+  }
+  // selected clusters in ascending order with their posting ranges
+  int nsel, npost;
+  {
+    const int i0 = tid * 4;
+    int f[4], cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[j] = (i0 + j < nsurv) && (S.smask[i0 + j] & 0x10);
+      cnt += f[j];
+    }
+    int r = block_exclusive_scan(cnt, &nsel);  // (all reads of fkey precede this barrier)
+    int len[4], psum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      len[j] = 0;
+      if (f[j]) {
+        const int lr = S.sidx[i0 + j];
+        const int b = S.offs[lr];
+        len[j] = S.offs[lr + 1] - b;
+        S.b.s.slist[r] = (uint16_t)lr;
+        S.b.s.soff[r] = b;
+        psum += len[j];
+        ++r;
+      }
+    }
+    int pr = block_exclusive_scan(psum, &npost);
+    r -= cnt;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (f[j]) { S.b.s.ppre[r++] = pr; pr += len[j]; }
+    if (tid == 0) S.b.s.ppre[nsel] = npost;
+  }
+  mark(M_SELLIST);
+  exchange(S, P_SEL, nsel, npost, 0, 0);  // also publishes the selected bitmap words
+  const int sel_base = before(S, 0, rank), nsel_all = total(S, 0), npost_all = total(S, 1);
+  for (int k = tid; k < nsel; k += FT)
+    if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = r0 + S.b.s.slist[k];
+  mark(M_SELX);
+
+  // ---------------------------------------------------------------- P6
+  int nkept = 0;
+  {
+    int *klist = reinterpret_cast<int *>(S.big);
+    const int KMAX = BIG / 4;
+    const uint32_t *selbits = w.selbits + (size_t)cell * (nc >> 5);
+    for (int p0 = 0; p0 < npost; p0 += FT * 4) {
+      int jj[4], cid[4], mate[4], tok[4], keep[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int p = p0 + tid * 4 + j;
+        jj[j] = -1;
+        cid[j] = 0;
+        if (p < npost) {
+          int lo = 0, hi = nsel - 1;
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (S.b.s.ppre[mid] <= p) lo = mid; else hi = mid - 1;
+          }
+          cid[j] = r0 + S.b.s.slist[lo];
+          jj[j] = S.b.s.soff[lo] + (p - S.b.s.ppre[lo]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        mate[j] = jj[j] >= 0 ? c.mates[jj[j]] : -1;
+        tok[j] = jj[j] >= 0 ? c.values[jj[j]] : 0;
+      }
+      int cnt = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool dup = mate[j] >= 0 && mate[j] < cid[j] && ((__ldcg(selbits + (mate[j] >> 5)) >> (mate[j] & 31)) & 1u);
+        keep[j] = jj[j] >= 0 && !dup;
+        cnt += keep[j];
+      }
+      int tot;
+      int r = nkept + block_exclusive_scan(cnt, &tot);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (keep[j]) {
+          if (r < KMAX) klist[r] = tok[j];
+          ++r;
+        }
+      nkept += tot;
+    }
+  }
+  mark(M_KEEP);
+  exchange(S, P_POOL, nkept, 0, 0, 0);
+  const int kept_base = before(S, 0, rank), npool = total(S, 0);
+  {
+    const int *klist = reinterpret_cast<const int *>(S.big);
+    int32_t *pool = w.pool + (size_t)cell * cap;
+    for (int k = tid; k < nkept && k < BIG / 4; k += FT)
+      if (kept_base + k < cap) pool[kept_base + k] = klist[k];
+  }
+  if (npool > cap) st |= ST_POOL_OVER;
+  if (npool < M15_MIN) st |= ST_POOL_UNDER;
+  if (rank == 0 && tid == 0) {
+    counts[C_POOL] = npool;
+    counts[C_SEL] = min(nsel_all, SEL_MAX);
+    counts[C_POSTINGS] = npost_all;
+    counts[C_STATUS] = (int)st;
+  }
+  cluster_sync();  // the pool is complete in global memory
+  mark(M_POOL);
+
+  // ---------------------------------------------------------------- P7
+  // Stage-1.5, 1.6 and II scores of a balanced share of the pool positions,
+  // from one gather of their prefix2 | residual2 | residual4 rows.  The 1.6
+  // and II selections break ties by the lower union (candidate) position,
+  // which orders members like their pool position does, so their keys can
+  // carry the pool position and need no second gather.
+  const int n15 = min(npool, cap);
+  const int pc = ((n15 + CL * 32 - 1) / (CL * 32)) * 32;
+  const int q0 = min(n15, rank * pc), m15 = min(n15, q0 + pc) - q0;
+  {
+    for (int i = tid; i < m15; i += FT) S.b.p.tok[i] = __ldcg(w.pool + (size_t)cell * cap + q0 + i);
+    __syncthreads();
+    for (int b0 = 0; b0 < m15; b0 += BATCH_S2) {
+      const int nb = min(BATCH_S2, m15 - b0);
+      __syncthreads();
+      for (int q = tid; q < nb * 16; q += FT) {
+        const int rr = q >> 4, part = q & 15;
+        const int tok = S.b.p.tok[b0 + rr];
+        const uint8_t *src = part < 4   ? c.prefix2 + (size_t)tok * 64 + part * 16
+                             : part < 8 ? c.residual2 + (size_t)tok * 64 + (part - 4) * 16
+                                        : c.residual4 + (size_t)tok * 128 + (part - 8) * 16;
+        cp16(S.big + rr * STRIDE_S2 + part * 16, src);
+      }
+      cp_wait_all();
+      __syncthreads();
+      if (b0 == 0) mark(M_S15G);
+      const int tiles = (nb + 15) >> 4;
+      {
+        BFrag F;
+        load_frag(S, R_Q15, lane, F);
+        const double scA = pow2d(S.shift[R_Q15][hA]), scB = pow2d(S.shift[R_Q15][hB]);
+        for (int tile = warp; tile < tiles; tile += FW) {
+          const int rg = tile * 16 + gq, r8 = rg + 8;
+          long long dsum[2];
+          tile_dots<0>(S.big + min(rg, nb - 1) * STRIDE_S2, S.big + min(r8, nb - 1) * STRIDE_S2, t, F, dsum);
+          dsum[0] = 2 * dsum[0] - 3 * S.sxsum[R_Q15][hA];  // weights 2p - 3
+          dsum[1] = 2 * dsum[1] - 3 * S.sxsum[R_Q15][hB];
+          const int row = (t & 1) ? r8 : rg;
+          if (row < nb) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+              S.b.p.sc15[k ? hB : hA][b0 + row] = (uint16_t)ord16(bf16_rne(exact_to_float(dsum[k], k ? scB : scA)));
+          }
+        }
+      }
+      {
+        BFrag F;
+        load_frag(S, R_QS, lane, F);
+        const double s16A = pow2d(S.shift[R_QS][hA] + 4), s16B = pow2d(S.shift[R_QS][hB] + 4);
+        const double s2A = pow2d(S.shift[R_QS][hA]), s2B = pow2d(S.shift[R_QS][hB]);
+        for (int tile = warp; tile < tiles; tile += FW) {
+          const int rg = tile * 16 + gq, r8 = rg + 8;
+          long long dh[2], dl[2];
+          tile_dots_8bit(S.big + min(rg, nb - 1) * STRIDE_S2, S.big + min(r8, nb - 1) * STRIDE_S2, t, F, dh, dl);
+          const int row = (t & 1) ? r8 : rg;
+          if (row < nb) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int h = k ? hB : hA;
+              const long long sx = S.sxsum[R_QS][h];
+              // operand 16*qs, weights 2*c4 - 15: the same digits, scale 2^4 higher
+              S.b.p.sc16[h][b0 + row] =
+                  (uint16_t)ord16(bf16_rne(exact_to_float(2 * dh[k] - 15 * sx, k ? s16B : s16A)));
+              // weights 2*code8 - 255 = 16*(2*c4 - 15) + (2*r4 - 15)
+              S.b.p.sc2[h][b0 + row] =
+                  (uint16_t)ord16(bf16_rne(exact_to_float(32 * dh[k] + 2 * dl[k] - 255 * sx, k ? s2B : s2A)));
+            }
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  mark(M_S15);
+
+  // ---------------------------------------------------------------- P8
+  {
+    cluster_select(S, m15, (uint32_t)min(UNION15, n15), 32, false, KEY_S15, q0, mark);
+  }
+  mark(M_S15SEL);
+  int nu;
+  {
+    uint32_t tu[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) tu[h] = S.ctl.th[h] ? S.ctl.th[h] : 0xffffffffu;
+    if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_S15 * G + tid] = tu[tid];
+    const int i0 = tid * 2;
+    int f[2], cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = i0 + j;
+      f[j] = 0;
+      if (i < m15) {
+        const uint32_t lowk = 0xffffu - (uint32_t)(q0 + i);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) f[j] |= (((uint32_t)S.b.p.sc15[h][i] << 16) | lowk) >= tu[h];
+      }
+      cnt += f[j];
+    }
+    int r = block_exclusive_scan(cnt, &nu);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (i0 + j < m15) {
+        S.b.p.flag[i0 + j] = (uint8_t)f[j];
+        S.b.p.urank[i0 + j] = (uint16_t)r;
+        r += f[j];
+      }
+  }
+  exchange(S, P_U15, nu, 0, 0, 0);
+  const int u_base = before(S, 0, rank), nu_all = min(total(S, 0), U15_MAX);
+  for (int i = tid; i < m15; i += FT) {
+    if (!S.b.p.flag[i]) continue;
+    const int u = u_base + S.b.p.urank[i];
+    if (u < U15_MAX) {
+      w.u15pos[(size_t)cell * U15_MAX + u] = q0 + i;
+      w.u15tok[(size_t)cell * U15_MAX + u] = S.b.p.tok[i];
+    }
+  }
+  if (rank == 0 && tid == 0) counts[C_U15] = nu_all;
+  mark(M_U15);
+
+  // ---------------------------------------------------------------- P9
+  {
+    cluster_select(S, m15, (uint32_t)min(M16, nu_all), 32, false, KEY_S16, q0, mark);
+  }
+  mark(M_S16SEL);
+  int ncl;
+  {
+    uint32_t tc[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) tc[h] = S.ctl.th[h] ? S.ctl.th[h] : 0xffffffffu;
+    if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_S16 * G + tid] = tc[tid];
+    const int i0 = tid * 2;
+    int f[2], cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = i0 + j;
+      f[j] = 0;
+      if (i < m15 && S.b.p.flag[i]) {
+        const uint32_t lowk = 0xffffu - (uint32_t)(q0 + i);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) f[j] |= (((uint32_t)S.b.p.sc16[h][i] << 16) | lowk) >= tc[h];
+      }
+      cnt += f[j];
+    }
+    int r = block_exclusive_scan(cnt, &ncl);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (f[j]) S.b.p.clist[r++] = (uint16_t)(i0 + j);
+  }
+  exchange(S, P_CAND, ncl, 0, 0, 0);
+  const int c_base = before(S, 0, rank), ncand = min(total(S, 0), CAND_MAX);
+  if (rank == 0 && tid == 0) counts[C_CAND] = ncand;
+  // candidates: their union position, and their Stage-II key and token for
+  // each head pushed to CTA h (slot = candidate rank)
+  for (int k = tid; k < ncl; k += FT) {
+    const int cr = c_base + k;
+    if (cr >= CAND_MAX) break;
+    const int i = S.b.p.clist[k];
+    const uint32_t u = (uint32_t)(u_base + S.b.p.urank[i]);
+    w.cand[(size_t)cell * CAND_MAX + cr] = (int)u;
+    const int tok = S.b.p.tok[i];
+    prefetch_l2_bulk(c.kv8 + (size_t)tok * REC, REC);  // for attention should it win
+    uint32_t *k2 = reinterpret_cast<uint32_t *>(S.big);
+    int *t2 = reinterpret_cast<int *>(S.big) + CAND_MAX;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const uint32_t key = ((uint32_t)S.b.p.sc2[h][i] << 16) | (0xffffu - u);
+      st_remote(remote(k2 + cr, (uint32_t)h), key);
+      st_remote(remote(t2 + cr, (uint32_t)h), (uint32_t)tok);
+    }
+  }
+  cluster_sync();  // Stage-II keys of all candidates are in CTAs 0-3
+  mark(M_S2);
+
+  // --------------------------------------------------------------- P12
+  if (rank < G) {
+    // exact top-100 of head h in rank order: block radix select over the
+    // (at most 1024) candidate keys held two per thread, then ranks
+    const int h = rank;
+    const uint32_t *k2 = reinterpret_cast<const uint32_t *>(S.big);
+    const int *t2 = reinterpret_cast<const int *>(S.big) + CAND_MAX;
+    uint32_t *wkey = reinterpret_cast<uint32_t *>(S.big + 8 * CAND_MAX);
+    int *widx = reinterpret_cast<int *>(S.big + 8 * CAND_MAX) + TOPK;
+    const uint32_t v[2] = {tid < ncand ? k2[tid] : 0u, tid + FT < ncand ? k2[tid + FT] : 0u};
+    const uint32_t K = (uint32_t)min(TOPK, ncand);
+    uint32_t prefix = 0, mask = 0, krem = K;
+    if (tid == 0) { S.n_win = 0; S.ctl.done[0] = K == 0; }
+    for (int sh = 24; sh >= 0; sh -= 8) {
+      __syncthreads();
+      if (S.ctl.done[0]) break;
+      for (int e = tid; e < 256; e += FT) S.hist[e] = 0;
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+        hist_add_warp(S.hist, v[r] != 0u && (v[r] & mask) == prefix ? (v[r] >> sh) & 255u : 0xffffffffu);
+      __syncthreads();
+      if (warp == 0) {
+        int bin;
+        uint32_t above;
+        warp_find_desc(S.hist, krem, lane, bin, above);
+        if (lane == 0) {
+          S.ctl.prefix[0] = prefix | ((uint32_t)bin << sh);
+          S.ctl.krem[0] = krem - above;
+          S.ctl.done[0] = sh == 0 || S.hist[bin] == krem - above;
+        }
+      }
+      __syncthreads();
+      prefix = S.ctl.prefix[0];
+      krem = S.ctl.krem[0];
+      mask |= 255u << sh;
+    }
+    // keys are distinct and non-zero: exactly K of them are >= prefix
+    const uint32_t th = K ? prefix : 0xffffffffu;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int slot = warp_claim(&S.n_win, v[r] != 0u && v[r] >= th);
+      if (slot >= 0 && slot < TOPK) { wkey[slot] = v[r]; widx[slot] = tid + r * FT; }
+    }
+    __syncthreads();
+    const int m = min(S.n_win, TOPK);
+    int32_t *fpos = w.final_pos + ((size_t)cell * G + h) * TOPK;
+    int32_t *fids = w.final_ids + ((size_t)cell * G + h) * TOPK;
+    if (tid < m) {
+      const uint32_t key = wkey[tid];
+      int rk = 0;
+      for (int j = 0; j < m; ++j) rk += wkey[j] > key;
+      fpos[rk] = (int)(0xffffu - (key & 0xffffu));
+      fids[rk] = t2[widx[tid]];
+    } else if (tid < TOPK) {
+      // fewer than 100 candidates: a failed step the status word reports
+      fpos[tid] = -1;
+      fids[tid] = 0;
+    }
+  }
+  cluster_sync();  // final ids complete in global memory
+  mark(M_S2SEL);
+
+  // --------------------------------------------------------------- P13
+  {
+    const int sink = w.sink, local = w.local, T = w.T, dense = sink + local;
+    const int nitems = dense + G * TOPK;
+    const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
+    float qv[G][8];
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qv[h][e] = S.sx[h * D + 8 * lane + e] * qscale;
+    float m[G], l[G], o[G][8];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      m[h] = -INFINITY;
+      l[h] = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
+    }
+    const int nw = CL * FW, gw = rank * FW + warp;
+    const int32_t *fids = w.final_ids + (size_t)cell * G * TOPK;
+    // this warp's items are gw, gw + nw, ...: lane j holds item j's token and
+    // head (-1: dense key shared by the four heads); records are loaded one
+    // item ahead of the one being folded in
+    const int nmine = gw < nitems ? (nitems - gw + nw - 1) / nw : 0;
+    int my_tok = 0, my_head = -1;
+    if (lane < nmine) {
+      const int it = gw + lane * nw;
+      if (it < sink) {
+        my_tok = it;
+      } else if (it < dense) {
+        my_tok = T - local + (it - sink);
+      } else {
+        const int r = it - dense;
+        my_head = r / TOPK;
+        my_tok = __ldcg(fids + r);
+      }
+    }
+    auto record = [&](int j, uint2 &kb, uint2 &vb) {
+      const uint8_t *rec = c.kv8 + (size_t)__shfl_sync(0xffffffffu, my_tok, j) * REC;
+      kb = *reinterpret_cast<const uint2 *>(rec + 8 * lane);
+      vb = *reinterpret_cast<const uint2 *>(rec + 256 + 8 * lane);
+    };
+    uint2 kb, vb;
+    if (nmine > 0) record(0, kb, vb);
+#pragma unroll 1
+    for (int j = 0; j < nmine; ++j) {
+      const int head = __shfl_sync(0xffffffffu, my_head, j);
+      float kf[8], vf[8];
+      fp8x8(kb, kf);
+      fp8x8(vb, vf);
+      if (j + 1 < nmine) record(j + 1, kb, vb);
+      float dot[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float a = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a = fmaf(qv[h][e], kf[e], a);
+        dot[h] = a;
+      }
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+        for (int h = 0; h < G; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o2);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        if (head >= 0 && head != h) continue;
+        const float mn = fmaxf(m[h], dot[h]);
+        const float scale = exp2f(m[h] - mn);
+        const float p = exp2f(dot[h] - mn);
+        l[h] = l[h] * scale + p;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[h][e] = fmaf(o[h][e], scale, p * vf[e]);
+        m[h] = mn;
+      }
+    }
+    mark(M_ATTN_ITEMS);
+    // warps -> CTA partial per head
+    float *ao = reinterpret_cast<float *>(S.big);   // [FW][G][D]
+    float *am = ao + FW * G * D;                     // [G][FW]
+    float *al = am + G * FW;                         // [G][FW]
+    float *part = reinterpret_cast<float *>(S.big + 72 * 1024);  // [G][PART]: m, l, -, -, o[D]
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      if (lane == 0) { am[h * FW + warp] = m[h]; al[h * FW + warp] = l[h]; }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ao[(warp * G + h) * D + 8 * lane + e] = o[h][e];
+    }
+    __syncthreads();
+    {
+      const int h = tid >> 7, d2 = (tid & 127) * 2;
+      float M = -INFINITY;
+      for (int k = 0; k < FW; ++k) M = fmaxf(M, am[h * FW + k]);
+      float L = 0.0f, O0 = 0.0f, O1 = 0.0f;
+      if (M != -INFINITY)
+        for (int k = 0; k < FW; ++k) {
+          const float mk = am[h * FW + k];
+          if (mk == -INFINITY) continue;
+          const float e = exp2f(mk - M);
+          L += al[h * FW + k] * e;
+          O0 += ao[(k * G + h) * D + d2] * e;
+          O1 += ao[(k * G + h) * D + d2 + 1] * e;
+        }
+      part[h * PART + 4 + d2] = O0;
+      part[h * PART + 4 + d2 + 1] = O1;
+      if ((tid & 127) == 0) { part[h * PART] = M; part[h * PART + 1] = L; }
+    }
+    cluster_sync();
+    mark(M_ATTN_CTA);
+    // CTA `rank` finishes output dimensions [16 rank, 16 rank + 16) of the four heads
+    if (tid < G * 16) {
+      const int h = tid >> 4, d = 16 * rank + (tid & 15);
+      // online log-sum-exp merge of the 16 CTA partials (log2 domain)
+      float M = -INFINITY, L = 0.0f, O = 0.0f;
+#pragma unroll 4
+      for (int r = 0; r < CL; ++r) {
+        const float mr = ld_remote_f(remote(part + h * PART, (uint32_t)r));
+        const float lr = ld_remote_f(remote(part + h * PART + 1, (uint32_t)r));
+        const float orr = ld_remote_f(remote(part + h * PART + 4 + d, (uint32_t)r));
+        if (mr == -INFINITY) continue;
+        if (mr > M) {
+          const float e = exp2f(M - mr);
+          L = L * e + lr;
+          O = O * e + orr;
+          M = mr;
+        } else {
+          const float e = exp2f(mr - M);
+          L += lr * e;
+          O += orr * e;
+        }
+      }
+      w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
+    }
+  }
+  mark(M_ATTN);
+  if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
+  cluster_sync();  // no CTA leaves while its shared memory may still be read
+}
+
+const char *const kMarkNames[M_NTAGS] = {
+    "start", "issue", "qprep_exponents", "qprep", "cluster_start", "slice_landed", "coarse",
+    "select_histogram", "select_barrier", "select_readback", "coarse_select", "survivors",
+    "fine_gather", "fine", "fine_select", "selected_list", "selected_exchange", "pool_keep", "pool",
+    "s15_gather", "s15_score", "s15_select", "u15_union", "s16_score", "s16_select", "candidates",
+    "s2_score", "s2_select", "attn_items", "attn_cta", "attention"};
+
+}  // namespace
+
+bool fused_supported(const Work &w) {
+  return w.nc % 32 == 0 && w.nc <= CL * PER_MAX && w.cap <= CL * POS_MAX && w.cap % 32 == 0;
+}
+
+cudaError_t prepare_fused_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(k_funnel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_funnel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
+cudaError_t launch_fused(const Work &w, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL, w.n_cells, 1);
+  cfg.blockDim = dim3(FT, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_funnel, w);
+}
+
+const char *fused_mark_name(int tag) { return (tag >= 0 && tag < M_NTAGS) ? kMarkNames[tag] : ""; }
+
+}  // namespace skv

@@ -13,9 +13,9 @@ pytestmark = pytest.mark.gpu
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
 
 
-def _engine(n_slots, context, nc, capacity=13056, sink=128, local=256):
+def _engine(n_slots, context, nc, capacity=13056, sink=128, local=256, staged=None):
     return _native.Engine(n_slots=n_slots, context=context, sink=sink, local=local, nc=nc,
-                          capacity=capacity, device=0)
+                          capacity=capacity, device=0, staged=staged)
 
 
 def _upload_kv(eng, slot, k, v):
@@ -40,10 +40,11 @@ def gold():
     return Golden()
 
 
-def test_reference_built_index(gold, cuda):
+@pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
+def test_reference_built_index(gold, cuda, staged):
     """Engine on the index the reference itself built: ids equal the pinned oracle."""
     views = gold.views()
-    eng = _engine(1, gold.context, views[0]["nc"])
+    eng = _engine(1, gold.context, views[0]["nc"], staged=staged)
     try:
         eng.upload_index(0, views)
         _upload_kv(eng, 0, gold.k, gold.v)
@@ -98,11 +99,12 @@ def test_fp8_conversion_edge_values(cuda):
         eng.close()
 
 
-def test_batched_slots_match_single(cuda):
-    """Three independent caches in one engine (one launch per stage) vs the oracle."""
+@pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
+def test_batched_slots_match_single(cuda, staged):
+    """Three independent caches in one engine (one launch per step or stage) vs the oracle."""
     cases = [Case(context=8192, nprobe=128, seed=s) for s in (21, 22, 23)]
     nc = cases[0].index.cells()[0]["centroids"].shape[0]
-    eng = _engine(3, 8192, nc)
+    eng = _engine(3, 8192, nc, staged=staged)
     try:
         for s, c in enumerate(cases):
             eng.upload_index(s, [device_view(x) for x in c.index.cells()])
@@ -117,11 +119,12 @@ def test_batched_slots_match_single(cuda):
         eng.close()
 
 
-def test_capacity_overflow_is_reported(cuda):
+@pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
+def test_capacity_overflow_is_reported(cuda, staged):
     """A pool above the configured capacity sets the status word; sync raises."""
     case = Case(context=8192, nprobe=128, seed=11)
     nc = case.index.cells()[0]["centroids"].shape[0]
-    eng = _engine(1, 8192, nc, capacity=2048)
+    eng = _engine(1, 8192, nc, capacity=2048, staged=staged)
     try:
         eng.upload_index(0, [device_view(c) for c in case.index.cells()])
         _upload_kv(eng, 0, case.k, case.v)

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from oracle import oracle as O
-from seoulkv_b200 import SeoulKV4, SeoulKV4Config
+from seoulkv_b200 import SeoulKV4, SeoulKV4Config, _native
 from tests.helpers import Case, bits
 
 pytestmark = pytest.mark.gpu
@@ -17,6 +17,13 @@ MAX_ABS, MEAN_ABS = 2e-2, 2e-3
 @pytest.fixture(scope="module")
 def case():
     return Case(context=8192, nprobe=128, seed=11)
+
+
+@pytest.fixture(params=["fused", "staged"])
+def path(request, monkeypatch):
+    """Both device paths: the single cluster kernel and the 14 staged kernels."""
+    monkeypatch.setattr(_native, "FORCE_STAGED", request.param == "staged")
+    return request.param
 
 
 def _compare(eng, res, nc, capacity):
@@ -47,9 +54,11 @@ def _compare(eng, res, nc, capacity):
         assert counts[g, 5] == 0, f"cell {g}: status"
 
 
-def test_funnel_parity_and_output(case, cuda):
+def test_funnel_parity_and_output(case, cuda, path):
     cfg = SeoulKV4Config(debug=True)
     with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
+        attn.run(case.query(100))
+        assert attn._engine.fused == (path == "fused")
         for qseed in (101, 102, 103):
             q = case.query(qseed)
             y = attn.run(q).to_torch()
@@ -65,7 +74,7 @@ def test_funnel_parity_and_output(case, cuda):
             assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
 
 
-def test_device_query_and_replay(case, cuda):
+def test_device_query_and_replay(case, cuda, path):
     q = case.query(201)
     with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
         a = attn.run(q).to_torch()
