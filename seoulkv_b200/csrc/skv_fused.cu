@@ -178,14 +178,16 @@ __device__ __forceinline__ uint32_t remote(const void *p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
   return r;
 }
+// Remote loads carry no "memory" clobber, so that several can be in flight;
+// the cluster barriers (which do) keep them after the writes they read.
 __device__ __forceinline__ uint32_t ld_remote(uint32_t a) {
   uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
 }
 __device__ __forceinline__ float ld_remote_f(uint32_t a) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
 __device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
@@ -318,6 +320,44 @@ __device__ __forceinline__ uint32_t select_key(const FusedSmem &S, int kind, int
   }
 }
 
+// One radix-histogram pass over this CTA's keys of `KIND`: keys with
+// (key & mk[h]) == pf[h] add one to bin h*256 + digit (bits sh..sh+7).
+// Run-length counting: a thread counts its current bin per head in a
+// register and adds it when the bin changes and at the end (the warp's lanes
+// on lane 0's bin in one atomic); selection keys crowd into few bins, where
+// per-key shared atomics from all warps serialise.
+template <int KIND>
+__device__ __forceinline__ void hist_pass(FusedSmem &S, int nloc, int q0, const uint32_t (&pf)[4],
+                                          const uint32_t (&mk)[4], int sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t cur[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu}, run[4] = {0u, 0u, 0u, 0u};
+#pragma unroll 1
+  for (int i = tid; i < nloc; i += FT) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint32_t v = select_key(S, KIND, h, i, q0);
+      if ((v & mk[h]) != pf[h]) continue;
+      const uint32_t bin = h * 256 + ((v >> sh) & 255u);
+      if (bin != cur[h]) {
+        if (run[h]) atomicAdd(&S.hist[cur[h]], run[h]);
+        cur[h] = bin;
+        run[h] = 0u;
+      }
+      ++run[h];
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const uint32_t b0 = __shfl_sync(0xffffffffu, cur[h], 0);
+    const uint32_t tot0 = __reduce_add_sync(0xffffffffu, cur[h] == b0 ? run[h] : 0u);
+    if (lane == 0) {
+      if (b0 != 0xffffffffu && tot0) atomicAdd(&S.hist[b0], tot0);
+    } else if (cur[h] != b0 && run[h]) {
+      atomicAdd(&S.hist[cur[h]], run[h]);
+    }
+  }
+}
+
 // K-th largest of the cluster's keys (select_key of `kind`) for each of
 // the four heads; the top `nbits` bits of the 32-bit keys are significant.  On return S.ctl.th[h] holds, per head:
 //   exact:  the K-th largest key (all nbits resolved);
@@ -351,36 +391,11 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
       pf[h] = live ? S.ctl.prefix[h] : 1u;
       mk[h] = live ? S.ctl.mask[h] : 0u;
     }
-    // run-length counting: a thread counts its current bin per head in a
-    // register and adds it when the bin changes and at the end (the warp's
-    // lanes on lane 0's bin in one atomic); selection keys crowd into few
-    // bins, where per-key shared atomics from all warps serialise
-    uint32_t cur[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu}, run[4] = {0u, 0u, 0u, 0u};
-#pragma unroll 1
-    for (int i = tid; i < nloc; i += FT) {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const uint32_t v = select_key(S, kind, h, i, q0);
-        if ((v & mk[h]) != pf[h]) continue;
-        const uint32_t bin = h * 256 + ((v >> sh) & 255u);
-        if (bin != cur[h]) {
-          if (run[h]) atomicAdd(&S.hist[cur[h]], run[h]);
-          cur[h] = bin;
-          run[h] = 0u;
-        }
-        ++run[h];
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const uint32_t b0 = __shfl_sync(0xffffffffu, cur[h], 0);
-      const uint32_t on0 = cur[h] == b0 ? run[h] : 0u;
-      const uint32_t tot0 = __reduce_add_sync(0xffffffffu, on0);
-      if (lane == 0) {
-        if (b0 != 0xffffffffu && tot0) atomicAdd(&S.hist[b0], tot0);
-      } else if (cur[h] != b0 && run[h]) {
-        atomicAdd(&S.hist[cur[h]], run[h]);
-      }
+    switch (kind) {
+      case KEY_COARSE: hist_pass<KEY_COARSE>(S, nloc, q0, pf, mk, sh); break;
+      case KEY_FINE: hist_pass<KEY_FINE>(S, nloc, q0, pf, mk, sh); break;
+      case KEY_S15: hist_pass<KEY_S15>(S, nloc, q0, pf, mk, sh); break;
+      default: hist_pass<KEY_S16>(S, nloc, q0, pf, mk, sh); break;
     }
     if (tid < 64) S.red[nbuf][tid] = 0;
     __syncthreads();
@@ -391,7 +406,13 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     }
     cluster_sync();
     mark(M_SYNC);
-    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = ld_remote(remote(&S.red[buf][e & 63], (uint32_t)(e >> 6)));
+    {
+      static_assert(4 * 256 == 2 * FT, "two reduced bins per thread");
+      const uint32_t a = ld_remote(remote(&S.red[buf][tid & 63], (uint32_t)(tid >> 6)));
+      const uint32_t b = ld_remote(remote(&S.red[buf][(tid + FT) & 63], (uint32_t)((tid + FT) >> 6)));
+      S.hist[tid] = a;
+      S.hist[tid + FT] = b;
+    }
     __syncthreads();
     if (warp < 4 && !S.ctl.done[warp]) {
       const int h = warp;
@@ -532,14 +553,38 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   mark(M_START);
 
   // ---------------------------------------------------------------- P0
-  // the small inputs first, so that they do not queue behind the slice
-  for (int i = tid; i < 4 * D; i += FT) S.sx[i] = bf16f(w.q[((size_t)slot * 16 + g * 4) * D + i]);
-  for (int i = tid; i < D; i += FT) S.kscale[i] = c.key_scale[i];
-  for (int i = tid; i < nrows; i += FT) S.resid[i] = c.resid[r0 + i];
-  for (int i = tid; i <= nrows; i += FT) S.offs[i] = c.offsets[r0 + i];
-  for (int i = tid; i < (nrows >> 5); i += FT) {
-    S.scale4[i] = c.coarse_scale4[(r0 >> 5) + i];
-    S.fscale[i] = c.fine_scale[(r0 >> 5) + i];
+  // the small inputs first, so that they do not queue behind the slice; all
+  // loads are issued before any shared-memory store (the stores could alias
+  // the generic source pointers and would otherwise serialise the loads)
+  {
+    static_assert(PER_MAX == 4 * FT && 4 * D == 2 * FT && PER_MAX / 32 <= FT && D <= FT, "load shapes");
+    const uint16_t *qsrc = w.q + ((size_t)slot * 16 + g * 4) * D;
+    uint16_t qv[2], rv[4];
+    int ov[5];
+    float ks = 0.0f, s4 = 0.0f, fs = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) qv[k] = qsrc[tid + k * FT];
+    if (tid < D) ks = c.key_scale[tid];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rv[k] = tid + k * FT < nrows ? c.resid[r0 + tid + k * FT] : (uint16_t)0;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) ov[k] = tid + k * FT <= nrows ? c.offsets[r0 + tid + k * FT] : 0;
+    if (tid < (nrows >> 5)) {
+      s4 = c.coarse_scale4[(r0 >> 5) + tid];
+      fs = c.fine_scale[(r0 >> 5) + tid];
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) S.sx[tid + k * FT] = bf16f(qv[k]);
+    if (tid < D) S.kscale[tid] = ks;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) S.resid[tid + k * FT] = rv[k];
+#pragma unroll
+    for (int k = 0; k < 5; ++k)
+      if (tid + k * FT <= PER_MAX) S.offs[tid + k * FT] = ov[k];
+    if (tid < PER_MAX / 32) {
+      S.scale4[tid] = s4;
+      S.fscale[tid] = fs;
+    }
   }
   for (int i = tid; i < 3 * 64; i += FT) (&S.red[0][0])[i] = 0;
   if (tid == 0) {
@@ -918,7 +963,13 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   const int pc = ((n15 + CL * 32 - 1) / (CL * 32)) * 32;
   const int q0 = min(n15, rank * pc), m15 = min(n15, q0 + pc) - q0;
   {
-    for (int i = tid; i < m15; i += FT) S.b.p.tok[i] = __ldcg(w.pool + (size_t)cell * cap + q0 + i);
+    {
+      static_assert(POS_MAX == 2 * FT, "two pool positions per thread");
+      const int32_t *src = w.pool + (size_t)cell * cap + q0;
+      const int t0v = tid < m15 ? __ldcg(src + tid) : 0, t1v = tid + FT < m15 ? __ldcg(src + tid + FT) : 0;
+      if (tid < m15) S.b.p.tok[tid] = t0v;
+      if (tid + FT < m15) S.b.p.tok[tid + FT] = t1v;
+    }
     __syncthreads();
     for (int b0 = 0; b0 < m15; b0 += BATCH_S2) {
       const int nb = min(BATCH_S2, m15 - b0);
@@ -1257,24 +1308,25 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     // CTA `rank` finishes output dimensions [16 rank, 16 rank + 16) of the four heads
     if (tid < G * 16) {
       const int h = tid >> 4, d = 16 * rank + (tid & 15);
-      // online log-sum-exp merge of the 16 CTA partials (log2 domain)
-      float M = -INFINITY, L = 0.0f, O = 0.0f;
-#pragma unroll 4
+      // the 16 CTA partials, all loads in flight at once, then the
+      // log-sum-exp merge (log2 domain)
+      float ms[CL], ls[CL], os[CL];
+#pragma unroll
       for (int r = 0; r < CL; ++r) {
-        const float mr = ld_remote_f(remote(part + h * PART, (uint32_t)r));
-        const float lr = ld_remote_f(remote(part + h * PART + 1, (uint32_t)r));
-        const float orr = ld_remote_f(remote(part + h * PART + 4 + d, (uint32_t)r));
-        if (mr == -INFINITY) continue;
-        if (mr > M) {
-          const float e = exp2f(M - mr);
-          L = L * e + lr;
-          O = O * e + orr;
-          M = mr;
-        } else {
-          const float e = exp2f(mr - M);
-          L += lr * e;
-          O += orr * e;
-        }
+        ms[r] = ld_remote_f(remote(part + h * PART, (uint32_t)r));
+        ls[r] = ld_remote_f(remote(part + h * PART + 1, (uint32_t)r));
+        os[r] = ld_remote_f(remote(part + h * PART + 4 + d, (uint32_t)r));
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < CL; ++r) M = fmaxf(M, ms[r]);
+      float L = 0.0f, O = 0.0f;
+#pragma unroll
+      for (int r = 0; r < CL; ++r) {
+        if (ms[r] == -INFINITY) continue;
+        const float e = exp2f(ms[r] - M);
+        L += ls[r] * e;
+        O += os[r] * e;
       }
       w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
     }
