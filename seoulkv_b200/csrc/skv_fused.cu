@@ -21,7 +21,8 @@
 //   P8  top-1600 per head, ascending union (cluster scan)
 //   P9  Stage-1.6 scores of this CTA's union members
 //   P10 top-256 per head, candidates (cluster scan)
-//   P11 Stage-II scores of this CTA's candidates
+//   P11 Stage-II scores of this CTA's candidates (small gather), pushed to
+//       CTA h for head h
 //   P12 exact top-100 per head (CTA h of the cluster), rank order
 //   P13 attention: sink + local + top-100 partials per CTA, combined across
 //       the cluster through distributed shared memory
@@ -97,7 +98,7 @@ struct FusedSmem {
     uint32_t fkey[4][PER_MAX];                                        // P4-P5
     struct { uint16_t slist[PER_MAX]; int soff[PER_MAX]; int ppre[PER_MAX + 1]; } s;  // P5-P6
     struct {
-      uint16_t sc15[4][POS_MAX], sc16[4][POS_MAX], sc2[4][POS_MAX];   // ordered BF16 scores
+      uint16_t sc15[4][POS_MAX], sc16[4][POS_MAX];   // ordered BF16 scores
       int tok[POS_MAX];
       uint16_t urank[POS_MAX];     // rank among this CTA's union members
       uint16_t clist[POS_MAX];     // candidates (local positions)
@@ -954,11 +955,11 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   mark(M_POOL);
 
   // ---------------------------------------------------------------- P7
-  // Stage-1.5, 1.6 and II scores of a balanced share of the pool positions,
-  // from one gather of their prefix2 | residual2 | residual4 rows.  The 1.6
-  // and II selections break ties by the lower union (candidate) position,
-  // which orders members like their pool position does, so their keys can
-  // carry the pool position and need no second gather.
+  // Stage-1.5 and 1.6 scores of a balanced share of the pool positions,
+  // from one gather of their prefix2 | residual2 rows.  The 1.6 selection
+  // breaks ties by the lower union position, which orders members like
+  // their pool position does, so its keys carry the pool position and the
+  // rows need no second gather.
   const int n15 = min(npool, cap);
   const int pc = ((n15 + CL * 32 - 1) / (CL * 32)) * 32;
   const int q0 = min(n15, rank * pc), m15 = min(n15, q0 + pc) - q0;
@@ -971,16 +972,13 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       if (tid + FT < m15) S.b.p.tok[tid + FT] = t1v;
     }
     __syncthreads();
-    for (int b0 = 0; b0 < m15; b0 += BATCH_S2) {
-      const int nb = min(BATCH_S2, m15 - b0);
+    for (int b0 = 0; b0 < m15; b0 += BATCH_FINE) {
+      const int nb = min(BATCH_FINE, m15 - b0);
       __syncthreads();
-      for (int q = tid; q < nb * 16; q += FT) {
-        const int rr = q >> 4, part = q & 15;
+      for (int q = tid; q < nb * 8; q += FT) {
+        const int rr = q >> 3, part = q & 7;
         const int tok = S.b.p.tok[b0 + rr];
-        const uint8_t *src = part < 4   ? c.prefix2 + (size_t)tok * 64 + part * 16
-                             : part < 8 ? c.residual2 + (size_t)tok * 64 + (part - 4) * 16
-                                        : c.residual4 + (size_t)tok * 128 + (part - 8) * 16;
-        cp16(S.big + rr * STRIDE_S2 + part * 16, src);
+        cp16(S.big + rr * STRIDE_FINE + part * 16, (part < 4 ? c.prefix2 : c.residual2) + (size_t)tok * 64 + (part & 3) * 16);
       }
       cp_wait_all();
       __syncthreads();
@@ -993,7 +991,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         for (int tile = warp; tile < tiles; tile += FW) {
           const int rg = tile * 16 + gq, r8 = rg + 8;
           long long dsum[2];
-          tile_dots<0>(S.big + min(rg, nb - 1) * STRIDE_S2, S.big + min(r8, nb - 1) * STRIDE_S2, t, F, dsum);
+          tile_dots<0>(S.big + min(rg, nb - 1) * STRIDE_FINE, S.big + min(r8, nb - 1) * STRIDE_FINE, t, F, dsum);
           dsum[0] = 2 * dsum[0] - 3 * S.sxsum[R_Q15][hA];  // weights 2p - 3
           dsum[1] = 2 * dsum[1] - 3 * S.sxsum[R_Q15][hB];
           const int row = (t & 1) ? r8 : rg;
@@ -1008,23 +1006,18 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         BFrag F;
         load_frag(S, R_QS, lane, F);
         const double s16A = pow2d(S.shift[R_QS][hA] + 4), s16B = pow2d(S.shift[R_QS][hB] + 4);
-        const double s2A = pow2d(S.shift[R_QS][hA]), s2B = pow2d(S.shift[R_QS][hB]);
         for (int tile = warp; tile < tiles; tile += FW) {
           const int rg = tile * 16 + gq, r8 = rg + 8;
-          long long dh[2], dl[2];
-          tile_dots_8bit(S.big + min(rg, nb - 1) * STRIDE_S2, S.big + min(r8, nb - 1) * STRIDE_S2, t, F, dh, dl);
+          long long dh[2];
+          tile_dots<1>(S.big + min(rg, nb - 1) * STRIDE_FINE, S.big + min(r8, nb - 1) * STRIDE_FINE, t, F, dh);
           const int row = (t & 1) ? r8 : rg;
           if (row < nb) {
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
               const int h = k ? hB : hA;
-              const long long sx = S.sxsum[R_QS][h];
               // operand 16*qs, weights 2*c4 - 15: the same digits, scale 2^4 higher
-              S.b.p.sc16[h][b0 + row] =
-                  (uint16_t)ord16(bf16_rne(exact_to_float(2 * dh[k] - 15 * sx, k ? s16B : s16A)));
-              // weights 2*code8 - 255 = 16*(2*c4 - 15) + (2*r4 - 15)
-              S.b.p.sc2[h][b0 + row] =
-                  (uint16_t)ord16(bf16_rne(exact_to_float(32 * dh[k] + 2 * dl[k] - 255 * sx, k ? s2B : s2A)));
+              S.b.p.sc16[h][b0 + row] = (uint16_t)ord16(
+                  bf16_rne(exact_to_float(2 * dh[k] - 15 * S.sxsum[R_QS][h], k ? s16B : s16A)));
             }
           }
         }
@@ -1112,23 +1105,55 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   exchange(S, P_CAND, ncl, 0, 0, 0);
   const int c_base = before(S, 0, rank), ncand = min(total(S, 0), CAND_MAX);
   if (rank == 0 && tid == 0) counts[C_CAND] = ncand;
-  // candidates: their union position, and their Stage-II key and token for
-  // each head pushed to CTA h (slot = candidate rank)
+  // candidates: their union position; their Stage-II keys (8-bit scores of
+  // a small gather) and tokens for head h are pushed to CTA h (slot =
+  // candidate rank), into the Stage-1.5 score area, which is dead by now
+  uint32_t *k2 = reinterpret_cast<uint32_t *>(&S.b.p.sc15[0][0]);
+  int *t2 = reinterpret_cast<int *>(&S.b.p.sc15[0][0]) + CAND_MAX;
   for (int k = tid; k < ncl; k += FT) {
     const int cr = c_base + k;
     if (cr >= CAND_MAX) break;
     const int i = S.b.p.clist[k];
-    const uint32_t u = (uint32_t)(u_base + S.b.p.urank[i]);
-    w.cand[(size_t)cell * CAND_MAX + cr] = (int)u;
-    const int tok = S.b.p.tok[i];
-    prefetch_l2_bulk(c.kv8 + (size_t)tok * REC, REC);  // for attention should it win
-    uint32_t *k2 = reinterpret_cast<uint32_t *>(S.big);
-    int *t2 = reinterpret_cast<int *>(S.big) + CAND_MAX;
+    w.cand[(size_t)cell * CAND_MAX + cr] = u_base + S.b.p.urank[i];
+    prefetch_l2_bulk(c.kv8 + (size_t)S.b.p.tok[i] * REC, REC);  // for attention should it win
+  }
+  {
+    BFrag F;
+    load_frag(S, R_QS, lane, F);
+    const double s2A = pow2d(S.shift[R_QS][hA]), s2B = pow2d(S.shift[R_QS][hB]);
+    for (int b0 = 0; b0 < ncl; b0 += BATCH_S2) {
+      const int nb = min(BATCH_S2, ncl - b0);
+      __syncthreads();
+      for (int q = tid; q < nb * 16; q += FT) {
+        const int rr = q >> 4, part = q & 15;
+        const int tok = S.b.p.tok[S.b.p.clist[b0 + rr]];
+        const uint8_t *src = part < 4   ? c.prefix2 + (size_t)tok * 64 + part * 16
+                             : part < 8 ? c.residual2 + (size_t)tok * 64 + (part - 4) * 16
+                                        : c.residual4 + (size_t)tok * 128 + (part - 8) * 16;
+        cp16(S.big + rr * STRIDE_S2 + part * 16, src);
+      }
+      cp_wait_all();
+      __syncthreads();
+      const int tiles = (nb + 15) >> 4;
+      for (int tile = warp; tile < tiles; tile += FW) {
+        const int rg = tile * 16 + gq, r8 = rg + 8;
+        long long dh[2], dl[2];
+        tile_dots_8bit(S.big + min(rg, nb - 1) * STRIDE_S2, S.big + min(r8, nb - 1) * STRIDE_S2, t, F, dh, dl);
+        const int row = (t & 1) ? r8 : rg, cr = c_base + b0 + row;
+        if (row < nb && cr < CAND_MAX) {
+          const int i = S.b.p.clist[b0 + row];
+          const uint32_t u = (uint32_t)(u_base + S.b.p.urank[i]);
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const uint32_t key = ((uint32_t)S.b.p.sc2[h][i] << 16) | (0xffffu - u);
-      st_remote(remote(k2 + cr, (uint32_t)h), key);
-      st_remote(remote(t2 + cr, (uint32_t)h), (uint32_t)tok);
+          for (int k = 0; k < 2; ++k) {
+            const int h = k ? hB : hA;
+            // weights 2*code8 - 255 = 16*(2*c4 - 15) + (2*r4 - 15)
+            const long long dsum = 32 * dh[k] + 2 * dl[k] - 255 * S.sxsum[R_QS][h];
+            const uint32_t key = (ord16(bf16_rne(exact_to_float(dsum, k ? s2B : s2A))) << 16) | (0xffffu - u);
+            st_remote(remote(k2 + cr, (uint32_t)h), key);
+            st_remote(remote(t2 + cr, (uint32_t)h), (uint32_t)S.b.p.tok[i]);
+          }
+        }
+      }
     }
   }
   cluster_sync();  // Stage-II keys of all candidates are in CTAs 0-3
@@ -1139,10 +1164,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     // exact top-100 of head h in rank order: block radix select over the
     // (at most 1024) candidate keys held two per thread, then ranks
     const int h = rank;
-    const uint32_t *k2 = reinterpret_cast<const uint32_t *>(S.big);
-    const int *t2 = reinterpret_cast<const int *>(S.big) + CAND_MAX;
-    uint32_t *wkey = reinterpret_cast<uint32_t *>(S.big + 8 * CAND_MAX);
-    int *widx = reinterpret_cast<int *>(S.big + 8 * CAND_MAX) + TOPK;
+    uint32_t *wkey = reinterpret_cast<uint32_t *>(S.big);
+    int *widx = reinterpret_cast<int *>(S.big) + TOPK;
     const uint32_t v[2] = {tid < ncand ? k2[tid] : 0u, tid + FT < ncand ? k2[tid + FT] : 0u};
     const uint32_t K = (uint32_t)min(TOPK, ncand);
     uint32_t prefix = 0, mask = 0, krem = K;
