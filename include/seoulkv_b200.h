@@ -140,6 +140,7 @@ int skv_debug_ids(void *handle, int32_t *out);
 #define SKV_STAGE_RESIDUAL4 11  /* uint8 [4][T][128] key codes & 15            */
 #define SKV_STAGE_KV8 12        /* uint8 [4][T][512] FP8-e4m3 [K | V] records  */
 #define SKV_STAGE_KEY_SCALE 13  /* float [4][256] per-dimension max |k|        */
+#define SKV_STAGE_FINAL_KEYS 14 /* uint32 [4][4][100] Stage-II keys of the ranks (0: none) */
 int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
                    size_t *written);
 
@@ -170,6 +171,38 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
                        int32_t *n_marks);
 /* Name of a phase mark tag (static string). */
 const char *skv_phase_name(int32_t tag);
+
+/* Sequence-sharded decode -- no counterpart in the reference (its decode is
+ * single-device).  A long context is split into contiguous token ranges,
+ * one engine per GPU (sink zone on the first shard, local window on the
+ * last, sink = local = 0 on the others); after skv_run each shard's local
+ * top-100 per head is merged into the same global top-100 on every GPU,
+ * every shard attends over the winners it owns plus its dense zones, and the
+ * shards' partials are combined.  The host moves the lists and partials
+ * between GPUs (an all-gather each); every pointer below is device memory
+ * and every call is ordered on `stream`.
+ *
+ * skv_shard_outputs: this engine's per-rank Stage-II keys and shard-local
+ *   token ids of slot `slot`, [4][4][100] each (key 0: rank unused).  Valid
+ *   after the step that wrote them completes; overwritten by the next run. */
+int skv_shard_outputs(void *handle, int32_t slot, const uint32_t **keys, const int32_t **ids);
+/* Exact global top-100 per (cell, head): candidates ordered by Stage-II score
+ * (descending), then local rank, then global token id (ascending).
+ *   keys, ids  [n_shards][n_cells][4][100] as skv_shard_outputs gives them
+ *   begin      [n_shards] first global token of each shard
+ *   out_gids   [n_cells][4][100] global token ids, -1 past the winners
+ * n_shards <= 10. */
+int skv_shard_merge(const uint32_t *keys, const int32_t *ids, const int32_t *begin, int32_t n_shards,
+                    int32_t n_cells, int32_t *out_gids, void *stream);
+/* This shard's partial attention for every cell of the engine over its
+ * dense zones and the winners of `gids` ([n_cells][4][100] global ids) in
+ * [token_begin, token_begin + context): partials [n_cells][4][260] floats =
+ * (m, l, 0, 0, o[256]) with scores in the log2 domain, o not normalised.
+ * Uses the query of the last skv_bind_query. */
+int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, float *partials, void *stream);
+/* Log-sum-exp combine: partials [n_shards][n_cells][4][260] -> out BF16
+ * [n_cells / 4][16][256]. */
+int skv_shard_combine(const float *partials, int32_t n_shards, int32_t n_cells, uint16_t *out, void *stream);
 
 /* Sparse attention that allocates nothing -- no counterpart in the reference.
  *

@@ -295,3 +295,90 @@ def attention(q_bits: np.ndarray, k8: np.ndarray, v8: np.ndarray, keys: np.ndarr
     p = np.exp(s)
     o = (p[:, None] * v8[keys]).sum(axis=0) / p.sum()
     return bf16_bits(o.astype(np.float32))
+
+
+# ------------------------------------------------------ sequence sharding
+#
+# The reference decodes on one device; the sharded mode of this project has
+# no reference counterpart, so its oracle is the single-device funnel above
+# run per shard, plus the merge rule and the attention over the union, in
+# plain Python/numpy.
+
+def ord16(bits) -> np.ndarray:
+    """Total order of BF16 bit patterns as unsigned 16-bit keys."""
+    b = np.asarray(bits, dtype=np.uint32)
+    return np.where(b & 0x8000, b ^ 0xFFFF, b ^ 0x8000).astype(np.uint32)
+
+
+def stage2_rank_keys(res: dict) -> np.ndarray:
+    """Stage-II keys [ordered score | 0xffff - u] of the 100 ranks per query head (0: no rank).
+
+    ``res`` is one ``run_cell`` result; uint32 [4, 100].
+    """
+    keys = np.zeros((G, TOPK), np.uint32)
+    where = {int(u): c for c, u in enumerate(res["cand"])}
+    for h in range(G):
+        for r in range(TOPK):
+            u = int(res["final_pos"][h][r])
+            if u < 0:
+                continue
+            score = int(res["s2_scores"][h][where[u]])
+            keys[h, r] = (int(ord16(score)) << 16) | (0xFFFF - u)
+    return keys
+
+
+def merge_shards(keys: np.ndarray, ids: np.ndarray, begin) -> np.ndarray:
+    """Global top-100 per (cell, head) from every shard's ranks.
+
+    ``keys``/``ids`` [n_shards, 4, 4, 100] (shard-local ids), ``begin``
+    [n_shards]; candidates ordered by ordered score descending, then local
+    rank, then global token id ascending.  Returns int32 [4, 4, 100], -1 past
+    the winners.
+    """
+    n = keys.shape[0]
+    out = np.full((G, G, TOPK), -1, np.int32)
+    for g in range(G):
+        for h in range(G):
+            cand = []
+            for s in range(n):
+                for r in range(TOPK):
+                    key = int(keys[s, g, h, r])
+                    if key:
+                        gid = int(begin[s]) + int(ids[s, g, h, r])
+                        cand.append((-(key >> 16), r, gid))
+            cand.sort()
+            for i, (_, _, gid) in enumerate(cand[:TOPK]):
+                out[g, h, i] = gid
+    return out
+
+
+def sharded_reference(shards: list, q_bits: np.ndarray):
+    """One sharded decode step on the CPU.
+
+    ``shards``: per shard a dict with ``cells`` (four CellInputs), ``begin``,
+    ``context``, ``sink``, ``local`` and the decoded FP8 ``k8``/``v8`` float64
+    [4, context, 256]; ``q_bits`` uint16 [16, 256].  Returns (global ids int32
+    [4, 4, 100], BF16 output bits [16, 256], per-shard run_cell results).
+    """
+    n = len(shards)
+    keys = np.zeros((n, G, G, TOPK), np.uint32)
+    ids = np.zeros((n, G, G, TOPK), np.int32)
+    results = []
+    for s, sh in enumerate(shards):
+        res = [run_cell(sh["cells"][g], q_bits[4 * g:4 * g + 4]) for g in range(G)]
+        results.append(res)
+        for g in range(G):
+            keys[s, g] = stage2_rank_keys(res[g])
+            ids[s, g] = res[g]["final_ids"]
+    begin = [sh["begin"] for sh in shards]
+    gids = merge_shards(keys, ids, begin)
+    total = shards[-1]["begin"] + shards[-1]["context"]
+    dense = list(range(shards[0]["sink"])) + list(range(total - shards[-1]["local"], total))
+    out = np.zeros((16, D), np.uint16)
+    for g in range(G):
+        kk = np.concatenate([sh["k8"][g] for sh in shards])
+        vv = np.concatenate([sh["v8"][g] for sh in shards])
+        for h in range(G):
+            sel = np.asarray(dense + [int(x) for x in gids[g, h] if x >= 0], dtype=np.int64)
+            out[4 * g + h] = attention(q_bits[4 * g + h], kk, vv, sel)
+    return gids, out, results

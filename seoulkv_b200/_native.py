@@ -20,13 +20,14 @@ SKV_STATUS_FINE_SHORT = 4
 SKV_E_CAPACITY = -3
 
 STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8,
-             prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13)
+             prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13, final_keys=14)
 
 EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
     "skv_upload_kv", "skv_bind_query", "skv_run", "skv_sync", "skv_status", "skv_output",
     "skv_debug_ids", "skv_read_stage", "skv_traffic", "skv_profile_step", "skv_kernel_name",
     "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name",
+    "skv_shard_outputs", "skv_shard_merge", "skv_shard_attention", "skv_shard_combine",
 )
 
 SKV_FLAG_STAGED = 1
@@ -114,6 +115,14 @@ def load() -> ctypes.CDLL:
                                            ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
         lib.skv_phase_name.restype = ctypes.c_char_p
         lib.skv_phase_name.argtypes = [ctypes.c_int32]
+        lib.skv_shard_outputs.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
+                                          ctypes.POINTER(ctypes.c_void_p)]
+        lib.skv_shard_merge.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+        lib.skv_shard_attention.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                            ctypes.c_void_p]
+        lib.skv_shard_combine.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                          ctypes.c_void_p]
         _lib = lib
         return lib
 
@@ -245,7 +254,31 @@ class Engine:
                                           128, ctypes.byref(n)), "skv_profile_phases")
         return [(self.lib.skv_phase_name(int(tags[i])).decode(), float(cyc[i])) for i in range(n.value)]
 
+    def shard_outputs(self, slot: int = 0) -> tuple[int, int]:
+        """Device addresses of this engine's Stage-II keys and shard-local ids [4][4][100]."""
+        k, i = ctypes.c_void_p(), ctypes.c_void_p()
+        check(self.lib.skv_shard_outputs(self.handle, slot, ctypes.byref(k), ctypes.byref(i)), "skv_shard_outputs")
+        return int(k.value), int(i.value)
+
+    def shard_attention(self, gids: int, token_begin: int, partials: int, stream: int = 0) -> None:
+        check(self.lib.skv_shard_attention(self.handle, ctypes.c_void_p(gids), token_begin,
+                                           ctypes.c_void_p(partials), ctypes.c_void_p(stream or None)),
+              "skv_shard_attention")
+
     def traffic(self) -> dict:
         t = SkvTraffic()
         check(self.lib.skv_traffic(self.handle, ctypes.byref(t)), "skv_traffic")
         return {n: getattr(t, n) for n, _ in SkvTraffic._fields_}
+
+
+def shard_merge(keys: int, ids: int, begin: int, n_shards: int, n_cells: int, out_gids: int, stream: int = 0) -> None:
+    """Exact global top-100 from every shard's lists (device addresses)."""
+    check(load().skv_shard_merge(ctypes.c_void_p(keys), ctypes.c_void_p(ids), ctypes.c_void_p(begin), n_shards,
+                                 n_cells, ctypes.c_void_p(out_gids), ctypes.c_void_p(stream or None)),
+          "skv_shard_merge")
+
+
+def shard_combine(partials: int, n_shards: int, n_cells: int, out: int, stream: int = 0) -> None:
+    """Log-sum-exp combine of every shard's partials into BF16 output (device addresses)."""
+    check(load().skv_shard_combine(ctypes.c_void_p(partials), n_shards, n_cells, ctypes.c_void_p(out),
+                                   ctypes.c_void_p(stream or None)), "skv_shard_combine")

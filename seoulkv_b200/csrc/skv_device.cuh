@@ -100,6 +100,7 @@ struct Work {
   uint32_t *k2;             // [cell][4][CAND_MAX] Stage-II keys
   int32_t *final_pos;       // [cell][4][TOPK]
   int32_t *final_ids;       // [cell][4][TOPK]
+  uint32_t *final_keys;     // [cell][4][TOPK] Stage-II keys [ordered bf16 score | 0xffff - u], 0 = none
   int32_t *counts;          // [cell][NCOUNT]
   float *attn_part;         // [cell][4][ATTN_SPLIT][PART]
   uint32_t *arrive;         // [cell] attention partitions finished (step)

@@ -15,6 +15,7 @@
 #include "skv_device.cuh"
 #include "skv_fused.cuh"
 #include "skv_kernels.cuh"
+#include "skv_shard.cuh"
 
 using namespace skv;
 
@@ -222,6 +223,7 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(dalloc(e, &w.k2, C * G * CAND_MAX));
   TRY(dalloc(e, &w.final_pos, C * G * TOPK));
   TRY(dalloc(e, &w.final_ids, C * G * TOPK));
+  TRY(dalloc(e, &w.final_keys, C * G * TOPK));
   TRY(dalloc(e, &w.counts, C * NCOUNT));
   TRY(dalloc(e, &w.attn_part, C * G * ATTN_SPLIT * PART));
   TRY(dalloc(e, &w.arrive, C));
@@ -524,6 +526,7 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
     case SKV_STAGE_U15: src = w.u15pos + c0 * U15_MAX; n = (size_t)G * U15_MAX * 4; break;
     case SKV_STAGE_CAND: src = w.cand + c0 * CAND_MAX; n = (size_t)G * CAND_MAX * 4; break;
     case SKV_STAGE_FINAL_POS: src = w.final_pos + c0 * G * TOPK; n = (size_t)G * G * TOPK * 4; break;
+    case SKV_STAGE_FINAL_KEYS: src = w.final_keys + c0 * G * TOPK; n = (size_t)G * G * TOPK * 4; break;
     case SKV_STAGE_LOHI: {
       // ordered keys back to BF16 patterns, [cell][lo/hi][head][nc]
       std::vector<uint16_t> lo(G * G * nc), hi(G * G * nc);
@@ -570,6 +573,60 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
   n = std::min(n, bytes);
   CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost));
   if (written) *written = n;
+  return SKV_OK;
+}
+
+// ------------------------------------------------------- sharded decode
+
+namespace {
+// Makes the device that owns `p` current (the shard kernels run where their data is).
+int use_device_of(const void *p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess || a.type != cudaMemoryTypeDevice)
+    return fail(SKV_E_INVALID, "expected a device pointer");
+  CK(cudaSetDevice(a.device));
+  return SKV_OK;
+}
+}  // namespace
+
+int skv_shard_outputs(void *handle, int32_t slot, const uint32_t **keys, const int32_t **ids) {
+  Engine *e = as_engine(handle);
+  if (!e || !keys || !ids) return fail(SKV_E_INVALID, "null engine or output");
+  if (slot < 0 || slot >= e->desc.n_slots) return fail(SKV_E_INVALID, "slot out of range");
+  *keys = e->work.final_keys + (size_t)slot * G * G * TOPK;
+  *ids = e->work.final_ids + (size_t)slot * G * G * TOPK;
+  return SKV_OK;
+}
+
+int skv_shard_merge(const uint32_t *keys, const int32_t *ids, const int32_t *begin, int32_t n_shards,
+                    int32_t n_cells, int32_t *out_gids, void *stream) {
+  if (!keys || !ids || !begin || !out_gids) return fail(SKV_E_INVALID, "null buffer");
+  if (n_shards < 1 || n_shards > shard_max_shards()) return fail(SKV_E_INVALID, "n_shards out of range");
+  if (n_cells < 1 || n_cells % G) return fail(SKV_E_INVALID, "n_cells must be a positive multiple of 4");
+  int rc = use_device_of(keys);
+  if (rc) return rc;
+  CK(launch_shard_merge(keys, ids, begin, n_shards, n_cells, out_gids, static_cast<cudaStream_t>(stream)));
+  return SKV_OK;
+}
+
+int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, float *partials, void *stream) {
+  Engine *e = as_engine(handle);
+  if (!e || !gids || !partials) return fail(SKV_E_INVALID, "null engine or buffer");
+  if (token_begin < 0) return fail(SKV_E_INVALID, "negative token_begin");
+  int rc = ready(e);
+  if (rc) return rc;
+  CK(cudaSetDevice(e->desc.device));
+  CK(launch_shard_attention(e->work, gids, token_begin, partials, static_cast<cudaStream_t>(stream)));
+  return SKV_OK;
+}
+
+int skv_shard_combine(const float *partials, int32_t n_shards, int32_t n_cells, uint16_t *out, void *stream) {
+  if (!partials || !out) return fail(SKV_E_INVALID, "null buffer");
+  if (n_shards < 1) return fail(SKV_E_INVALID, "n_shards out of range");
+  if (n_cells < 1 || n_cells % G) return fail(SKV_E_INVALID, "n_cells must be a positive multiple of 4");
+  int rc = use_device_of(partials);
+  if (rc) return rc;
+  CK(launch_shard_combine(partials, n_shards, n_cells, out, static_cast<cudaStream_t>(stream)));
   return SKV_OK;
 }
 

@@ -1205,16 +1205,19 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     const int m = min(S.n_win, TOPK);
     int32_t *fpos = w.final_pos + ((size_t)cell * G + h) * TOPK;
     int32_t *fids = w.final_ids + ((size_t)cell * G + h) * TOPK;
+    uint32_t *fkeys = w.final_keys + ((size_t)cell * G + h) * TOPK;
     if (tid < m) {
       const uint32_t key = wkey[tid];
       int rk = 0;
       for (int j = 0; j < m; ++j) rk += wkey[j] > key;
       fpos[rk] = (int)(0xffffu - (key & 0xffffu));
       fids[rk] = t2[widx[tid]];
+      fkeys[rk] = key;
     } else if (tid < TOPK) {
       // fewer than 100 candidates: a failed step the status word reports
       fpos[tid] = -1;
       fids[tid] = 0;
+      fkeys[tid] = 0u;
     }
   }
   cluster_sync();  // final ids complete in global memory

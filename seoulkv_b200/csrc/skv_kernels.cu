@@ -759,6 +759,7 @@ __global__ void __launch_bounds__(1024) k_s2_select(Work w) {
   const int m = min(s_n, TOPK);
   int32_t *fpos = w.final_pos + ((size_t)cell * G + h) * TOPK;
   int32_t *fids = w.final_ids + ((size_t)cell * G + h) * TOPK;
+  uint32_t *fkeys = w.final_keys + ((size_t)cell * G + h) * TOPK;
   if (tid < m) {
     const uint32_t key = s_win[tid];
     int rank = 0;
@@ -767,11 +768,13 @@ __global__ void __launch_bounds__(1024) k_s2_select(Work w) {
     const bool live = u < nu;
     fpos[rank] = live ? u : -1;
     fids[rank] = live ? w.u15tok[(size_t)cell * U15_MAX + u] : 0;
+    fkeys[rank] = live ? key : 0u;
   } else if (tid < TOPK) {
     // fewer than 100 candidates: a failed step that the status word reports;
     // keep the attention gather in bounds
     fpos[tid] = -1;
     fids[tid] = 0;
+    fkeys[tid] = 0u;
   }
 }
 

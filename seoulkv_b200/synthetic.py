@@ -53,6 +53,36 @@ def make_kv(context: int, *, seed: int, components: int = 256, chunk: int = 6553
     return k, v, mixes
 
 
+def make_kv_range(total: int, begin: int, end: int, *, seed: int, components: int = 256, block: int = 65536):
+    """K/V of tokens [begin, end) of a ``total``-token sequence, generated block by block.
+
+    Each ``block``-token block of each KV head draws its components, noise and
+    V from its own generator (seeded by seed, head and block), so any token
+    range of the same sequence can be produced on its own: a shard of a long
+    context generates only its slice and every shard agrees on the mixtures.
+    Returns (k, v, mixtures) like make_kv (a different sequence than make_kv
+    for the same seed).
+    """
+    if not 0 <= begin < end <= total:
+        raise ValueError("require 0 <= begin < end <= total")
+    gen = torch.Generator().manual_seed(int(seed))
+    mixes = [Mixture(components, gen) for _ in range(N_KV)]
+    n = end - begin
+    k = torch.empty(N_KV, n, DIM, dtype=torch.bfloat16)
+    v = torch.empty(N_KV, n, DIM, dtype=torch.bfloat16)
+    for h, mix in enumerate(mixes):
+        for b0 in range(begin - begin % block, end, block):
+            bg = torch.Generator().manual_seed(int(seed) * 1_000_003 + h * 100_003 + b0 // block)
+            b1 = min(total, b0 + block)
+            comp = torch.multinomial(mix.weights, b1 - b0, replacement=True, generator=bg)
+            x = mix.centres[comp] + 0.35 * torch.randn(b1 - b0, DIM, generator=bg)
+            vb = torch.randn(b1 - b0, DIM, generator=bg)
+            s, e = max(begin, b0), min(end, b1)
+            k[h, s - begin:e - begin] = _rope(x[s - b0:e - b0], torch.arange(s, e)).bfloat16()
+            v[h, s - begin:e - begin] = vb[s - b0:e - b0].bfloat16()
+    return k, v, mixes
+
+
 def make_query(context: int, mixes, *, seed: int) -> torch.Tensor:
     """CPU BF16 Q [1, 1, 16, 256]: a component centre of head j // 4 plus N(0, 0.2), RoPE'd at T."""
     gen = torch.Generator().manual_seed(int(seed))

@@ -57,6 +57,24 @@ class Case:
         return res, out
 
 
+class ShardCase(Case):
+    """One shard of a sequence-sharded synthetic cache (``ShardPlan``)."""
+
+    def __init__(self, plan, nprobe=128, seed=31, components=64):
+        self.plan = plan
+        self.context, self.sink, self.local = plan.context, plan.shard_sink, plan.shard_local
+        self.k, self.v, self.mixes = synthetic.make_kv_range(plan.total, plan.begin, plan.end, seed=seed,
+                                                             components=components)
+        self.index = SeoulKV4Index.build(self.k, self.v, sink=self.sink, local=self.local, nprobe=nprobe)
+        self.planes = O.key_codec(bits(self.k))
+        self._k8 = self._v8 = None
+
+    def reference_view(self):
+        k8, v8 = self.kv8()
+        return dict(cells=self.cells(), begin=self.plan.begin, context=self.context, sink=self.sink,
+                    local=self.local, k8=k8, v8=v8)
+
+
 # ------------------------------------------------------------ golden data
 
 GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "golden_t8192.npz"
