@@ -4,9 +4,13 @@ One step = one decode of one query token through one layer (4 KV heads,
 16 query heads, d=256): coarse -> fine -> Stage-1.5 -> Stage-1.6 -> Stage-II
 -> FP8 attention.  Each step uses a fresh Q; L2 is flushed (a 256 MiB write)
 before every timed step, so the index planes are read cold.  With
-``--gpus N`` (torchrun), every rank decodes its own independent layer (weak
-scaling, no collective on the data path); the reported value is the
-whole-job time per layer, max over ranks.
+``--gpus N`` (torchrun) the layer is sequence-sharded: a context of
+N x 131072 tokens (1M at N = 8) split into contiguous
+128K ranges, one per GPU, each with its own index; every step runs the local
+funnels, an exact global top-100 merge and a log-sum-exp combine of the
+attention partials over NVLink (two NCCL all-gathers).  Weak scaling: the
+per-GPU context is fixed; the value is the time per decode step of the whole
+sharded layer, max over ranks.
 
 ``--impl reference`` times the CPU restatement of the reference pipeline
 (the reference ships no runnable CPU decode; its device path needs a
@@ -47,6 +51,7 @@ def parse():
     p.add_argument("--nprobe", type=int, default=384)
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--cpu-steps", type=int, default=2)
+    p.add_argument("--components", type=int, default=256, help="mixture components per KV head")
     return p.parse_args()
 
 
@@ -164,8 +169,12 @@ def run_reference(args):
     cores = os.cpu_count() or 1
     seed = CONFIG_INDEX * 1000
     dev = "cuda:0" if torch.cuda.is_available() else "cpu"
-    k, v, mixes, index = make_layer(args.context, args.nprobe, seed, dev)
     from seoulkv_b200 import synthetic
+
+    if world > 1:
+        run_reference_sharded(args, world, dev)
+        return
+    k, v, mixes, index = make_layer(args.context, args.nprobe, seed, dev)
 
     cells = oracle_cells(k, index)
     k8 = O.fp8_e4m3(k.float().numpy())
@@ -196,6 +205,152 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_sharded(args, world, dev):
+    """CPU arm of the sequence-sharded layer: shard 0's funnel and attention
+    restated on the host, times the shard count (the host decodes the shards
+    in turn)."""
+    from oracle import oracle as O
+    from seoulkv_b200 import SeoulKV4Index, synthetic
+    from seoulkv_b200.sharded import ShardPlan
+
+    total = args.context * world
+    plan = ShardPlan(total, world, 0)
+    seed = 3 * 1000
+    k, v, mixes = synthetic.make_kv_range(total, plan.begin, plan.end, seed=seed, components=args.components)
+    index = SeoulKV4Index.build(k, v, sink=plan.shard_sink, local=plan.shard_local, nprobe=args.nprobe,
+                                build_device=dev)
+    cells = oracle_cells(k, index)
+    k8 = O.fp8_e4m3(k.float().numpy())
+    v8 = O.fp8_e4m3(v.float().numpy())
+    steps = max(1, min(args.steps, args.cpu_steps))
+    qs = [synthetic.make_query(total, mixes, seed=seed * 7919 + i) for i in range(steps + 1)]
+    with ThreadPoolExecutor(max_workers=4) as pool:
+        oracle_decode(cells, qs[0], k8, v8, plan.context, pool)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            oracle_decode(cells, qs[1 + i], k8, v8, plan.context, pool)
+        dt = time.perf_counter() - t0
+    us = dt / steps * 1e6 * world
+    line = {
+        "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": 1,
+        "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f64-exact dots, f32 post-ops, bf16 scores", "data": "synthetic (BASELINE generator, seeded)",
+        "impl": "reference",
+        "config": {"workload": f"1 layer sequence-sharded over {world} GPUs, T={total} ({args.context} per GPU)",
+                   "context": total, "context_per_gpu": args.context, "nprobe": args.nprobe},
+        "cpu_baseline": {"value": us, "unit": UNIT, "cores": 4, "kind": "port",
+                         "sample": f"{steps} decode steps of shard 0 ({args.context} tokens; funnel + attention, "
+                                   f"4 KV heads on 4 threads, C restatement), x {world} shards decoded in turn"},
+        "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_sharded(args, world, rank, local, device):
+    """The sequence-sharded layer: N x args.context tokens, one range per rank."""
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from seoulkv_b200 import SeoulKV4Config, SeoulKV4Index, synthetic
+    from seoulkv_b200.sharded import ShardedSeoulKV4, ShardPlan
+
+    total = args.context * world
+    plan = ShardPlan(total, world, rank)
+    seed = 3 * 1000  # BASELINE configs[3]: sequence-sharded long context
+    k, v, mixes = synthetic.make_kv_range(total, plan.begin, plan.end, seed=seed, components=args.components)
+    index = SeoulKV4Index.build(k, v, sink=plan.shard_sink, local=plan.shard_local, nprobe=args.nprobe,
+                                build_device=str(device))
+    sh = ShardedSeoulKV4(device=device, k=k, v=v, index=index, plan=plan, config=SeoulKV4Config(debug=True))
+    n_q = args.warmup + args.steps
+    qs_host = [synthetic.make_query(total, mixes, seed=seed * 7919 + i) for i in range(max(n_q, args.e2e_steps + 2))]
+    q_dev = [q.to(device) for q in qs_host[:n_q]]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for i in range(args.warmup):
+        flush.zero_()
+        sh.run(q_dev[i])
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = Clocks(local)
+    dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        sh.run(q_dev[args.warmup + i])
+        ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    clk = clocks.stop()
+    per = np.array([a.elapsed_time(b) for a, b in zip(starts, ends)]) * 1e3  # µs
+    t = torch.tensor([float(per.sum())], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    value = float(t.item()) / args.steps
+
+    # parity: this shard's funnel vs the CPU restatement (ids bit-exact); the
+    # merge vs the restated merge rule on the gathered lists; one output on
+    # every rank
+    qi = args.warmup + args.steps - 1
+    out = sh.run(q_dev[qi]).clone()
+    torch.cuda.synchronize(device)
+    cells = oracle_cells(k, index)
+    qb = q_dev[qi].cpu().contiguous().view(torch.int16).numpy().view(np.uint16).reshape(16, 256)
+    with ThreadPoolExecutor(max_workers=4) as pool:
+        res = list(pool.map(lambda g: O.run_cell(cells[g], qb[4 * g:4 * g + 4]), range(4)))
+    local_ok = np.array_equal(sh.attn.debug_snapshot()["selected_ids"].numpy(),
+                              np.stack([r["final_ids"] for r in res]))
+    begin = [ShardPlan(total, world, r).begin for r in range(world)]
+    merged = O.merge_shards(sh.keys_all.cpu().numpy().view(np.uint32), sh.ids_all.cpu().numpy(), begin)
+    merge_ok = np.array_equal(merged, sh.gids.cpu().numpy())
+    outs = torch.empty(world, *out.shape, dtype=out.dtype, device=device)
+    dist.all_gather_into_tensor(outs.view(-1), out.contiguous().view(-1))
+    same_out = bool(all(torch.equal(outs[0], outs[r]) for r in range(world)))
+    flags = torch.tensor([int(local_ok), int(merge_ok)], device=device)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    parity = {"local_ids_bit_exact_all_shards": bool(flags[0]), "global_merge_exact": bool(flags[1]),
+              "same_output_on_every_rank": same_out,
+              "note": "per-shard funnel ids vs the CPU restatement, global merge vs the restated merge rule"}
+
+    # end to end through the public API: pinned host Q -> run -> host output
+    qp = [q.pin_memory() for q in qs_host[:args.e2e_steps + 2]]
+    for i in range(2):
+        sh.run(qp[i]).cpu()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        sh.run(qp[i + 2]).cpu()
+    e2e_us = torch.tensor([(time.perf_counter() - t0) / max(1, args.e2e_steps) * 1e6], device=device,
+                          dtype=torch.float64)
+    dist.all_reduce(e2e_us, op=dist.ReduceOp.MAX)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": value / 1e3, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64-exact dots, f32 softmax, bf16 scores, fp8 K/V",
+            "data": "synthetic (BASELINE generator, seeded, block-seeded per token range), fresh Q per step",
+            "config": {"workload": f"1 layer sequence-sharded over {world} GPUs, T={total} "
+                                   f"({args.context} per GPU), 4 KV / 16 Q heads, d=256, nprobe={args.nprobe} "
+                                   f"per shard, sink on the first shard, local on the last, exact global top-100",
+                       "context": total, "context_per_gpu": args.context, "nprobe": args.nprobe,
+                       "components": args.components, "l2": "flushed before every step",
+                       "parallelism": f"sequence-sharded x{world}, NCCL all-gather of top-100 lists and partials"},
+            "p50_us": float(np.percentile(per, 50)), "p99_us": float(np.percentile(per, 99)),
+            "tokens_per_s": 1e6 / value, "parity": parity, "cpu_baseline": None,
+            "e2e": {"value": float(e2e_us.item()), "unit": UNIT, "h2d_bytes_per_step": 16 * 256 * 2,
+                    "d2h_bytes_per_step": 16 * 256 * 2, "timing": "host wall clock incl. sync, max over ranks"},
+            "clocks": clk,
+            "gpu_launches": (sh.attn._engine.kernels_per_step() + 3) * args.steps * world,
+        }
+        print(json.dumps(line), flush=True)
+    sh.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -210,6 +365,9 @@ def main():
                                 device_id=torch.device(f"cuda:{local}"))
     device = torch.device(f"cuda:{local}")
     torch.cuda.set_device(device)
+    if world > 1:
+        run_sharded(args, world, rank, local, device)
+        return
     from seoulkv_b200 import SeoulKV4, SeoulKV4Config, synthetic
 
     seed = CONFIG_INDEX * 1000 + rank
