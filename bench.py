@@ -52,6 +52,7 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--cpu-steps", type=int, default=2)
     p.add_argument("--components", type=int, default=256, help="mixture components per KV head")
+    p.add_argument("--staged", action="store_true", help="run the 14-kernel staged path instead of the fused one")
     return p.parse_args()
 
 
@@ -365,6 +366,9 @@ def main():
                                 device_id=torch.device(f"cuda:{local}"))
     device = torch.device(f"cuda:{local}")
     torch.cuda.set_device(device)
+    from seoulkv_b200 import _native
+
+    _native.FORCE_STAGED = args.staged
     if world > 1:
         run_sharded(args, world, rank, local, device)
         return
