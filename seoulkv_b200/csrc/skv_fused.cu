@@ -80,8 +80,9 @@ struct SelCtl {
 
 struct FusedSmem {
   uint32_t frag[3 * FRAG_ROW];     // int8 digit fragments of the three operand rows
-  uint32_t hist[4 * 256];          // local histograms / reduced bins read back
-  uint32_t red[3][64];             // bins this CTA owns (three rotating buffers)
+  uint32_t hist[4 * 256];          // local histograms (selection rounds alternate with hist2)
+  uint32_t hist2[4 * 256];
+  alignas(16) uint32_t red[3][64]; // bins this CTA owns (three rotating buffers)
   unsigned long long mbar[NCHUNK];
   int pub[NPUB][4];                // values published to the cluster
   int all[CL][4];                  // the cluster's values of the latest exchange
@@ -189,6 +190,11 @@ __device__ __forceinline__ uint32_t ld_remote(uint32_t a) {
 __device__ __forceinline__ float ld_remote_f(uint32_t a) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_remote_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
 }
 __device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
@@ -328,8 +334,8 @@ __device__ __forceinline__ uint32_t select_key(const FusedSmem &S, int kind, int
 // on lane 0's bin in one atomic); selection keys crowd into few bins, where
 // per-key shared atomics from all warps serialise.
 template <int KIND>
-__device__ __forceinline__ void hist_pass(FusedSmem &S, int nloc, int q0, const uint32_t (&pf)[4],
-                                          const uint32_t (&mk)[4], int sh) {
+__device__ __forceinline__ void hist_pass(uint32_t *hist, const FusedSmem &S, int nloc, int q0,
+                                          const uint32_t (&pf)[4], const uint32_t (&mk)[4], int sh) {
   const int tid = threadIdx.x, lane = tid & 31;
   uint32_t cur[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu}, run[4] = {0u, 0u, 0u, 0u};
 #pragma unroll 1
@@ -340,7 +346,7 @@ __device__ __forceinline__ void hist_pass(FusedSmem &S, int nloc, int q0, const 
       if ((v & mk[h]) != pf[h]) continue;
       const uint32_t bin = h * 256 + ((v >> sh) & 255u);
       if (bin != cur[h]) {
-        if (run[h]) atomicAdd(&S.hist[cur[h]], run[h]);
+        if (run[h]) atomicAdd(&hist[cur[h]], run[h]);
         cur[h] = bin;
         run[h] = 0u;
       }
@@ -352,11 +358,44 @@ __device__ __forceinline__ void hist_pass(FusedSmem &S, int nloc, int q0, const 
     const uint32_t b0 = __shfl_sync(0xffffffffu, cur[h], 0);
     const uint32_t tot0 = __reduce_add_sync(0xffffffffu, cur[h] == b0 ? run[h] : 0u);
     if (lane == 0) {
-      if (b0 != 0xffffffffu && tot0) atomicAdd(&S.hist[b0], tot0);
+      if (b0 != 0xffffffffu && tot0) atomicAdd(&hist[b0], tot0);
     } else if (cur[h] != b0 && run[h]) {
-      atomicAdd(&S.hist[cur[h]], run[h]);
+      atomicAdd(&hist[cur[h]], run[h]);
     }
   }
+}
+
+// warp_find_desc over bins held in registers: lane l holds c[j] = bin
+// 255 - 8l - j.  Also returns the count in the found bin.
+__device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t k, int lane, int &bin,
+                                               uint32_t &above, uint32_t &cnt) {
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += c[j];
+  uint32_t incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t excl = incl - s;
+  const bool mine = excl < k && k <= incl;
+  const unsigned bal = __ballot_sync(0xffffffffu, mine);
+  int b = 0;
+  uint32_t ab = 0, cn = 0;
+  if (mine) {
+    uint32_t acc = excl;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (acc + c[j] >= k) { b = 255 - 8 * lane - j; ab = acc; cn = c[j]; break; }
+      acc += c[j];
+    }
+  }
+  const int src = bal ? __ffs(bal) - 1 : 0;
+  bin = __shfl_sync(0xffffffffu, b, src);
+  above = __shfl_sync(0xffffffffu, ab, src);
+  cnt = __shfl_sync(0xffffffffu, cn, src);
+  return bal != 0;
 }
 
 // K-th largest of the cluster's keys (select_key of `kind`) for each of
@@ -377,12 +416,13 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     S.ctl.done[tid] = K == 0;
     S.ctl.th[tid] = K == 0 ? 0xffffffffu : 0u;
   }
+  for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
   __syncthreads();
-  for (int sh = 24; sh >= 32 - nbits; sh -= 8) {
+  int r = 0;  // round of this selection: local histograms alternate between hist and hist2
+  for (int sh = 24; sh >= 32 - nbits; sh -= 8, ++r) {
     if (S.ctl.done[0] && S.ctl.done[1] && S.ctl.done[2] && S.ctl.done[3]) break;
     const int buf = S.round % 3, nbuf = (S.round + 1) % 3;
-    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
-    __syncthreads();
+    uint32_t *lh = (r & 1) ? S.hist2 : S.hist, *other = (r & 1) ? S.hist : S.hist2;
     // the four heads in one pass (independent chains per thread); a
     // finished head matches no key
     uint32_t pf[4], mk[4];
@@ -393,33 +433,31 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
       mk[h] = live ? S.ctl.mask[h] : 0u;
     }
     switch (kind) {
-      case KEY_COARSE: hist_pass<KEY_COARSE>(S, nloc, q0, pf, mk, sh); break;
-      case KEY_FINE: hist_pass<KEY_FINE>(S, nloc, q0, pf, mk, sh); break;
-      case KEY_S15: hist_pass<KEY_S15>(S, nloc, q0, pf, mk, sh); break;
-      default: hist_pass<KEY_S16>(S, nloc, q0, pf, mk, sh); break;
+      case KEY_COARSE: hist_pass<KEY_COARSE>(lh, S, nloc, q0, pf, mk, sh); break;
+      case KEY_FINE: hist_pass<KEY_FINE>(lh, S, nloc, q0, pf, mk, sh); break;
+      case KEY_S15: hist_pass<KEY_S15>(lh, S, nloc, q0, pf, mk, sh); break;
+      default: hist_pass<KEY_S16>(lh, S, nloc, q0, pf, mk, sh); break;
     }
     if (tid < 64) S.red[nbuf][tid] = 0;
     __syncthreads();
     mark(M_HIST);
     for (int e = tid; e < 4 * 256; e += FT) {
-      const uint32_t c = S.hist[e];
+      const uint32_t c = lh[e];
       if (c) red_remote(remote(&S.red[buf][e & 63], (uint32_t)(e >> 6)), c);
+      other[e] = 0u;  // the next round's local histogram
     }
     cluster_sync();
     mark(M_SYNC);
-    {
-      static_assert(4 * 256 == 2 * FT, "two reduced bins per thread");
-      const uint32_t a = ld_remote(remote(&S.red[buf][tid & 63], (uint32_t)(tid >> 6)));
-      const uint32_t b = ld_remote(remote(&S.red[buf][(tid + FT) & 63], (uint32_t)((tid + FT) >> 6)));
-      S.hist[tid] = a;
-      S.hist[tid + FT] = b;
-    }
-    __syncthreads();
     if (warp < 4 && !S.ctl.done[warp]) {
-      const int h = warp;
+      // head h's 256 reduced bins straight into registers: lane l reads bins
+      // 248 - 8l .. 255 - 8l (one owner, two 16-byte loads)
+      const int h = warp, e0 = h * 256 + 248 - 8 * lane;
+      const uint32_t a = remote(&S.red[buf][e0 & 63], (uint32_t)(e0 >> 6));
+      const uint4 lo4 = ld_remote_v4(a), hi4 = ld_remote_v4(a + 16);
+      const uint32_t c[8] = {hi4.w, hi4.z, hi4.y, hi4.x, lo4.w, lo4.z, lo4.y, lo4.x};  // bins 255-8l-j
       int bin;
-      uint32_t above;
-      const bool found = warp_find_desc(S.hist + h * 256, S.ctl.krem[h], lane, bin, above);
+      uint32_t above, cnt;
+      const bool found = warp_find_regs(c, S.ctl.krem[h], lane, bin, above, cnt);
       if (lane == 0) {
         if (!found) {
           S.ctl.done[h] = 1;
@@ -427,7 +465,6 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
         } else {
           const uint32_t pf = S.ctl.prefix[h] | ((uint32_t)bin << sh);
           const uint32_t kr = S.ctl.krem[h] - above;
-          const uint32_t cnt = S.hist[h * 256 + bin];
           S.ctl.prefix[h] = pf;
           S.ctl.mask[h] |= 255u << sh;
           S.ctl.krem[h] = kr;
