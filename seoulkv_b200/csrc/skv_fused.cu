@@ -89,8 +89,6 @@ struct FusedSmem {
   SelCtl ctl;
   int shift[3][4];
   float qscal[8];
-  int sE[12][8];
-  long long sXp[12][8];            // partial sums of X over 32 dimensions
   long long sxsum[3][4];           // sum over d of X_d per operand row and head
   int round, status, n_win, pad_;
   CellDev cell;                    // this cell's descriptor (read once from global)
@@ -639,39 +637,41 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   }
   __syncthreads();
   mark(M_ISSUE);
-  {
-    // 12 operand rows (row r, head h); thread (half, d) takes rows half + 2k
-    const int d = tid & 255, half = tid >> 8;
-    // operand row r of head h at dimension d
-    auto operand = [&](int r, int h) {
-      const float xa = S.sx[h * D + d];
-      if (r == R_Q) return xa;
-      const float prod = __fmul_rn(xa, S.kscale[d]);
-      return r == R_Q15 ? __fmul_rn(bf16f(bf16_rne(__fmul_rn(prod, 0.015625f))), 16.0f)
-                        : bf16f(bf16_rne(__fmul_rn(prod, 0.00390625f)));
-    };
-#pragma unroll 1
-    for (int k = 0; k < 6; ++k) {
-      const int p = half + 2 * k, r = p >> 2, h = p & 3;
-      const float x = operand(r, h);
-      int e = x != 0.0f ? ilogbf(x) : INT_MIN;
-      e = __reduce_max_sync(0xffffffffu, e);
-      if (lane == 0) S.sE[p][warp & 7] = e;
-    }
-    __syncthreads();
-    mark(M_QEXP);
-    uint8_t *fb = reinterpret_cast<uint8_t *>(S.frag);
-#pragma unroll 1
-    for (int k = 0; k < 6; ++k) {
-      const int p = half + 2 * k, r = p >> 2, h = p & 3;
-      int E = INT_MIN;
+  static_assert(FW == 16, "12 operand-row warps + 4 norm warps");
+  if (warp < 12) {
+    // operand row r = warp / 4 of head h = warp % 4, one warp per row; lane l
+    // takes dimensions l + 32k (k = 0..7): the row's exponent and its exact
+    // digit sum are warp reductions
+    const int r = warp >> 2, h = warp & 3;
+    float x[8];
+    int e = INT_MIN;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) E = max(E, S.sE[p][j]);
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      const float xa = S.sx[h * D + d];
+      float v = xa;
+      if (r != R_Q) {
+        const float prod = __fmul_rn(xa, S.kscale[d]);
+        v = r == R_Q15 ? __fmul_rn(bf16f(bf16_rne(__fmul_rn(prod, 0.015625f))), 16.0f)
+                       : bf16f(bf16_rne(__fmul_rn(prod, 0.00390625f)));
+      }
+      x[k] = v;
+      e = max(e, v != 0.0f ? ilogbf(v) : INT_MIN);
+    }
+    const int E = __reduce_max_sync(0xffffffffu, e);
+    uint8_t *fb = reinterpret_cast<uint8_t *>(S.frag) + r * FRAG_ROW * 4;
+    long long xsum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
       int X = 0;
       if (E != INT_MIN) {
-        const double v = (double)operand(r, h);
+        const double v = (double)x[k];
+        // kept elements are integers on the 2^(E-29) grid, |X| < 2^30
         if (!(fabs(v) < pow2d(E - 22))) X = __double2int_rn(v * pow2d(29 - E));
       }
+      xsum += X;
+      // four signed base-256 digits, X = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3
       int dg[4];
       dg[0] = (int)(int8_t)(X & 0xff);
       int rest = (X - dg[0]) >> 8;
@@ -679,44 +679,41 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       rest = (rest - dg[1]) >> 8;
       dg[2] = (int)(int8_t)(rest & 0xff);
       dg[3] = (rest - dg[2]) >> 8;
+      // fragment byte of dimension d: k-step, register, byte, thread-in-quad
       const int ks = d >> 5, reg = (d >> 4) & 1, byte = (d >> 2) & 3, tq = d & 3, nt = h >> 1;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int lane_b = 4 * (4 * (h & 1) + j) + tq;
-        fb[r * FRAG_ROW * 4 + (((ks * 2 + nt) * 32 + lane_b) * 2 + reg) * 4 + byte] = (uint8_t)(int8_t)dg[j];
+        fb[(((ks * 2 + nt) * 32 + lane_b) * 2 + reg) * 4 + byte] = (uint8_t)(int8_t)dg[j];
       }
-      if (d == 0) S.shift[r][h] = E == INT_MIN ? 0 : E - 29;
-      long long xsum = X;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) xsum += __shfl_xor_sync(0xffffffffu, xsum, o);
-      if (lane == 0) S.sXp[p][warp & 7] = xsum;
     }
-    if (warp < 4) {
-      // lambda*|q| and 3*sum(q): pairwise FP64 sums in dimension order
-      const int h = warp;
-      double v[8], sq[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { v[j] = (double)S.sx[h * D + 8 * lane + j]; sq[j] = v[j] * v[j]; }
-      double a = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-      double b = ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
+    for (int o = 16; o > 0; o >>= 1) xsum += __shfl_xor_sync(0xffffffffu, xsum, o);
+    if (lane == 0) {
+      S.shift[r][h] = E == INT_MIN ? 0 : E - 29;
+      S.sxsum[r][h] = xsum;
+    }
+  } else {
+    // lambda*|q| and 3*sum(q) of head warp - 12: pairwise FP64 sums in
+    // dimension order
+    const int h = warp - 12;
+    double v[8], sq[8];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        a = a + __shfl_xor_sync(0xffffffffu, a, o);
-        b = b + __shfl_xor_sync(0xffffffffu, b, o);
-      }
-      if (lane == 0) {
-        S.qscal[h] = __fmul_rn(__double2float_rn(__dsqrt_rn(b)), c.lam);
-        S.qscal[4 + h] = __fmul_rn(3.0f, __double2float_rn(a));
-      }
+    for (int j = 0; j < 8; ++j) { v[j] = (double)S.sx[h * D + 8 * lane + j]; sq[j] = v[j] * v[j]; }
+    double a = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    double b = ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      a = a + __shfl_xor_sync(0xffffffffu, a, o);
+      b = b + __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (lane == 0) {
+      S.qscal[h] = __fmul_rn(__double2float_rn(__dsqrt_rn(b)), c.lam);
+      S.qscal[4 + h] = __fmul_rn(3.0f, __double2float_rn(a));
     }
   }
   __syncthreads();
-  if (tid < 12) {
-    long long x = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x += S.sXp[tid][j];
-    S.sxsum[tid >> 2][tid & 3] = x;
-  }
+  mark(M_QEXP);
   mark(M_QPREP);
   // this CTA has started and its owner bins are zero; the matching wait
   // precedes the first distributed-shared-memory access (P2)
