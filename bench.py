@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--cpu-steps", type=int, default=2)
     p.add_argument("--components", type=int, default=256, help="mixture components per KV head")
     p.add_argument("--staged", action="store_true", help="run the 14-kernel staged path instead of the fused one")
+    p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
+                   help="sharded exchange: peer memory inside the step graph, or NCCL all-gathers")
     return p.parse_args()
 
 
@@ -261,7 +263,8 @@ def run_sharded(args, world, rank, local, device):
     k, v, mixes = synthetic.make_kv_range(total, plan.begin, plan.end, seed=seed, components=args.components)
     index = SeoulKV4Index.build(k, v, sink=plan.shard_sink, local=plan.shard_local, nprobe=args.nprobe,
                                 build_device=str(device))
-    sh = ShardedSeoulKV4(device=device, k=k, v=v, index=index, plan=plan, config=SeoulKV4Config(debug=True))
+    sh = ShardedSeoulKV4(device=device, k=k, v=v, index=index, plan=plan, config=SeoulKV4Config(debug=True),
+                         transport=args.transport)
     n_q = args.warmup + args.steps
     qs_host = [synthetic.make_query(total, mixes, seed=seed * 7919 + i) for i in range(max(n_q, args.e2e_steps + 2))]
     q_dev = [q.to(device) for q in qs_host[:n_q]]
@@ -304,8 +307,16 @@ def run_sharded(args, world, rank, local, device):
     local_ok = np.array_equal(sh.attn.debug_snapshot()["selected_ids"].numpy(),
                               np.stack([r["final_ids"] for r in res]))
     begin = [ShardPlan(total, world, r).begin for r in range(world)]
-    merged = O.merge_shards(sh.keys_all.cpu().numpy().view(np.uint32), sh.ids_all.cpu().numpy(), begin)
-    merge_ok = np.array_equal(merged, sh.gids.cpu().numpy())
+    from seoulkv_b200.sharded import _Dev
+
+    kp, ip = sh.attn._engine.shard_outputs(0)
+    mine = torch.stack([torch.as_tensor(_Dev(p, (4, 4, 100), "<i4", stream.cuda_stream), device=device)
+                        for p in (kp, ip)]).clone()
+    lists = torch.empty(world, 2, 4, 4, 100, dtype=torch.int32, device=device)
+    dist.all_gather_into_tensor(lists.view(-1), mine.view(-1))
+    lists = lists.cpu().numpy()
+    merged = O.merge_shards(lists[:, 0].view(np.uint32), lists[:, 1], begin)
+    merge_ok = np.array_equal(merged, sh.selected_ids().cpu().numpy())
     outs = torch.empty(world, *out.shape, dtype=out.dtype, device=device)
     dist.all_gather_into_tensor(outs.view(-1), out.contiguous().view(-1))
     same_out = bool(all(torch.equal(outs[0], outs[r]) for r in range(world)))
@@ -338,13 +349,17 @@ def run_sharded(args, world, rank, local, device):
                                    f"per shard, sink on the first shard, local on the last, exact global top-100",
                        "context": total, "context_per_gpu": args.context, "nprobe": args.nprobe,
                        "components": args.components, "l2": "flushed before every step",
-                       "parallelism": f"sequence-sharded x{world}, NCCL all-gather of top-100 lists and partials"},
+                       "parallelism": f"sequence-sharded x{world}, " + (
+                           "top-100 lists and partials exchanged over peer memory (NVLink) inside the step graph"
+                           if args.transport == "p2p" else "NCCL all-gathers of top-100 lists and partials"),
+                       "transport": args.transport},
             "p50_us": float(np.percentile(per, 50)), "p99_us": float(np.percentile(per, 99)),
             "tokens_per_s": 1e6 / value, "parity": parity, "cpu_baseline": None,
             "e2e": {"value": float(e2e_us.item()), "unit": UNIT, "h2d_bytes_per_step": 16 * 256 * 2,
                     "d2h_bytes_per_step": 16 * 256 * 2, "timing": "host wall clock incl. sync, max over ranks"},
             "clocks": clk,
-            "gpu_launches": (sh.attn._engine.kernels_per_step() + 3) * args.steps * world,
+            "gpu_launches": (sh.attn._engine.kernels_per_step() + (4 if args.transport == "p2p" else 3))
+                            * args.steps * world,
         }
         print(json.dumps(line), flush=True)
     sh.close()

@@ -204,6 +204,24 @@ int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, 
  * [n_cells / 4][16][256]. */
 int skv_shard_combine(const float *partials, int32_t n_shards, int32_t n_cells, uint16_t *out, void *stream);
 
+/* Sequence-sharded group over peer memory (NVLink), without a collective
+ * library: skv_shard_setup allocates this shard's exchange region (one slot,
+ * n_shards <= 8; begin = host array of every shard's first global token) and
+ * writes its 64-byte CUDA IPC handle to ipc_handle; after the caller has
+ * moved every shard's handle to every shard, skv_shard_connect (handles =
+ * n_shards x 64 bytes in shard order) maps the peers' regions.  From then on
+ * every skv_run is the whole layer step: the funnel, then each shard writes
+ * its top-100 lists and its attention partials straight into every peer's
+ * region and waits (bounded; SKV_STATUS_TIMEOUT on expiry) for the others',
+ * so skv_output gives the layer's BF16 output on every shard.  All shards
+ * must call skv_run once per step. */
+int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t *begin, void *ipc_handle);
+int skv_shard_connect(void *handle, const void *ipc_handles);
+int32_t skv_shard_ipc_handle_bytes(void);
+/* Device address of the connected group's global winners [4][4][100]
+ * (global token ids, -1 past the end) of the last step. */
+int skv_shard_gids(void *handle, const int32_t **gids);
+
 /* Sparse attention that allocates nothing -- no counterpart in the reference.
  *
  * For callers that cannot allocate device memory while running (for example

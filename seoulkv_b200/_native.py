@@ -28,6 +28,7 @@ EXPORTS = (
     "skv_debug_ids", "skv_read_stage", "skv_traffic", "skv_profile_step", "skv_kernel_name",
     "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name",
     "skv_shard_outputs", "skv_shard_merge", "skv_shard_attention", "skv_shard_combine",
+    "skv_shard_setup", "skv_shard_connect", "skv_shard_ipc_handle_bytes", "skv_shard_gids",
 )
 
 SKV_FLAG_STAGED = 1
@@ -123,6 +124,11 @@ def load() -> ctypes.CDLL:
                                             ctypes.c_void_p]
         lib.skv_shard_combine.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                           ctypes.c_void_p]
+        lib.skv_shard_setup.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                        ctypes.c_void_p]
+        lib.skv_shard_connect.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.skv_shard_ipc_handle_bytes.restype = ctypes.c_int32
+        lib.skv_shard_gids.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
         _lib = lib
         return lib
 
@@ -264,6 +270,25 @@ class Engine:
         check(self.lib.skv_shard_attention(self.handle, ctypes.c_void_p(gids), token_begin,
                                            ctypes.c_void_p(partials), ctypes.c_void_p(stream or None)),
               "skv_shard_attention")
+
+    def shard_setup(self, rank: int, n_shards: int, begin: list[int]) -> bytes:
+        """Allocate this shard's peer-exchange region; returns its IPC handle."""
+        nb = int(self.lib.skv_shard_ipc_handle_bytes())
+        h = ctypes.create_string_buffer(nb)
+        b = np.asarray(begin, dtype=np.int32)
+        check(self.lib.skv_shard_setup(self.handle, rank, n_shards, _ptr(b), h), "skv_shard_setup")
+        return h.raw
+
+    def shard_gids_ptr(self) -> int:
+        """Device address of the connected group's global winners [4][4][100]."""
+        p = ctypes.c_void_p()
+        check(self.lib.skv_shard_gids(self.handle, ctypes.byref(p)), "skv_shard_gids")
+        return int(p.value)
+
+    def shard_connect(self, handles: bytes) -> None:
+        """Map every peer's region (handles of all shards, in shard order)."""
+        buf = ctypes.create_string_buffer(handles, len(handles))
+        check(self.lib.skv_shard_connect(self.handle, buf), "skv_shard_connect")
 
     def traffic(self) -> dict:
         t = SkvTraffic()

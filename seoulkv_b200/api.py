@@ -165,7 +165,8 @@ class SeoulKV4:
                 device=torch.cuda.get_device_name(self._device_index),
                 attention_zones=zones.metadata(),
                 attention_kv_dtype="FP8_E4M3",
-                kernels_per_step=16,
+                kernels_per_step=self._engine.kernels_per_step(),
+                device_path="fused cluster kernel" if self._engine.fused else "staged kernels",
                 stage15_capacity=self._config.stage15_capacity,
                 graph_replay=True,
             )

@@ -62,11 +62,36 @@ struct Engine {
   cudaGraphExec_t exec = nullptr;
   bool fused = false;             // one cluster kernel per step (else the staged kernels)
   long long *phase_ts = nullptr;  // fused phase timestamps (skv_profile_phases)
+  // sequence-sharded group over peer memory (skv_shard_setup / skv_shard_connect)
+  struct {
+    bool active = false;
+    int rank = -1, n = 0;
+    int32_t begin[SHARD_MAX] = {};
+    void *region = nullptr;              // this shard's exchange region
+    void *opened[SHARD_MAX] = {};        // peers' regions mapped here (IPC)
+    uint32_t *epoch = nullptr;
+    int32_t *gids = nullptr;             // [4][4][100] global winners
+    float *part = nullptr;               // [4][4][PART] this shard's partials
+  } link;
 };
 
-// Enqueue one decode step of the engine's path.
+ShardLinkDev link_view(const Engine *e) {
+  ShardLinkDev L{};
+  for (int p = 0; p < e->link.n; ++p) L.peer[p] = p == e->link.rank ? e->link.region : e->link.opened[p];
+  for (int p = 0; p < e->link.n; ++p) L.begin[p] = e->link.begin[p];
+  L.rank = e->link.rank;
+  L.n_shards = e->link.n;
+  L.token_begin = e->link.begin[e->link.rank];
+  L.epoch = e->link.epoch;
+  return L;
+}
+
+// Enqueue one decode step of the engine's path; for a connected shard group
+// the global merge, attention and combine over peer memory follow.
 cudaError_t launch_step(const Engine *e, const Work &w, cudaStream_t st) {
-  return e->fused ? launch_fused(w, st) : launch_funnel(w, st);
+  cudaError_t r = e->fused ? launch_fused(w, st) : launch_funnel(w, st);
+  if (r != cudaSuccess || !e->link.active) return r;
+  return launch_shard_p2p_step(w, link_view(e), e->link.gids, e->link.part, w.counts + C_STATUS, st);
 }
 
 template <class T>
@@ -244,6 +269,9 @@ void skv_destroy(void *handle) {
   cudaSetDevice(e->desc.device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   if (e->ran && e->done) cudaEventSynchronize(e->done);
+  for (void *p : e->link.opened)
+    if (p) cudaIpcCloseMemHandle(p);
+  if (e->link.region) cudaFree(e->link.region);
   if (e->exec) cudaGraphExecDestroy(e->exec);
   if (e->graph) cudaGraphDestroy(e->graph);
   for (auto &b : e->bufs) free_cell(b, true, true);
@@ -617,6 +645,59 @@ int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, 
   if (rc) return rc;
   CK(cudaSetDevice(e->desc.device));
   CK(launch_shard_attention(e->work, gids, token_begin, partials, static_cast<cudaStream_t>(stream)));
+  return SKV_OK;
+}
+
+int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t *begin, void *ipc_handle) {
+  Engine *e = as_engine(handle);
+  if (!e || !begin || !ipc_handle) return fail(SKV_E_INVALID, "null engine or buffer");
+  if (n_shards < 1 || n_shards > SHARD_MAX || rank < 0 || rank >= n_shards)
+    return fail(SKV_E_INVALID, "rank / n_shards out of range (at most 8 shards)");
+  if (e->n_cells != SHARD_CELLS) return fail(SKV_E_INVALID, "a shard engine holds one slot");
+  if (e->link.region) return fail(SKV_E_STATE, "shard group already set up");
+  CK(cudaSetDevice(e->desc.device));
+  for (int p = 0; p < n_shards; ++p) e->link.begin[p] = begin[p];
+  e->link.rank = rank;
+  e->link.n = n_shards;
+  CK(cudaMalloc(&e->link.region, shard_region_bytes()));
+  CK(cudaMemset(e->link.region, 0, shard_region_bytes()));
+  int rc = dalloc(e, &e->link.epoch, 1);
+  if (!rc) rc = dalloc(e, &e->link.gids, (size_t)SHARD_CELLS * G * TOPK);
+  if (!rc) rc = dalloc(e, &e->link.part, (size_t)SHARD_CELLS * G * PART);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, e->link.region));
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  return SKV_OK;
+}
+
+int skv_shard_connect(void *handle, const void *ipc_handles) {
+  Engine *e = as_engine(handle);
+  if (!e || !ipc_handles) return fail(SKV_E_INVALID, "null engine or handles");
+  if (!e->link.region) return fail(SKV_E_STATE, "skv_shard_setup first");
+  if (e->link.active) return fail(SKV_E_STATE, "shard group already connected");
+  CK(cudaSetDevice(e->desc.device));
+  for (int p = 0; p < e->link.n; ++p) {
+    if (p == e->link.rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char *>(ipc_handles) + (size_t)p * sizeof(h), sizeof(h));
+    CK(cudaIpcOpenMemHandle(&e->link.opened[p], h, cudaIpcMemLazyEnablePeerAccess));
+  }
+  CK(cudaDeviceSynchronize());
+  e->link.active = true;
+  // the step graph is captured again with the merge/attention/combine kernels
+  if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = nullptr; }
+  if (e->graph) { cudaGraphDestroy(e->graph); e->graph = nullptr; }
+  return SKV_OK;
+}
+
+int32_t skv_shard_ipc_handle_bytes(void) { return (int32_t)sizeof(cudaIpcMemHandle_t); }
+
+int skv_shard_gids(void *handle, const int32_t **gids) {
+  Engine *e = as_engine(handle);
+  if (!e || !gids) return fail(SKV_E_INVALID, "null engine or output");
+  if (!e->link.gids) return fail(SKV_E_STATE, "skv_shard_setup first");
+  *gids = e->link.gids;
   return SKV_OK;
 }
 

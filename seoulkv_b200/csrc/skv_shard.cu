@@ -214,6 +214,128 @@ __global__ void __launch_bounds__(256) k_shard_combine(const float *partials, in
   }
 }
 
+// ------------------------------------------------ peer-memory exchange
+//
+// Without a collective library: every shard owns an exchange region in its
+// own memory that the other shards write into over NVLink (CUDA IPC
+// mappings), and per-step epoch flags say when a peer's part has landed.
+// Each (cell, head) CTA pushes its own list to every peer and then waits for
+// every peer's list of the same (cell, head); each cell CTA does the same
+// with the attention partials.  No CTA waits for another CTA of its own GPU.
+// Waits are bounded: after SHARD_WAIT_POLLS polls the step's status word gets
+// ST_TIMEOUT and the kernel carries on with whatever arrived.
+
+constexpr long long SHARD_WAIT_POLLS = 1 << 24;  // ~1.6 s at 100 ns per poll
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits (thread 0) until flag[s] >= epoch for every shard s; false on timeout.
+__device__ bool wait_flags(const uint32_t *flag, int stride, int n_shards, uint32_t epoch) {
+  for (int s = 0; s < n_shards; ++s) {
+    long long polls = 0;
+    while (ld_acquire_sys(flag + (size_t)s * stride) < epoch) {
+      if (++polls > SHARD_WAIT_POLLS) return false;
+      __nanosleep(100);
+    }
+  }
+  return true;
+}
+
+// One CTA per (cell, head): push this shard's list to every peer's slot
+// `rank`, signal, wait for every shard's list of this (cell, head), merge.
+__global__ void __launch_bounds__(MERGE_THREADS) k_shard_merge_p2p(ShardLinkDev L, const uint32_t *keys,
+                                                                   const int32_t *ids, int32_t *out,
+                                                                   int32_t *status) {
+  const int ch = blockIdx.x, tid = threadIdx.x, n = L.n_shards;
+  const uint32_t epoch = *L.epoch + 1;
+  __shared__ unsigned long long sk[MERGE_THREADS];
+  __shared__ int s_ok;
+  if (tid < TOPK) {
+    const uint32_t kv = keys[(size_t)ch * TOPK + tid];
+    const int32_t iv = ids[(size_t)ch * TOPK + tid];
+    for (int p = 0; p < n; ++p) {
+      ShardRegion *R = reinterpret_cast<ShardRegion *>(L.peer[p]);
+      R->keys[L.rank][ch][tid] = kv;
+      R->ids[L.rank][ch][tid] = iv;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int p = 0; p < n; ++p) st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_lists[L.rank][ch], epoch);
+    const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+    s_ok = wait_flags(&mine->flag_lists[0][ch], SHARD_CELLS * G, n, epoch);
+    if (!s_ok) atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
+  }
+  __syncthreads();
+  const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+  unsigned long long kv = 0ull;
+  int gid = -1;
+  if (tid < n * TOPK) {
+    const int s = tid / TOPK, r = tid - s * TOPK;
+    const uint32_t key = __ldcv(&R->keys[s][ch][r]);
+    if (key) {
+      gid = L.begin[s] + __ldcv(&R->ids[s][ch][r]);
+      kv = ((unsigned long long)(key >> 16) << 48) | ((unsigned long long)(0xffffu - (uint32_t)r) << 32) |
+           (unsigned long long)(0xffffffffu - (uint32_t)gid);
+    }
+  }
+  sk[tid] = kv;
+  const int valid = __syncthreads_count(kv != 0ull);
+  int32_t *dst = out + (size_t)ch * TOPK;
+  if (kv) {
+    int rank = 0;
+    for (int j = 0; j < n * TOPK; ++j) rank += sk[j] > kv;
+    if (rank < TOPK) dst[rank] = gid;
+  }
+  if (tid < TOPK && tid >= valid) dst[tid] = -1;
+}
+
+// One CTA per cell: push this shard's partials of the cell to every peer,
+// signal, wait for every shard's partials of the cell, combine into BF16.
+__global__ void __launch_bounds__(256) k_shard_combine_p2p(ShardLinkDev L, const float *part, uint16_t *out,
+                                                          int32_t *status) {
+  const int cell = blockIdx.x, g = cell & 3, d = threadIdx.x, n = L.n_shards;
+  const uint32_t epoch = *L.epoch + 1;
+  __shared__ int s_ok;
+  for (int p = 0; p < n; ++p) {
+    ShardRegion *R = reinterpret_cast<ShardRegion *>(L.peer[p]);
+    for (int i = d; i < G * PART; i += 256) R->part[L.rank][cell][i / PART][i % PART] = part[(size_t)cell * G * PART + i];
+  }
+  __syncthreads();
+  if (d == 0) {
+    __threadfence_system();
+    for (int p = 0; p < n; ++p) st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_parts[L.rank][cell], epoch);
+    const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+    s_ok = wait_flags(&mine->flag_parts[0][cell], SHARD_CELLS, n, epoch);
+    if (!s_ok) atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
+  }
+  __syncthreads();
+  const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+  for (int h = 0; h < G; ++h) {
+    float M = -INFINITY;
+    for (int s = 0; s < n; ++s) M = fmaxf(M, __ldcv(&R->part[s][cell][h][0]));
+    float Lsum = 0.0f, O = 0.0f;
+    for (int s = 0; s < n; ++s) {
+      const float m = __ldcv(&R->part[s][cell][h][0]);
+      if (m == -INFINITY) continue;
+      const float e = exp2f(m - M);
+      Lsum += __ldcv(&R->part[s][cell][h][1]) * e;
+      O += __ldcv(&R->part[s][cell][h][4 + d]) * e;
+    }
+    out[((size_t)(cell >> 2) * 16 + g * 4 + h) * D + d] = bf16_rne(O / Lsum);
+  }
+}
+
+__global__ void k_shard_epoch(ShardLinkDev L) { *L.epoch += 1; }
+
 }  // namespace
 
 cudaError_t launch_shard_merge(const uint32_t *keys, const int32_t *ids, const int32_t *begin, int n_shards,
@@ -234,5 +356,16 @@ cudaError_t launch_shard_combine(const float *partials, int n_shards, int n_cell
 }
 
 int shard_max_shards() { return MERGE_THREADS / TOPK; }
+
+size_t shard_region_bytes() { return sizeof(ShardRegion); }
+
+cudaError_t launch_shard_p2p_step(const Work &w, const ShardLinkDev &L, int32_t *gids, float *part,
+                                  int32_t *status, cudaStream_t st) {
+  k_shard_merge_p2p<<<SHARD_CELLS * G, MERGE_THREADS, 0, st>>>(L, w.final_keys, w.final_ids, gids, status);
+  k_shard_attn<<<dim3(ATTN_SPLIT, SHARD_CELLS), 256, 0, st>>>(w, gids, L.token_begin, part);
+  k_shard_combine_p2p<<<SHARD_CELLS, 256, 0, st>>>(L, part, w.out, status);
+  k_shard_epoch<<<1, 1, 0, st>>>(L);
+  return cudaGetLastError();
+}
 
 }  // namespace skv

@@ -16,9 +16,16 @@ other shards index their whole range, sink = local = 0).  One decode step:
 4. the partials are all-gathered and combined by log-sum-exp into the same
    BF16 output on every GPU.
 
-Steps 2-4 are CUDA kernels behind the C ABI (``skv_shard_merge``,
-``skv_shard_attention``, ``skv_shard_combine``); the two exchanges are
-``torch.distributed`` all-gathers (NCCL over NVLink on a GPU node).
+Steps 2-4 are CUDA kernels behind the C ABI.  Two transports move the lists
+and partials between GPUs:
+
+* ``"p2p"`` (default with more than one shard): every GPU maps its peers'
+  exchange regions once (CUDA IPC handles swapped over the process group);
+  the merge and combine kernels write straight into the peers' memory over
+  NVLink and wait (bounded) on per-step flags, so a whole step -- funnel,
+  merge, attention, combine -- is one CUDA graph with no host round trip;
+* ``"nccl"``: two ``torch.distributed`` all-gathers between separate
+  merge / attention / combine launches.
 """
 
 from __future__ import annotations
@@ -119,7 +126,7 @@ class ShardedSeoulKV4:
     """
 
     def __init__(self, *, device, k, v, index, plan: ShardPlan, config: SeoulKV4Config | None = None,
-                 group=None):
+                 group=None, transport: str | None = None):
         zones = index.zones
         if (zones.context, zones.sink, zones.local) != (plan.context, plan.shard_sink, plan.shard_local):
             raise ValueError("index zones do not match the shard plan")
@@ -140,6 +147,19 @@ class ShardedSeoulKV4:
         self.part = torch.empty(4, 4, PART, dtype=torch.float32, device=dev)
         self.part_all = torch.empty(n, 4, 4, PART, dtype=torch.float32, device=dev)
         self.out = torch.empty(16, 256, dtype=torch.int16, device=dev)
+        self.transport = transport or ("p2p" if n > 1 else "nccl")
+        if self.transport not in ("p2p", "nccl"):
+            raise ValueError("transport must be 'p2p' or 'nccl'")
+        if self.transport == "p2p":
+            # the engine now, so that its step graph is captured with the exchange kernels
+            self.attn._engine = self.attn._initialize()
+            self.attn._host_kv = None
+            mine = self.attn._engine.shard_setup(plan.shard, n, [r * plan.total // n for r in range(n)])
+            handles = [mine]
+            if n > 1:
+                handles = [None] * n
+                self.exchange.dist.all_gather_object(handles, mine, group=group)
+            self.attn._engine.shard_connect(b"".join(handles))
 
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
@@ -147,6 +167,12 @@ class ShardedSeoulKV4:
     def run(self, q: torch.Tensor) -> torch.Tensor:
         """One decode step of the whole layer; returns CUDA BF16 [1, 1, 16, 256]."""
         st = self._stream()
+        if self.transport == "p2p":
+            # funnel + merge + attention + combine, one graph; the engine's output is the layer's
+            self.attn.run(q)
+            eng = self.attn._engine
+            out = torch.as_tensor(_Dev(eng.output_device_ptr(), (16, 256), "<i2", st), device=self.device)
+            return out.view(torch.bfloat16).reshape(1, 1, 16, 256)
         self.attn.run(q)  # this shard's funnel (its own attention output is not used)
         eng = self.attn._engine
         kp, ip = eng.shard_outputs(0)
@@ -164,6 +190,10 @@ class ShardedSeoulKV4:
 
     def selected_ids(self) -> torch.Tensor:
         """Global token ids of the last step: CUDA int32 [4, 4, 100] (KV head, query head, rank; -1 past the end)."""
+        if self.transport == "p2p":
+            eng = self.attn._engine
+            ptr = eng.shard_gids_ptr()
+            return torch.as_tensor(_Dev(ptr, (4, 4, 100), "<i4", self._stream()), device=self.device)
         return self.gids
 
     def close(self) -> None:
