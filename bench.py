@@ -294,6 +294,28 @@ def run_sharded(args, world, rank, local, device):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     value = float(t.item()) / args.steps
 
+    # this shard's funnel alone (one non-graph launch, L2 flushed), every rank
+    fun = []
+    for _ in range(5):
+        flush.zero_()
+        torch.cuda.synchronize(device)
+        fun.append(sum(ms for _, ms in sh.attn._engine.profile_step(stream.cuda_stream)) * 1e3)
+    fun_all = torch.empty(world, dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(fun_all, torch.tensor([float(np.median(fun))], dtype=torch.float64, device=device))
+    shard_funnel_us = [round(float(x), 1) for x in fun_all.cpu()]
+    # phase marks of one whole group step (all ranks together; fused path only)
+    phases = None
+    if sh.attn._engine.fused and args.transport == "p2p":
+        mhz = (clk or {}).get("sm_mhz") or 1965.0
+        acc = {}
+        for _ in range(3):
+            flush.zero_()
+            torch.cuda.synchronize(device)
+            dist.barrier()
+            for name, cyc in sh.attn._engine.profile_phases(stream.cuda_stream):
+                acc[name] = acc.get(name, 0.0) + cyc / 3
+        phases = {n: round(v / mhz, 2) for n, v in acc.items()}
+
     # parity: this shard's funnel vs the CPU restatement (ids bit-exact); the
     # merge vs the restated merge rule on the gathered lists; one output on
     # every rank
@@ -354,7 +376,8 @@ def run_sharded(args, world, rank, local, device):
                            if args.transport == "p2p" else "NCCL all-gathers of top-100 lists and partials"),
                        "transport": args.transport},
             "p50_us": float(np.percentile(per, 50)), "p99_us": float(np.percentile(per, 99)),
-            "tokens_per_s": 1e6 / value, "parity": parity, "cpu_baseline": None,
+            "tokens_per_s": 1e6 / value, "shard_funnel_us": shard_funnel_us, "phase_us": phases, "parity": parity,
+            "cpu_baseline": None,
             "e2e": {"value": float(e2e_us.item()), "unit": UNIT, "h2d_bytes_per_step": 16 * 256 * 2,
                     "d2h_bytes_per_step": 16 * 256 * 2, "timing": "host wall clock incl. sync, max over ranks"},
             "clocks": clk,

@@ -166,7 +166,9 @@ int32_t skv_kernels_per_step(void);
 const char *skv_step_kernel_name(void *handle, int32_t i);
 /* One fused step with SM-clock marks between its phases (CTA 0 of cell 0):
  * segment i ends at mark tags[i] and took cycles[i] SM cycles; n =
- * min(max_marks, marks).  Synchronises.  SKV_E_STATE on the staged path. */
+ * min(max_marks, marks).  Synchronises.  SKV_E_STATE on the staged path.
+ * In a connected shard group this is a whole group step: every shard must
+ * call it together. */
 int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles, int32_t max_marks,
                        int32_t *n_marks);
 /* Name of a phase mark tag (static string). */

@@ -45,6 +45,52 @@ enum Row { R_Q = 0, R_Q15 = 1, R_QS = 2 };
 
 constexpr uint32_t ST_POOL_OVER = 1u, ST_POOL_UNDER = 2u, ST_FINE_SHORT = 4u, ST_TIMEOUT = 8u;
 
+// ---- sequence-sharded group over peer memory (one slot of 4 cells per shard)
+constexpr int SHARD_MAX = 8;    // shards of a peer-memory group
+constexpr int SHARD_CELLS = 4;  // one slot: 4 KV heads
+constexpr int SHARD_CTAS = 16;  // CTAs of a fused cluster (one output-dimension share each)
+
+// The exchange region every shard owns and every peer writes into.
+struct ShardRegion {
+  uint32_t keys[SHARD_MAX][SHARD_CELLS * G][TOPK];        // [source shard][cell*4+head][rank]
+  int32_t ids[SHARD_MAX][SHARD_CELLS * G][TOPK];
+  float part[SHARD_MAX][SHARD_CELLS][G][PART];            // [source shard][cell][head][m, l, 0, 0, o]
+  uint32_t flag_lists[SHARD_MAX][SHARD_CELLS * G];        // epoch of each source's (cell, head) list
+  uint32_t flag_parts[SHARD_MAX][SHARD_CELLS];            // epoch of each source's cell partials
+  uint32_t flag_share[SHARD_MAX][SHARD_CELLS * SHARD_CTAS];  // ... of each source's (cell, dim share)
+};
+
+// Kernel-side view of a connected group.
+struct ShardLinkDev {
+  void *peer[SHARD_MAX];          // every shard's region as mapped here (own one included)
+  int32_t begin[SHARD_MAX];       // first global token of each shard
+  int32_t rank, n_shards, token_begin;
+  uint32_t *epoch;                // steps completed (device counter)
+};
+
+// Cross-GPU flags: release/acquire at system scope; bounded polls.
+constexpr long long SHARD_WAIT_POLLS = 1 << 24;  // ~1.7 s at ~100 ns per poll
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits until flag[s * stride] >= epoch for every shard s; false on timeout.
+__device__ __forceinline__ bool wait_flags(const uint32_t *flag, int stride, int n_shards, uint32_t epoch) {
+  for (int s = 0; s < n_shards; ++s) {
+    long long polls = 0;
+    while (ld_acquire_sys(flag + (size_t)s * stride) < epoch) {
+      if (++polls > SHARD_WAIT_POLLS) return false;
+      __nanosleep(100);
+    }
+  }
+  return true;
+}
+
 struct CellDev {
   const uint8_t *upper, *lower;      // [nc][64]
   const float *coarse_scale4;        // [nc/32]
@@ -107,6 +153,8 @@ struct Work {
   uint32_t *hist;           // [cell][4 stages][4 heads][4096] first-pass histograms (step)
   uint16_t *out;            // [n_slots][16][256] BF16
   long long *phase_ts;      // [FUSED_MARKS][2] (tag, SM clock) marks of cell 0, or null
+  const ShardLinkDev *link; // sequence-sharded group (device copy), or null
+  int32_t *shard_gids;      // [4][4][TOPK] the group's global winners (with link)
 };
 
 __device__ __forceinline__ uint16_t bf16_rne(float f) {

@@ -72,6 +72,7 @@ struct Engine {
     uint32_t *epoch = nullptr;
     int32_t *gids = nullptr;             // [4][4][100] global winners
     float *part = nullptr;               // [4][4][PART] this shard's partials
+    ShardLinkDev *dev = nullptr;         // device copy of the group (Work::link)
   } link;
 };
 
@@ -91,7 +92,10 @@ ShardLinkDev link_view(const Engine *e) {
 cudaError_t launch_step(const Engine *e, const Work &w, cudaStream_t st) {
   cudaError_t r = e->fused ? launch_fused(w, st) : launch_funnel(w, st);
   if (r != cudaSuccess || !e->link.active) return r;
-  return launch_shard_p2p_step(w, link_view(e), e->link.gids, e->link.part, w.counts + C_STATUS, st);
+  // the fused kernel exchanges inside itself (Work::link); the staged path
+  // runs the exchange kernels after its funnel
+  if (!e->fused) r = launch_shard_p2p_step(w, link_view(e), e->link.gids, e->link.part, w.counts + C_STATUS, st);
+  return r == cudaSuccess ? launch_shard_epoch(e->link.dev, st) : r;
 }
 
 template <class T>
@@ -437,7 +441,13 @@ int skv_run(void *handle, void *stream) {
   if (!e->exec) {
     CK(cudaStreamSynchronize(e->stream));
     CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t le = launch_step(e, e->work, e->stream);
+    // only the step graph carries the group; profiling launches run the funnel alone
+    Work w = e->work;
+    if (e->link.active) {
+      w.link = e->link.dev;
+      w.shard_gids = e->link.gids;
+    }
+    cudaError_t le = launch_step(e, w, e->stream);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (le != cudaSuccess) {
@@ -684,6 +694,12 @@ int skv_shard_connect(void *handle, const void *ipc_handles) {
     CK(cudaIpcOpenMemHandle(&e->link.opened[p], h, cudaIpcMemLazyEnablePeerAccess));
   }
   CK(cudaDeviceSynchronize());
+  if (!e->link.dev) {
+    int rc = dalloc(e, &e->link.dev, 1);
+    if (rc) return rc;
+  }
+  const ShardLinkDev view = link_view(e);
+  CK(cudaMemcpy(e->link.dev, &view, sizeof(view), cudaMemcpyHostToDevice));
   e->link.active = true;
   // the step graph is captured again with the merge/attention/combine kernels
   if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = nullptr; }
@@ -784,7 +800,12 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
   CK(cudaMemcpyAsync(e->phase_ts, ts.data(), ts.size() * sizeof(long long), cudaMemcpyHostToDevice, st));
   Work w = e->work;
   w.phase_ts = e->phase_ts;
+  if (e->link.active) {  // a connected shard group: every shard must profile this step together
+    w.link = e->link.dev;
+    w.shard_gids = e->link.gids;
+  }
   CK(launch_fused(w, st));
+  if (e->link.active) CK(launch_shard_epoch(e->link.dev, st));
   CK(cudaMemcpyAsync(ts.data(), e->phase_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   CK(cudaEventRecord(e->done, st));

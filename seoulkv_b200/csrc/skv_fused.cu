@@ -124,7 +124,8 @@ static_assert(kSmemBytes <= 227 * 1024, "fused shared memory exceeds 227 KB");
 enum MarkTag {
   M_START, M_ISSUE, M_QEXP, M_QPREP, M_STARTED, M_SLICE, M_COARSE, M_HIST, M_SYNC, M_READ, M_CSEL,
   M_SURV, M_FGATHER, M_FINE, M_FSEL, M_SELLIST, M_SELX, M_KEEP, M_POOL, M_S15G, M_S15, M_S15SEL,
-  M_U15, M_S16, M_S16SEL, M_CAND, M_S2, M_S2SEL, M_ATTN_ITEMS, M_ATTN_CTA, M_ATTN, M_NTAGS
+  M_U15, M_S16, M_S16SEL, M_CAND, M_S2, M_S2SEL, M_ATTN_ITEMS, M_ATTN_CTA, M_ATTN, M_XLIST, M_XSHARE,
+  M_NTAGS
 };
 
 struct Marker {
@@ -564,6 +565,121 @@ __device__ __forceinline__ void fp8x8(uint2 v, float *o) {
     const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&a));
     const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&b));
     o[4 * k + 0] = fa.x; o[4 * k + 1] = fa.y; o[4 * k + 2] = fb.x; o[4 * k + 3] = fb.y;
+  }
+}
+
+// ------------------------------------------- sequence-sharded exchanges
+//
+// With Work::link (a connected group of shards, one per GPU), CTA h of a
+// cell's cluster writes its head's top-100 (keys, shard-local ids) into every
+// peer's exchange region over NVLink, raises its per-step flag there, waits
+// (bounded) for every shard's list of the same (cell, head) in its own
+// region, and merges: every shard's list is sorted by the 64-bit key
+// [score | 0xffff - rank | ~global id], so a candidate's global rank is its
+// own rank plus, per other list, a binary search for the entries above it.
+// The merged global winners go to Work::shard_gids.
+
+__device__ __forceinline__ unsigned long long merge_key(uint32_t key, int r, int gid) {
+  return ((unsigned long long)(key >> 16) << 48) | ((unsigned long long)(0xffffu - (uint32_t)r) << 32) |
+         (unsigned long long)(0xffffffffu - (uint32_t)gid);
+}
+
+__device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, int h, const uint32_t *fkeys,
+                                         const int32_t *fids, Marker &mark) {
+  const ShardLinkDev &L = *w.link;
+  const int tid = threadIdx.x, n = L.n_shards, ch = cell * G + h;
+  const uint32_t epoch = *L.epoch + 1;
+  __syncthreads();  // this head's keys and ids are written
+  for (int i = tid; i < TOPK; i += FT) {
+    const uint32_t k = fkeys[i];
+    const int32_t id = fids[i];
+    for (int p = 0; p < n; ++p) {
+      ShardRegion *R = reinterpret_cast<ShardRegion *>(L.peer[p]);
+      R->keys[L.rank][ch][i] = k;
+      R->ids[L.rank][ch][i] = id;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // cumulative: orders the CTA's pushes (before the barrier) before the flags
+    __threadfence_system();
+    for (int p = 0; p < n; ++p)
+      st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_lists[L.rank][ch], epoch);
+    const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+    if (!wait_flags(&mine->flag_lists[0][ch], SHARD_CELLS * G, n, epoch))
+      atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
+  }
+  __syncthreads();
+  mark(M_XLIST);
+  const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+  int32_t *gout = w.shard_gids + (size_t)ch * TOPK;
+  int valid = 0;
+  for (int c = tid; c < n * TOPK; c += FT) {
+    const int s = c / TOPK, r = c - s * TOPK;
+    const uint32_t key = __ldcv(&R->keys[s][ch][r]);
+    if (!key) continue;
+    const int gid = L.begin[s] + __ldcv(&R->ids[s][ch][r]);
+    const unsigned long long kv = merge_key(key, r, gid);
+    int rank = r;
+    for (int s2 = 0; s2 < n; ++s2) {
+      if (s2 == s) continue;
+      int lo = 0, hi = TOPK;  // first entry of list s2 not above kv
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        const uint32_t k2 = __ldcv(&R->keys[s2][ch][mid]);
+        const bool above = k2 && merge_key(k2, mid, L.begin[s2] + __ldcv(&R->ids[s2][ch][mid])) > kv;
+        if (above) lo = mid + 1; else hi = mid;
+      }
+      rank += lo;
+    }
+    if (rank < TOPK) gout[rank] = gid;
+    ++valid;
+  }
+  int total;
+  block_exclusive_scan(valid, &total);
+  for (int i = total + tid; i < TOPK; i += FT) gout[i] = -1;  // fewer than 100 candidates in the group
+}
+
+// Sharded attention combine: this CTA's share (dimensions [16 r, 16 r + 16)
+// of the four heads, threads tid < 64 holding (M, L, O) of head tid / 16)
+// of this shard's partial goes to every peer, then the shards' shares of the
+// same dimensions are merged by log-sum-exp into the BF16 output.
+__device__ __noinline__ void shard_share(const Work &w, FusedSmem &S, int cell, int r, float M, float L, float O,
+                                         int h, int d, Marker &mark) {
+  const ShardLinkDev &L_ = *w.link;
+  const int tid = threadIdx.x, n = L_.n_shards, fs = cell * SHARD_CTAS + r;
+  const uint32_t epoch = *L_.epoch + 1;
+  if (tid < G * 16) {
+    for (int p = 0; p < n; ++p) {
+      float *dst = reinterpret_cast<ShardRegion *>(L_.peer[p])->part[L_.rank][cell][h];
+      dst[4 + d] = O;
+      if ((tid & 15) == 0) { dst[0] = M; dst[1] = L; }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();  // cumulative over the CTA's pushes
+    for (int p = 0; p < n; ++p)
+      st_release_sys(&reinterpret_cast<ShardRegion *>(L_.peer[p])->flag_share[L_.rank][fs], epoch);
+    const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L_.peer[L_.rank]);
+    if (!wait_flags(&mine->flag_share[0][fs], SHARD_CELLS * SHARD_CTAS, n, epoch))
+      atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
+  }
+  __syncthreads();
+  mark(M_XSHARE);
+  if (tid < G * 16) {
+    const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L_.peer[L_.rank]);
+    float Mx = -INFINITY;
+    for (int s = 0; s < n; ++s) Mx = fmaxf(Mx, __ldcv(&R->part[s][cell][h][0]));
+    float Ls = 0.0f, Os = 0.0f;
+    for (int s = 0; s < n; ++s) {
+      const float m = __ldcv(&R->part[s][cell][h][0]);
+      if (m == -INFINITY) continue;
+      const float e = exp2f(m - Mx);
+      Ls += __ldcv(&R->part[s][cell][h][1]) * e;
+      Os += __ldcv(&R->part[s][cell][h][4 + d]) * e;
+    }
+    w.out[((size_t)(cell >> 2) * 16 + (cell & 3) * 4 + h) * D + d] = bf16_rne(Os / Ls);
   }
 }
 
@@ -1253,8 +1369,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       fids[tid] = 0;
       fkeys[tid] = 0u;
     }
+    if (w.link) shard_lists(w, S, cell, h, fkeys, fids, mark);
   }
-  cluster_sync();  // final ids complete in global memory
+  cluster_sync();  // final ids (and, sharded, the group's global winners) complete in global memory
   mark(M_S2SEL);
 
   // --------------------------------------------------------------- P13
@@ -1291,7 +1408,15 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       } else {
         const int r = it - dense;
         my_head = r / TOPK;
-        my_tok = __ldcg(fids + r);
+        if (w.link) {
+          // sharded: the group's global winners this shard holds (-2: another shard's)
+          const int gid = __ldcg(w.shard_gids + (size_t)cell * G * TOPK + r);
+          const int tok = gid - w.link->token_begin;
+          if (gid >= 0 && tok >= 0 && tok < T) my_tok = tok;
+          else my_head = -2;
+        } else {
+          my_tok = __ldcg(fids + r);
+        }
       }
     }
     auto record = [&](int j, uint2 &kb, uint2 &vb) {
@@ -1304,6 +1429,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 #pragma unroll 1
     for (int j = 0; j < nmine; ++j) {
       const int head = __shfl_sync(0xffffffffu, my_head, j);
+      if (head == -2) {  // (warp-uniform)
+        if (j + 1 < nmine) record(j + 1, kb, vb);
+        continue;
+      }
       float kf[8], vf[8];
       fp8x8(kb, kf);
       fp8x8(vb, vf);
@@ -1366,8 +1495,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     cluster_sync();
     mark(M_ATTN_CTA);
     // CTA `rank` finishes output dimensions [16 rank, 16 rank + 16) of the four heads
+    float M = -INFINITY, L = 0.0f, O = 0.0f;
+    const int hh = tid >> 4, dd = 16 * rank + (tid & 15);
     if (tid < G * 16) {
-      const int h = tid >> 4, d = 16 * rank + (tid & 15);
+      const int h = hh, d = dd;
       // the 16 CTA partials, all loads in flight at once, then the
       // log-sum-exp merge (log2 domain)
       float ms[CL], ls[CL], os[CL];
@@ -1377,10 +1508,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         ls[r] = ld_remote_f(remote(part + h * PART + 1, (uint32_t)r));
         os[r] = ld_remote_f(remote(part + h * PART + 4 + d, (uint32_t)r));
       }
-      float M = -INFINITY;
 #pragma unroll
       for (int r = 0; r < CL; ++r) M = fmaxf(M, ms[r]);
-      float L = 0.0f, O = 0.0f;
 #pragma unroll
       for (int r = 0; r < CL; ++r) {
         if (ms[r] == -INFINITY) continue;
@@ -1388,8 +1517,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         L += ls[r] * e;
         O += os[r] * e;
       }
-      w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
+      if (!w.link) w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
     }
+    if (w.link) shard_share(w, S, cell, rank, M, L, O, hh, dd, mark);
   }
   mark(M_ATTN);
   if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
@@ -1401,7 +1531,8 @@ const char *const kMarkNames[M_NTAGS] = {
     "select_histogram", "select_barrier", "select_readback", "coarse_select", "survivors",
     "fine_gather", "fine", "fine_select", "selected_list", "selected_exchange", "pool_keep", "pool",
     "s15_gather", "s15_score", "s15_select", "u15_union", "s16_score", "s16_select", "candidates",
-    "s2_score", "s2_select", "attn_items", "attn_cta", "attention"};
+    "s2_score", "s2_select", "attn_items", "attn_cta", "attention", "shard_list_exchange",
+    "shard_share_exchange"};
 
 }  // namespace
 

@@ -225,29 +225,6 @@ __global__ void __launch_bounds__(256) k_shard_combine(const float *partials, in
 // Waits are bounded: after SHARD_WAIT_POLLS polls the step's status word gets
 // ST_TIMEOUT and the kernel carries on with whatever arrived.
 
-constexpr long long SHARD_WAIT_POLLS = 1 << 24;  // ~1.6 s at 100 ns per poll
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Waits (thread 0) until flag[s] >= epoch for every shard s; false on timeout.
-__device__ bool wait_flags(const uint32_t *flag, int stride, int n_shards, uint32_t epoch) {
-  for (int s = 0; s < n_shards; ++s) {
-    long long polls = 0;
-    while (ld_acquire_sys(flag + (size_t)s * stride) < epoch) {
-      if (++polls > SHARD_WAIT_POLLS) return false;
-      __nanosleep(100);
-    }
-  }
-  return true;
-}
-
 // One CTA per (cell, head): push this shard's list to every peer's slot
 // `rank`, signal, wait for every shard's list of this (cell, head), merge.
 __global__ void __launch_bounds__(MERGE_THREADS) k_shard_merge_p2p(ShardLinkDev L, const uint32_t *keys,
@@ -268,7 +245,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_shard_merge_p2p(ShardLinkDev 
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence_system();
+    __threadfence_system();  // cumulative over the CTA's pushes
     for (int p = 0; p < n; ++p) st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_lists[L.rank][ch], epoch);
     const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
     s_ok = wait_flags(&mine->flag_lists[0][ch], SHARD_CELLS * G, n, epoch);
@@ -311,7 +288,7 @@ __global__ void __launch_bounds__(256) k_shard_combine_p2p(ShardLinkDev L, const
   }
   __syncthreads();
   if (d == 0) {
-    __threadfence_system();
+    __threadfence_system();  // cumulative over the CTA's pushes
     for (int p = 0; p < n; ++p) st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_parts[L.rank][cell], epoch);
     const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
     s_ok = wait_flags(&mine->flag_parts[0][cell], SHARD_CELLS, n, epoch);
@@ -334,7 +311,7 @@ __global__ void __launch_bounds__(256) k_shard_combine_p2p(ShardLinkDev L, const
   }
 }
 
-__global__ void k_shard_epoch(ShardLinkDev L) { *L.epoch += 1; }
+__global__ void k_shard_epoch(const ShardLinkDev *L) { *L->epoch += 1; }
 
 }  // namespace
 
@@ -364,7 +341,11 @@ cudaError_t launch_shard_p2p_step(const Work &w, const ShardLinkDev &L, int32_t 
   k_shard_merge_p2p<<<SHARD_CELLS * G, MERGE_THREADS, 0, st>>>(L, w.final_keys, w.final_ids, gids, status);
   k_shard_attn<<<dim3(ATTN_SPLIT, SHARD_CELLS), 256, 0, st>>>(w, gids, L.token_begin, part);
   k_shard_combine_p2p<<<SHARD_CELLS, 256, 0, st>>>(L, part, w.out, status);
-  k_shard_epoch<<<1, 1, 0, st>>>(L);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_shard_epoch(const ShardLinkDev *dlink, cudaStream_t st) {
+  k_shard_epoch<<<1, 1, 0, st>>>(dlink);
   return cudaGetLastError();
 }
 
