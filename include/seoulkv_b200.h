@@ -207,17 +207,22 @@ int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, 
 int skv_shard_combine(const float *partials, int32_t n_shards, int32_t n_cells, uint16_t *out, void *stream);
 
 /* Sequence-sharded group over peer memory (NVLink), without a collective
- * library: skv_shard_setup allocates this shard's exchange region (one slot,
- * n_shards <= 8; begin = host array of every shard's first global token) and
- * writes its 64-byte CUDA IPC handle to ipc_handle; after the caller has
- * moved every shard's handle to every shard, skv_shard_connect (handles =
- * n_shards x 64 bytes in shard order) maps the peers' regions.  From then on
- * every skv_run is the whole layer step: the funnel, then each shard writes
- * its top-100 lists and its attention partials straight into every peer's
- * region and waits (bounded; SKV_STATUS_TIMEOUT on expiry) for the others',
- * so skv_output gives the layer's BF16 output on every shard.  All shards
- * must call skv_run once per step. */
-int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t *begin, void *ipc_handle);
+ * library.  skv_shard_setup (after skv_upload_kv; one slot, n_shards <= 8;
+ * begin = host array of every shard's first global token; total / sink /
+ * local = the whole layer's context and dense zones) allocates this shard's
+ * exchange region and writes skv_shard_ipc_handle_bytes() bytes of CUDA IPC
+ * handles (the region and the four FP8 record buffers) to ipc_handles; after
+ * the caller has moved every shard's handles to every shard,
+ * skv_shard_connect (n_shards x that many bytes, in shard order) maps the
+ * peers' memory.  From then on every skv_run is the whole layer step: the
+ * funnel; every shard writes its top-100 lists straight into every peer's
+ * region and waits (bounded; SKV_STATUS_TIMEOUT on expiry) for the others';
+ * the merged global winners and the dense zones are attended with their
+ * records read from the owning shard's memory, so skv_output gives the
+ * layer's BF16 output on every shard.  All shards must call skv_run once per
+ * step. */
+int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t *begin, int32_t total,
+                    int32_t sink, int32_t local, void *ipc_handles);
 int skv_shard_connect(void *handle, const void *ipc_handles);
 int32_t skv_shard_ipc_handle_bytes(void);
 /* Device address of the connected group's global winners [4][4][100]

@@ -125,7 +125,7 @@ def load() -> ctypes.CDLL:
         lib.skv_shard_combine.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                           ctypes.c_void_p]
         lib.skv_shard_setup.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
-                                        ctypes.c_void_p]
+                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
         lib.skv_shard_connect.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.skv_shard_ipc_handle_bytes.restype = ctypes.c_int32
         lib.skv_shard_gids.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
@@ -271,12 +271,13 @@ class Engine:
                                            ctypes.c_void_p(partials), ctypes.c_void_p(stream or None)),
               "skv_shard_attention")
 
-    def shard_setup(self, rank: int, n_shards: int, begin: list[int]) -> bytes:
-        """Allocate this shard's peer-exchange region; returns its IPC handle."""
+    def shard_setup(self, rank: int, n_shards: int, begin: list[int], total: int, sink: int, local: int) -> bytes:
+        """Allocate this shard's peer-exchange region; returns its IPC handles (region + FP8 records)."""
         nb = int(self.lib.skv_shard_ipc_handle_bytes())
         h = ctypes.create_string_buffer(nb)
         b = np.asarray(begin, dtype=np.int32)
-        check(self.lib.skv_shard_setup(self.handle, rank, n_shards, _ptr(b), h), "skv_shard_setup")
+        check(self.lib.skv_shard_setup(self.handle, rank, n_shards, _ptr(b), total, sink, local, h),
+              "skv_shard_setup")
         return h.raw
 
     def shard_gids_ptr(self) -> int:

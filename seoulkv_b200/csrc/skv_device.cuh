@@ -48,7 +48,6 @@ constexpr uint32_t ST_POOL_OVER = 1u, ST_POOL_UNDER = 2u, ST_FINE_SHORT = 4u, ST
 // ---- sequence-sharded group over peer memory (one slot of 4 cells per shard)
 constexpr int SHARD_MAX = 8;    // shards of a peer-memory group
 constexpr int SHARD_CELLS = 4;  // one slot: 4 KV heads
-constexpr int SHARD_CTAS = 16;  // CTAs of a fused cluster (one output-dimension share each)
 
 // The exchange region every shard owns and every peer writes into.
 struct ShardRegion {
@@ -57,14 +56,15 @@ struct ShardRegion {
   float part[SHARD_MAX][SHARD_CELLS][G][PART];            // [source shard][cell][head][m, l, 0, 0, o]
   uint32_t flag_lists[SHARD_MAX][SHARD_CELLS * G];        // epoch of each source's (cell, head) list
   uint32_t flag_parts[SHARD_MAX][SHARD_CELLS];            // epoch of each source's cell partials
-  uint32_t flag_share[SHARD_MAX][SHARD_CELLS * SHARD_CTAS];  // ... of each source's (cell, dim share)
 };
 
 // Kernel-side view of a connected group.
 struct ShardLinkDev {
   void *peer[SHARD_MAX];          // every shard's region as mapped here (own one included)
+  const uint8_t *kv8[SHARD_MAX][SHARD_CELLS];  // every shard's FP8 [K|V] records as mapped here
   int32_t begin[SHARD_MAX];       // first global token of each shard
   int32_t rank, n_shards, token_begin;
+  int32_t total, sink, local;     // the whole layer's context and dense zones
   uint32_t *epoch;                // steps completed (device counter)
 };
 

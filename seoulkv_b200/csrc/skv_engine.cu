@@ -69,6 +69,8 @@ struct Engine {
     int32_t begin[SHARD_MAX] = {};
     void *region = nullptr;              // this shard's exchange region
     void *opened[SHARD_MAX] = {};        // peers' regions mapped here (IPC)
+    void *kv8[SHARD_MAX][SHARD_CELLS] = {};  // peers' FP8 records mapped here (IPC)
+    int32_t total = 0, sink = 0, local = 0;
     uint32_t *epoch = nullptr;
     int32_t *gids = nullptr;             // [4][4][100] global winners
     float *part = nullptr;               // [4][4][PART] this shard's partials
@@ -80,6 +82,12 @@ ShardLinkDev link_view(const Engine *e) {
   ShardLinkDev L{};
   for (int p = 0; p < e->link.n; ++p) L.peer[p] = p == e->link.rank ? e->link.region : e->link.opened[p];
   for (int p = 0; p < e->link.n; ++p) L.begin[p] = e->link.begin[p];
+  for (int p = 0; p < e->link.n; ++p)
+    for (int c = 0; c < SHARD_CELLS; ++c)
+      L.kv8[p][c] = static_cast<const uint8_t *>(p == e->link.rank ? (void *)e->bufs[c].kv8 : e->link.kv8[p][c]);
+  L.total = e->link.total;
+  L.sink = e->link.sink;
+  L.local = e->link.local;
   L.rank = e->link.rank;
   L.n_shards = e->link.n;
   L.token_begin = e->link.begin[e->link.rank];
@@ -275,6 +283,9 @@ void skv_destroy(void *handle) {
   if (e->ran && e->done) cudaEventSynchronize(e->done);
   for (void *p : e->link.opened)
     if (p) cudaIpcCloseMemHandle(p);
+  for (auto &row : e->link.kv8)
+    for (void *p : row)
+      if (p) cudaIpcCloseMemHandle(p);
   if (e->link.region) cudaFree(e->link.region);
   if (e->exec) cudaGraphExecDestroy(e->exec);
   if (e->graph) cudaGraphDestroy(e->graph);
@@ -658,15 +669,23 @@ int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, 
   return SKV_OK;
 }
 
-int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t *begin, void *ipc_handle) {
+int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t *begin, int32_t total, int32_t sink,
+                    int32_t local, void *ipc_handles) {
   Engine *e = as_engine(handle);
-  if (!e || !begin || !ipc_handle) return fail(SKV_E_INVALID, "null engine or buffer");
+  if (!e || !begin || !ipc_handles) return fail(SKV_E_INVALID, "null engine or buffer");
   if (n_shards < 1 || n_shards > SHARD_MAX || rank < 0 || rank >= n_shards)
     return fail(SKV_E_INVALID, "rank / n_shards out of range (at most 8 shards)");
   if (e->n_cells != SHARD_CELLS) return fail(SKV_E_INVALID, "a shard engine holds one slot");
   if (e->link.region) return fail(SKV_E_STATE, "shard group already set up");
+  for (int c = 0; c < SHARD_CELLS; ++c)
+    if (!e->kv_ok[c]) return fail(SKV_E_STATE, "upload K/V before skv_shard_setup");
+  if (sink < 0 || local < 0 || sink + local > total || begin[0] != 0)
+    return fail(SKV_E_INVALID, "inconsistent layer context / zones");
   CK(cudaSetDevice(e->desc.device));
   for (int p = 0; p < n_shards; ++p) e->link.begin[p] = begin[p];
+  e->link.total = total;
+  e->link.sink = sink;
+  e->link.local = local;
   e->link.rank = rank;
   e->link.n = n_shards;
   CK(cudaMalloc(&e->link.region, shard_region_bytes()));
@@ -675,9 +694,15 @@ int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t 
   if (!rc) rc = dalloc(e, &e->link.gids, (size_t)SHARD_CELLS * G * TOPK);
   if (!rc) rc = dalloc(e, &e->link.part, (size_t)SHARD_CELLS * G * PART);
   if (rc) return rc;
+  // the exchange region, then the four FP8 record buffers
   cudaIpcMemHandle_t h;
+  char *out = static_cast<char *>(ipc_handles);
   CK(cudaIpcGetMemHandle(&h, e->link.region));
-  std::memcpy(ipc_handle, &h, sizeof(h));
+  std::memcpy(out, &h, sizeof(h));
+  for (int c = 0; c < SHARD_CELLS; ++c) {
+    CK(cudaIpcGetMemHandle(&h, e->bufs[c].kv8));
+    std::memcpy(out + (size_t)(1 + c) * sizeof(h), &h, sizeof(h));
+  }
   return SKV_OK;
 }
 
@@ -690,8 +715,13 @@ int skv_shard_connect(void *handle, const void *ipc_handles) {
   for (int p = 0; p < e->link.n; ++p) {
     if (p == e->link.rank) continue;
     cudaIpcMemHandle_t h;
-    std::memcpy(&h, static_cast<const char *>(ipc_handles) + (size_t)p * sizeof(h), sizeof(h));
+    const char *in = static_cast<const char *>(ipc_handles) + (size_t)p * (1 + SHARD_CELLS) * sizeof(h);
+    std::memcpy(&h, in, sizeof(h));
     CK(cudaIpcOpenMemHandle(&e->link.opened[p], h, cudaIpcMemLazyEnablePeerAccess));
+    for (int c = 0; c < SHARD_CELLS; ++c) {
+      std::memcpy(&h, in + (size_t)(1 + c) * sizeof(h), sizeof(h));
+      CK(cudaIpcOpenMemHandle(&e->link.kv8[p][c], h, cudaIpcMemLazyEnablePeerAccess));
+    }
   }
   CK(cudaDeviceSynchronize());
   if (!e->link.dev) {
@@ -707,7 +737,7 @@ int skv_shard_connect(void *handle, const void *ipc_handles) {
   return SKV_OK;
 }
 
-int32_t skv_shard_ipc_handle_bytes(void) { return (int32_t)sizeof(cudaIpcMemHandle_t); }
+int32_t skv_shard_ipc_handle_bytes(void) { return (int32_t)((1 + SHARD_CELLS) * sizeof(cudaIpcMemHandle_t)); }
 
 int skv_shard_gids(void *handle, const int32_t **gids) {
   Engine *e = as_engine(handle);

@@ -124,8 +124,7 @@ static_assert(kSmemBytes <= 227 * 1024, "fused shared memory exceeds 227 KB");
 enum MarkTag {
   M_START, M_ISSUE, M_QEXP, M_QPREP, M_STARTED, M_SLICE, M_COARSE, M_HIST, M_SYNC, M_READ, M_CSEL,
   M_SURV, M_FGATHER, M_FINE, M_FSEL, M_SELLIST, M_SELX, M_KEEP, M_POOL, M_S15G, M_S15, M_S15SEL,
-  M_U15, M_S16, M_S16SEL, M_CAND, M_S2, M_S2SEL, M_ATTN_ITEMS, M_ATTN_CTA, M_ATTN, M_XLIST, M_XSHARE,
-  M_NTAGS
+  M_U15, M_S16, M_S16SEL, M_CAND, M_S2, M_S2SEL, M_ATTN_ITEMS, M_ATTN_CTA, M_ATTN, M_XLIST, M_NTAGS
 };
 
 struct Marker {
@@ -638,49 +637,6 @@ __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, 
   int total;
   block_exclusive_scan(valid, &total);
   for (int i = total + tid; i < TOPK; i += FT) gout[i] = -1;  // fewer than 100 candidates in the group
-}
-
-// Sharded attention combine: this CTA's share (dimensions [16 r, 16 r + 16)
-// of the four heads, threads tid < 64 holding (M, L, O) of head tid / 16)
-// of this shard's partial goes to every peer, then the shards' shares of the
-// same dimensions are merged by log-sum-exp into the BF16 output.
-__device__ __noinline__ void shard_share(const Work &w, FusedSmem &S, int cell, int r, float M, float L, float O,
-                                         int h, int d, Marker &mark) {
-  const ShardLinkDev &L_ = *w.link;
-  const int tid = threadIdx.x, n = L_.n_shards, fs = cell * SHARD_CTAS + r;
-  const uint32_t epoch = *L_.epoch + 1;
-  if (tid < G * 16) {
-    for (int p = 0; p < n; ++p) {
-      float *dst = reinterpret_cast<ShardRegion *>(L_.peer[p])->part[L_.rank][cell][h];
-      dst[4 + d] = O;
-      if ((tid & 15) == 0) { dst[0] = M; dst[1] = L; }
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence_system();  // cumulative over the CTA's pushes
-    for (int p = 0; p < n; ++p)
-      st_release_sys(&reinterpret_cast<ShardRegion *>(L_.peer[p])->flag_share[L_.rank][fs], epoch);
-    const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L_.peer[L_.rank]);
-    if (!wait_flags(&mine->flag_share[0][fs], SHARD_CELLS * SHARD_CTAS, n, epoch))
-      atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
-  }
-  __syncthreads();
-  mark(M_XSHARE);
-  if (tid < G * 16) {
-    const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L_.peer[L_.rank]);
-    float Mx = -INFINITY;
-    for (int s = 0; s < n; ++s) Mx = fmaxf(Mx, __ldcv(&R->part[s][cell][h][0]));
-    float Ls = 0.0f, Os = 0.0f;
-    for (int s = 0; s < n; ++s) {
-      const float m = __ldcv(&R->part[s][cell][h][0]);
-      if (m == -INFINITY) continue;
-      const float e = exp2f(m - Mx);
-      Ls += __ldcv(&R->part[s][cell][h][1]) * e;
-      Os += __ldcv(&R->part[s][cell][h][4 + d]) * e;
-    }
-    w.out[((size_t)(cell >> 2) * 16 + (cell & 3) * 4 + h) * D + d] = bf16_rne(Os / Ls);
-  }
 }
 
 // ------------------------------------------------------------ the kernel
@@ -1376,7 +1332,11 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // --------------------------------------------------------------- P13
   {
-    const int sink = w.sink, local = w.local, T = w.T, dense = sink + local;
+    // sharded (Work::link): the whole layer's zones and global token ids; the
+    // records come from the owning shard's memory (plain loads over NVLink)
+    const ShardLinkDev *Lk = w.link;
+    const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local, T = Lk ? Lk->total : w.T;
+    const int dense = sink + local;
     const int nitems = dense + G * TOPK;
     const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
     float qv[G][8];
@@ -1408,11 +1368,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       } else {
         const int r = it - dense;
         my_head = r / TOPK;
-        if (w.link) {
-          // sharded: the group's global winners this shard holds (-2: another shard's)
+        if (Lk) {
+          // sharded: the group's global winners (-2: fewer than 100 in the group)
           const int gid = __ldcg(w.shard_gids + (size_t)cell * G * TOPK + r);
-          const int tok = gid - w.link->token_begin;
-          if (gid >= 0 && tok >= 0 && tok < T) my_tok = tok;
+          if (gid >= 0) my_tok = gid;
           else my_head = -2;
         } else {
           my_tok = __ldcg(fids + r);
@@ -1420,7 +1379,15 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       }
     }
     auto record = [&](int j, uint2 &kb, uint2 &vb) {
-      const uint8_t *rec = c.kv8 + (size_t)__shfl_sync(0xffffffffu, my_tok, j) * REC;
+      const int tok = __shfl_sync(0xffffffffu, my_tok, j);
+      const uint8_t *rec;
+      if (Lk) {
+        int s = 0;
+        while (s + 1 < Lk->n_shards && Lk->begin[s + 1] <= tok) ++s;
+        rec = Lk->kv8[s][cell] + (size_t)(tok - Lk->begin[s]) * REC;
+      } else {
+        rec = c.kv8 + (size_t)tok * REC;
+      }
       kb = *reinterpret_cast<const uint2 *>(rec + 8 * lane);
       vb = *reinterpret_cast<const uint2 *>(rec + 256 + 8 * lane);
     };
@@ -1496,9 +1463,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     mark(M_ATTN_CTA);
     // CTA `rank` finishes output dimensions [16 rank, 16 rank + 16) of the four heads
     float M = -INFINITY, L = 0.0f, O = 0.0f;
-    const int hh = tid >> 4, dd = 16 * rank + (tid & 15);
     if (tid < G * 16) {
-      const int h = hh, d = dd;
+      const int h = tid >> 4, d = 16 * rank + (tid & 15);
       // the 16 CTA partials, all loads in flight at once, then the
       // log-sum-exp merge (log2 domain)
       float ms[CL], ls[CL], os[CL];
@@ -1517,9 +1483,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         L += ls[r] * e;
         O += os[r] * e;
       }
-      if (!w.link) w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
+      w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
     }
-    if (w.link) shard_share(w, S, cell, rank, M, L, O, hh, dd, mark);
   }
   mark(M_ATTN);
   if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
@@ -1531,8 +1496,7 @@ const char *const kMarkNames[M_NTAGS] = {
     "select_histogram", "select_barrier", "select_readback", "coarse_select", "survivors",
     "fine_gather", "fine", "fine_select", "selected_list", "selected_exchange", "pool_keep", "pool",
     "s15_gather", "s15_score", "s15_select", "u15_union", "s16_score", "s16_select", "candidates",
-    "s2_score", "s2_select", "attn_items", "attn_cta", "attention", "shard_list_exchange",
-    "shard_share_exchange"};
+    "s2_score", "s2_select", "attn_items", "attn_cta", "attention", "shard_list_exchange"};
 
 }  // namespace
 

@@ -154,7 +154,8 @@ class ShardedSeoulKV4:
             # the engine now, so that its step graph is captured with the exchange kernels
             self.attn._engine = self.attn._initialize()
             self.attn._host_kv = None
-            mine = self.attn._engine.shard_setup(plan.shard, n, [r * plan.total // n for r in range(n)])
+            mine = self.attn._engine.shard_setup(plan.shard, n, [r * plan.total // n for r in range(n)],
+                                                 plan.total, plan.sink, plan.local)
             handles = [mine]
             if n > 1:
                 handles = [None] * n
