@@ -76,6 +76,26 @@ def test_single_shard_equals_plain_decode(cuda):
     _check_out(bits(got).reshape(16, 256), bits(want).reshape(16, 256))
 
 
+def test_single_shard_group_over_peer_memory(cuda):
+    """The in-kernel exchange path (a one-shard group maps only itself) equals the plain decode."""
+    plan = ShardPlan(8192, 1, 0)
+    case = ShardCase(plan)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as plain:
+        outs, ids = [], []
+        for s in (11, 12, 13):
+            q = synthetic.make_query(plan.total, case.mixes, seed=s)
+            outs.append(plain.run(q).to_torch())
+            ids.append(plain.debug_snapshot()["selected_ids"])
+    with ShardedSeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, plan=plan, transport="p2p") as sh:
+        assert sh.attn._engine.fused
+        for i, s in enumerate((11, 12, 13)):  # several steps: the per-step flags advance
+            q = synthetic.make_query(plan.total, case.mixes, seed=s)
+            got = sh.run(q).cpu()
+            assert torch.equal(sh.selected_ids().cpu().long(), ids[i])
+            _check_out(bits(got).reshape(16, 256), bits(outs[i]).reshape(16, 256))
+        sh.attn.synchronize()  # status: no exchange timed out
+
+
 def test_merge_rejects_bad_shapes(cuda):
     x = torch.zeros(11, 4, 4, 100, dtype=torch.int32, device=cuda)
     g = torch.zeros(4, 4, 100, dtype=torch.int32, device=cuda)
