@@ -13,6 +13,7 @@
 #pragma once
 #include <climits>
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 namespace skv {
@@ -185,10 +186,34 @@ __device__ __forceinline__ uint32_t *hist_of(const Work &w, int cell, int stage,
 // 2^e as a double, e in the normal range.
 __device__ __forceinline__ double pow2d(int e) { return __hiloint2double((e + 1023) << 20, 0); }
 
-// Exact digit sum -> FP32 score input (one rounding).
-__device__ __forceinline__ float exact_to_float(long long dsum, double scale) {
-  return __double2float_rn(__ll2double_rn(dsum) * scale);
+// Scale 2^e of an exact digit sum, in the two forms exact_to_float uses.
+struct Pow2 {
+  double d;
+  float f;
+  bool fast;  // 2^e is a normal FP32 number and no 64-bit sum scaled by it overflows
+};
+__device__ __forceinline__ Pow2 pow2s(int e) {
+  Pow2 p;
+  p.d = pow2d(e);
+  p.fast = e >= -126 && e <= 64;
+  p.f = p.fast ? __int_as_float((e + 127) << 23) : 0.0f;
+  return p;
 }
+
+// Exact digit sum -> FP32 score input, rounded once to nearest even.
+// dsum * 2^e is exact in double (|dsum| < 2^53); when 2^e is a normal FP32
+// number every non-zero result is normal (|dsum| >= 1) and finite
+// (|dsum| < 2^63, e <= 64), and rounding dsum to FP32 first and scaling by
+// 2^e afterwards is the same single rounding: one 64-bit integer conversion
+// instead of three double-precision operations.
+__device__ __forceinline__ float exact_to_float(long long dsum, const Pow2 &s) {
+  return s.fast ? __fmul_rn(__ll2float_rn(dsum), s.f) : __double2float_rn(__ll2double_rn(dsum) * s.d);
+}
+
+// BF16 round-to-nearest-even of a finite score by the conversion
+// instruction; equal to bf16_rne for every non-NaN input (scores computed from
+// exact digit sums are never NaN).
+__device__ __forceinline__ uint16_t bf16_score(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 
 // ------------------------------------------------------ tensor-core dots
 
@@ -227,12 +252,14 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
 __device__ __forceinline__ void combine_digits(const int (&acc)[2][4], int t, long long (&d)[2]) {
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
-    long long pg = (long long)acc[nt][0] + 256LL * acc[nt][1];
-    long long p8 = (long long)acc[nt][2] + 256LL * acc[nt][3];
-    if (t & 1) { pg *= 65536LL; p8 *= 65536LL; }
-    pg += __shfl_xor_sync(0xffffffffu, pg, 1);
-    p8 += __shfl_xor_sync(0xffffffffu, p8, 1);
-    d[nt] = (t & 1) ? p8 : pg;
+    // this lane's digit pair for rows g and g + 8 (|acc| < 2^19, so the pair
+    // sums fit 32 bits); even lanes hold digits 0-1 (weights 1, 256), odd
+    // lanes digits 2-3 (65536, 2^24); the even lane finishes row g, the odd
+    // lane row g + 8, each with one 32-bit value from its partner
+    const int pg = acc[nt][0] + 256 * acc[nt][1];
+    const int p8 = acc[nt][2] + 256 * acc[nt][3];
+    const int x = __shfl_xor_sync(0xffffffffu, (t & 1) ? pg : p8, 1);
+    d[nt] = (t & 1) ? (long long)p8 * 65536LL + x : (long long)pg + (long long)x * 65536LL;
   }
 }
 

@@ -76,6 +76,7 @@ enum Pub { P_SURV = 0, P_SEL = 1, P_POOL = 2, P_U15 = 3, P_CAND = 4 };
 struct SelCtl {
   uint32_t prefix[4], mask[4], krem[4], th[4];
   int done[4];
+  int own[4];    // this CTA holds the cluster's K-th largest key (its threshold is the global one)
 };
 
 struct FusedSmem {
@@ -83,6 +84,7 @@ struct FusedSmem {
   uint32_t hist[4 * 256];          // local histograms (selection rounds alternate with hist2)
   uint32_t hist2[4 * 256];
   alignas(16) uint32_t red[3][64]; // bins this CTA owns (three rotating buffers)
+  uint32_t tab[CL][64];            // the owned bins' counts per source CTA (last round of a 32-bit selection)
   unsigned long long mbar[NCHUNK];
   int pub[NPUB][4];                // values published to the cluster
   int all[CL][4];                  // the cluster's values of the latest exchange
@@ -327,38 +329,19 @@ __device__ __forceinline__ uint32_t select_key(const FusedSmem &S, int kind, int
 
 // One radix-histogram pass over this CTA's keys of `KIND`: keys with
 // (key & mk[h]) == pf[h] add one to bin h*256 + digit (bits sh..sh+7).
-// Run-length counting: a thread counts its current bin per head in a
-// register and adds it when the bin changes and at the end (the warp's lanes
-// on lane 0's bin in one atomic); selection keys crowd into few bins, where
-// per-key shared atomics from all warps serialise.
+// One shared-memory atomic per key: measured on B200 with BF16-like keys
+// crowded into a few bins, this is faster than run-length counting in
+// registers or per-warp aggregation (the atomic unit combines lanes of one
+// instruction that hit the same address).
 template <int KIND>
 __device__ __forceinline__ void hist_pass(uint32_t *hist, const FusedSmem &S, int nloc, int q0,
                                           const uint32_t (&pf)[4], const uint32_t (&mk)[4], int sh) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  uint32_t cur[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu}, run[4] = {0u, 0u, 0u, 0u};
 #pragma unroll 1
-  for (int i = tid; i < nloc; i += FT) {
+  for (int i = threadIdx.x; i < nloc; i += FT) {
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       const uint32_t v = select_key(S, KIND, h, i, q0);
-      if ((v & mk[h]) != pf[h]) continue;
-      const uint32_t bin = h * 256 + ((v >> sh) & 255u);
-      if (bin != cur[h]) {
-        if (run[h]) atomicAdd(&hist[cur[h]], run[h]);
-        cur[h] = bin;
-        run[h] = 0u;
-      }
-      ++run[h];
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    const uint32_t b0 = __shfl_sync(0xffffffffu, cur[h], 0);
-    const uint32_t tot0 = __reduce_add_sync(0xffffffffu, cur[h] == b0 ? run[h] : 0u);
-    if (lane == 0) {
-      if (b0 != 0xffffffffu && tot0) atomicAdd(&hist[b0], tot0);
-    } else if (cur[h] != b0 && run[h]) {
-      atomicAdd(&hist[cur[h]], run[h]);
+      if ((v & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v >> sh) & 255u)], 1u);
     }
   }
 }
@@ -396,29 +379,47 @@ __device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t 
   return bal != 0;
 }
 
-// K-th largest of the cluster's keys (select_key of `kind`) for each of
-// the four heads; the top `nbits` bits of the 32-bit keys are significant.  On return S.ctl.th[h] holds, per head:
-//   exact:  the K-th largest key (all nbits resolved);
-//   !exact: a threshold t with exactly K keys >= t when keys are distinct
-//           (the K-th largest key, or the floor of its bin when the whole
-//           bin is taken), 0 when K exceeds the number of keys or the
-//           K-th largest key is 0; 0xffffffff when K == 0.
-// Contains one cluster barrier per 8-bit round (at most nbits / 8).
+// K-th largest of the cluster's keys (select_key of `kind`) for each of the
+// four heads; nbits (16 or 32) top bits of the 32-bit keys are significant.
+// On return S.ctl.th[h] holds a threshold: the keys >= it, over the whole
+// cluster, are
+//   exact (16 bits):  those >= the K-th largest key;
+//   !exact (32 bits): exactly the K largest keys (keys are distinct), and
+//                     th is 0 when K exceeds the number of keys or the K-th
+//                     largest key is 0, 0xffffffff when K == 0.
+// Two 8-bit radix rounds resolve the top 16 bits (for 32-bit keys the BF16
+// score).  Keys of 32 bits that share the boundary score are then resolved
+// by position, not by two more rounds: their low 16 bits order them by
+// position (KEY_FINE: ascending for a positive score, descending for a
+// negative one; KEY_S15 and KEY_S16: descending), and positions ascend with
+// the CTA rank, so the krem largest tied keys are the first krem tied keys
+// counted from the favoured end of the rank order.  In the second round
+// every CTA also stores its count of every bin into the bin owner's
+// per-source table; after the barrier the head's warp reads the boundary
+// bin's 16 per-source counts, takes this CTA's quota from the counts on the
+// favoured side, and the threshold is the quota-th largest of this CTA's own
+// tied keys (a ballot scan in local order).  The thresholds then differ
+// between CTAs but select the keys a global K-th largest key would;
+// S.ctl.own[h] marks the CTA whose threshold is the cluster's K-th largest
+// key.  One cluster barrier per round.
 __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, int nbits, bool exact, int kind,
                                             int q0, Marker &mark) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rank = (int)cluster_rank();
   if (tid < 4) {
     S.ctl.prefix[tid] = 0;
     S.ctl.mask[tid] = 0;
     S.ctl.krem[tid] = K;
     S.ctl.done[tid] = K == 0;
     S.ctl.th[tid] = K == 0 ? 0xffffffffu : 0u;
+    S.ctl.own[tid] = rank == 0;
   }
   for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
   __syncthreads();
   int r = 0;  // round of this selection: local histograms alternate between hist and hist2
-  for (int sh = 24; sh >= 32 - nbits; sh -= 8, ++r) {
+  for (int sh = 24; sh >= 16; sh -= 8, ++r) {
     if (S.ctl.done[0] && S.ctl.done[1] && S.ctl.done[2] && S.ctl.done[3]) break;
+    const bool ties = !exact && nbits == 32 && sh == 16;
     const int buf = S.round % 3, nbuf = (S.round + 1) % 3;
     uint32_t *lh = (r & 1) ? S.hist2 : S.hist, *other = (r & 1) ? S.hist : S.hist2;
     // the four heads in one pass (independent chains per thread); a
@@ -441,7 +442,9 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     mark(M_HIST);
     for (int e = tid; e < 4 * 256; e += FT) {
       const uint32_t c = lh[e];
-      if (c) red_remote(remote(&S.red[buf][e & 63], (uint32_t)(e >> 6)), c);
+      const uint32_t owner = (uint32_t)(e >> 6);
+      if (c) red_remote(remote(&S.red[buf][e & 63], owner), c);
+      if (ties) st_remote(remote(&S.tab[rank][e & 63], owner), c);
       other[e] = 0u;  // the next round's local histogram
     }
     cluster_sync();
@@ -456,20 +459,57 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
       int bin;
       uint32_t above, cnt;
       const bool found = warp_find_regs(c, S.ctl.krem[h], lane, bin, above, cnt);
+      const uint32_t pf = S.ctl.prefix[h] | ((uint32_t)bin << sh);
+      const uint32_t kr = S.ctl.krem[h] - above;
+      bool tie = false;
       if (lane == 0) {
         if (!found) {
           S.ctl.done[h] = 1;
           S.ctl.th[h] = 0u;
         } else {
-          const uint32_t pf = S.ctl.prefix[h] | ((uint32_t)bin << sh);
-          const uint32_t kr = S.ctl.krem[h] - above;
           S.ctl.prefix[h] = pf;
           S.ctl.mask[h] |= 255u << sh;
           S.ctl.krem[h] = kr;
           if (sh == 32 - nbits || (!exact && cnt == kr && pf != 0u)) {
             S.ctl.done[h] = 1;
             S.ctl.th[h] = pf;
+          } else if (ties) {
+            S.ctl.done[h] = 1;
+            S.ctl.th[h] = 0u;  // the K-th largest key is 0 (pf == 0); else set below
           }
+        }
+      }
+      tie = found && ties && !(cnt == kr && pf != 0u) && pf != 0u;  // warp-uniform
+      if (tie) {
+        const uint32_t B = pf >> 16;
+        const int e = h * 256 + bin;
+        const bool up = kind == KEY_FINE && (B & 0x8000u);  // low 16 bits ascend with the position
+        const uint32_t cq = lane < CL ? ld_remote(remote(&S.tab[lane][e & 63], (uint32_t)(e >> 6))) : 0u;
+        const uint32_t pre = __reduce_add_sync(0xffffffffu, (up ? lane > rank : lane < rank) ? cq : 0u);
+        const uint32_t n = __shfl_sync(0xffffffffu, cq, rank);
+        const uint32_t quota = kr > pre ? min(kr - pre, n) : 0u;
+        uint32_t th = quota == 0 ? (B + 1u) << 16 : B << 16;  // none / all of the tied keys
+        if (quota > 0 && quota < n) {
+          // the pick-th tied key of this CTA in local order
+          const uint32_t pick = up ? n - quota + 1 : quota;
+          uint32_t seen = 0;
+          for (int base = 0; base < nloc; base += 32) {
+            const int i = base + lane;
+            const uint32_t v = i < nloc ? select_key(S, kind, h, i, q0) : 0u;
+            const bool f = i < nloc && (v >> 16) == B;
+            const unsigned bal = __ballot_sync(0xffffffffu, f);
+            const bool me = f && seen + (uint32_t)__popc(bal & ((1u << lane) - 1u)) + 1u == pick;
+            const unsigned hit = __ballot_sync(0xffffffffu, me);
+            if (hit) {
+              th = __shfl_sync(0xffffffffu, v, __ffs(hit) - 1);
+              break;
+            }
+            seen += (uint32_t)__popc(bal);
+          }
+        }
+        if (lane == 0) {
+          S.ctl.th[h] = th;
+          S.ctl.own[h] = pre < kr && kr <= pre + n;
         }
       }
     }
@@ -797,7 +837,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   {
     BFrag F;
     load_frag(S, R_Q, lane, F);
-    const double scA = pow2d(S.shift[R_Q][hA]), scB = pow2d(S.shift[R_Q][hB]);
+    const Pow2 scA = pow2s(S.shift[R_Q][hA]), scB = pow2s(S.shift[R_Q][hB]);
     const float qnA = S.qscal[hA], qnB = S.qscal[hB], c3A = S.qscal[4 + hA], c3B = S.qscal[4 + hB];
     const int tiles = nrows >> 4;
     if (mark.ts && tiles > 0) {
@@ -819,8 +859,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         const float centered = __fsub_rn(__fmul_rn(2.0f, dot), k ? c3B : c3A);
         const float v = __fmul_rn(centered, sc4);
         const float margin = __fmul_rn(k ? qnB : qnA, rr);
-        const uint16_t lo = (uint16_t)ord16(bf16_rne(__fsub_rn(v, margin)));
-        const uint16_t hi = (uint16_t)ord16(bf16_rne(__fadd_rn(v, margin)));
+        const uint16_t lo = (uint16_t)ord16(bf16_score(__fsub_rn(v, margin)));
+        const uint16_t hi = (uint16_t)ord16(bf16_score(__fadd_rn(v, margin)));
         S.b.c.lo[h][lr] = lo;
         S.b.c.hi[h][lr] = hi;
         glo[(size_t)h * nc + row] = lo;
@@ -890,7 +930,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   {
     BFrag F;
     load_frag(S, R_Q, lane, F);
-    const double scA = pow2d(S.shift[R_Q][hA]), scB = pow2d(S.shift[R_Q][hB]);
+    const Pow2 scA = pow2s(S.shift[R_Q][hA]), scB = pow2s(S.shift[R_Q][hB]);
     for (int b0 = 0; b0 < nsurv; b0 += BATCH_FINE) {
       const int nb = min(BATCH_FINE, nsurv - b0);
       __syncthreads();
@@ -918,7 +958,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
             const int h = kk ? hB : hA;
             uint32_t key = 0;
             if ((mk >> h) & 1)
-              key = ord_fused(bf16_rne(__fmul_rn(exact_to_float(dsum[kk], kk ? scB : scA), fs)), (uint32_t)pos);
+              key = ord_fused(bf16_score(__fmul_rn(exact_to_float(dsum[kk], kk ? scB : scA), fs)), (uint32_t)pos);
             S.b.fkey[h][k] = key;
           }
         }
@@ -941,7 +981,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       tf[h] = S.ctl.th[h];
       if (tf[h] == 0u) { tf[h] = 0xffffffffu; st |= ST_FINE_SHORT; }
     }
-    if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_FINE * G + tid] = tf[tid];
+    if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_FINE * G + tid] = tf[tid];
     for (int k = tid; k < nsurv; k += FT) {
       bool s = false;
 #pragma unroll
@@ -1093,7 +1133,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       {
         BFrag F;
         load_frag(S, R_Q15, lane, F);
-        const double scA = pow2d(S.shift[R_Q15][hA]), scB = pow2d(S.shift[R_Q15][hB]);
+        const Pow2 scA = pow2s(S.shift[R_Q15][hA]), scB = pow2s(S.shift[R_Q15][hB]);
         for (int tile = warp; tile < tiles; tile += FW) {
           const int rg = tile * 16 + gq, r8 = rg + 8;
           long long dsum[2];
@@ -1104,14 +1144,14 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
           if (row < nb) {
 #pragma unroll
             for (int k = 0; k < 2; ++k)
-              S.b.p.sc15[k ? hB : hA][b0 + row] = (uint16_t)ord16(bf16_rne(exact_to_float(dsum[k], k ? scB : scA)));
+              S.b.p.sc15[k ? hB : hA][b0 + row] = (uint16_t)ord16(bf16_score(exact_to_float(dsum[k], k ? scB : scA)));
           }
         }
       }
       {
         BFrag F;
         load_frag(S, R_QS, lane, F);
-        const double s16A = pow2d(S.shift[R_QS][hA] + 4), s16B = pow2d(S.shift[R_QS][hB] + 4);
+        const Pow2 s16A = pow2s(S.shift[R_QS][hA] + 4), s16B = pow2s(S.shift[R_QS][hB] + 4);
         for (int tile = warp; tile < tiles; tile += FW) {
           const int rg = tile * 16 + gq, r8 = rg + 8;
           long long dh[2];
@@ -1123,7 +1163,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
               const int h = k ? hB : hA;
               // operand 16*qs, weights 2*c4 - 15: the same digits, scale 2^4 higher
               S.b.p.sc16[h][b0 + row] = (uint16_t)ord16(
-                  bf16_rne(exact_to_float(2 * dh[k] - 15 * S.sxsum[R_QS][h], k ? s16B : s16A)));
+                  bf16_score(exact_to_float(2 * dh[k] - 15 * S.sxsum[R_QS][h], k ? s16B : s16A)));
             }
           }
         }
@@ -1143,7 +1183,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     uint32_t tu[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) tu[h] = S.ctl.th[h] ? S.ctl.th[h] : 0xffffffffu;
-    if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_S15 * G + tid] = tu[tid];
+    if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_S15 * G + tid] = tu[tid];
     const int i0 = tid * 2;
     int f[2], cnt = 0;
 #pragma unroll
@@ -1189,7 +1229,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     uint32_t tc[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) tc[h] = S.ctl.th[h] ? S.ctl.th[h] : 0xffffffffu;
-    if (rank == 0 && tid < 4) w.thr[(size_t)cell * 16 + T_S16 * G + tid] = tc[tid];
+    if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_S16 * G + tid] = tc[tid];
     const int i0 = tid * 2;
     int f[2], cnt = 0;
 #pragma unroll
@@ -1226,7 +1266,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   {
     BFrag F;
     load_frag(S, R_QS, lane, F);
-    const double s2A = pow2d(S.shift[R_QS][hA]), s2B = pow2d(S.shift[R_QS][hB]);
+    const Pow2 s2A = pow2s(S.shift[R_QS][hA]), s2B = pow2s(S.shift[R_QS][hB]);
     for (int b0 = 0; b0 < ncl; b0 += BATCH_S2) {
       const int nb = min(BATCH_S2, ncl - b0);
       __syncthreads();
@@ -1254,7 +1294,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
             const int h = k ? hB : hA;
             // weights 2*code8 - 255 = 16*(2*c4 - 15) + (2*r4 - 15)
             const long long dsum = 32 * dh[k] + 2 * dl[k] - 255 * S.sxsum[R_QS][h];
-            const uint32_t key = (ord16(bf16_rne(exact_to_float(dsum, k ? s2B : s2A))) << 16) | (0xffffu - u);
+            const uint32_t key = (ord16(bf16_score(exact_to_float(dsum, k ? s2B : s2A))) << 16) | (0xffffu - u);
             st_remote(remote(k2 + cr, (uint32_t)h), key);
             st_remote(remote(t2 + cr, (uint32_t)h), (uint32_t)S.b.p.tok[i]);
           }
@@ -1283,7 +1323,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       __syncthreads();
 #pragma unroll
       for (int r = 0; r < 2; ++r)
-        hist_add_warp(S.hist, v[r] != 0u && (v[r] & mask) == prefix ? (v[r] >> sh) & 255u : 0xffffffffu);
+        if (v[r] != 0u && (v[r] & mask) == prefix) atomicAdd(&S.hist[(v[r] >> sh) & 255u], 1u);
       __syncthreads();
       if (warp == 0) {
         int bin;

@@ -111,8 +111,8 @@ __global__ void __launch_bounds__(256) k_coarse(Work w) {
   BFrag F;
   load_bfrag(w, cell, R_Q, lane, F);
   const int hA = t >> 1, hB = 2 + hA;
-  const double scA = pow2d(w.shift[(cell * 3 + R_Q) * G + hA]);
-  const double scB = pow2d(w.shift[(cell * 3 + R_Q) * G + hB]);
+  const Pow2 scA = pow2s(w.shift[(cell * 3 + R_Q) * G + hA]);
+  const Pow2 scB = pow2s(w.shift[(cell * 3 + R_Q) * G + hB]);
   const float qnA = w.qscal[cell * 8 + hA], qnB = w.qscal[cell * 8 + hB];
   const float c3A = w.qscal[cell * 8 + 4 + hA], c3B = w.qscal[cell * 8 + 4 + hB];
   const int tiles = nc >> 4, stride = gridDim.x * 8;
@@ -142,8 +142,8 @@ __global__ void __launch_bounds__(256) k_coarse(Work w) {
       const float centered = __fsub_rn(__fmul_rn(2.0f, dot), k ? c3B : c3A);
       const float v = __fmul_rn(centered, sc4);
       const float margin = __fmul_rn(k ? qnB : qnA, r);
-      const uint32_t lo = ord16(bf16_rne(__fsub_rn(v, margin)));
-      const uint32_t hi = ord16(bf16_rne(__fadd_rn(v, margin)));
+      const uint32_t lo = ord16(bf16_score(__fsub_rn(v, margin)));
+      const uint32_t hi = ord16(bf16_score(__fadd_rn(v, margin)));
       w.lo[((size_t)cell * G + h) * nc + row] = (uint16_t)lo;
       w.hi[((size_t)cell * G + h) * nc + row] = (uint16_t)hi;
     }
@@ -258,8 +258,8 @@ __global__ void __launch_bounds__(256) k_fine(Work w) {
   BFrag F;
   load_bfrag(w, cell, R_Q, lane, F);
   const int hA = t >> 1, hB = 2 + hA;
-  const double scA = pow2d(w.shift[(cell * 3 + R_Q) * G + hA]);
-  const double scB = pow2d(w.shift[(cell * 3 + R_Q) * G + hB]);
+  const Pow2 scA = pow2s(w.shift[(cell * 3 + R_Q) * G + hA]);
+  const Pow2 scB = pow2s(w.shift[(cell * 3 + R_Q) * G + hB]);
   for (int tile = warp; tile * 16 < total; tile += 8) {
     const int rg = tile * 16 + g, r8 = rg + 8;
     const int cg = rg < total ? s_cid[rg] : 0, c8 = r8 < total ? s_cid[r8] : 0;
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(256) k_fine(Work w) {
         const int h = k ? hB : hA;
         uint32_t key = 0;
         if ((mk >> h) & 1) {
-          key = ord_fused(bf16_rne(__fmul_rn(exact_to_float(dsum[k], k ? scB : scA), fs)), (uint32_t)pos);
+          key = ord_fused(bf16_score(__fmul_rn(exact_to_float(dsum[k], k ? scB : scA), fs)), (uint32_t)pos);
         }
         w.fkeys[((size_t)cell * G + h) * nc + pos] = key;
       }
@@ -539,8 +539,8 @@ __global__ void __launch_bounds__(SCHUNK) k_pool_s15(Work w) {
   BFrag F;
   load_bfrag(w, cell, R_Q15, lane, F);
   const int hA = t >> 1, hB = 2 + hA;
-  const double scA = pow2d(w.shift[(cell * 3 + R_Q15) * G + hA]);
-  const double scB = pow2d(w.shift[(cell * 3 + R_Q15) * G + hB]);
+  const Pow2 scA = pow2s(w.shift[(cell * 3 + R_Q15) * G + hA]);
+  const Pow2 scB = pow2s(w.shift[(cell * 3 + R_Q15) * G + hB]);
   for (int tile = warp; tile * 16 < nloc; tile += SCHUNK / 32) {
     const int rg = tile * 16 + g, r8 = rg + 8;
     const int tg = rg < nloc ? (rg < POOL_LIST ? s_tok[rg] : pool[base_kept + rg]) : 0;
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(SCHUNK) k_pool_s15(Work w) {
       const uint32_t pos = (uint32_t)(base_kept + row);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
-        const uint32_t sc = ord16(bf16_rne(exact_to_float(dsum[k], k ? scB : scA)));
+        const uint32_t sc = ord16(bf16_score(exact_to_float(dsum[k], k ? scB : scA)));
         const uint32_t key = (sc << 16) | (0xffffu - pos);
         w.k15[((size_t)cell * G + (k ? hB : hA)) * w.cap + pos] = key;
       }
@@ -611,8 +611,8 @@ __global__ void __launch_bounds__(256) k_s16(Work w) {
   BFrag F;
   load_bfrag(w, cell, R_QS, lane, F);
   const int hA = t >> 1, hB = 2 + hA;
-  const double scA = pow2d(w.shift[(cell * 3 + R_QS) * G + hA] + 4);
-  const double scB = pow2d(w.shift[(cell * 3 + R_QS) * G + hB] + 4);
+  const Pow2 scA = pow2s(w.shift[(cell * 3 + R_QS) * G + hA] + 4);
+  const Pow2 scB = pow2s(w.shift[(cell * 3 + R_QS) * G + hB] + 4);
   for (int tile = warp; tile * 16 < total; tile += 8) {
     const int rg = tile * 16 + g, r8 = rg + 8;
     const int tg = rg < total ? s_tok[rg] : 0, t8 = r8 < total ? s_tok[r8] : 0;
@@ -641,7 +641,7 @@ __global__ void __launch_bounds__(256) k_s16(Work w) {
         for (int k = 0; k < 2; ++k) {
           const int h = k ? hB : hA;
           // operand 16*qs: the same digits with the scale raised by 2^4
-          const uint32_t s = ord16(bf16_rne(exact_to_float(dsum[k], k ? scB : scA)));
+          const uint32_t s = ord16(bf16_score(exact_to_float(dsum[k], k ? scB : scA)));
           const uint32_t key = (s << 16) | (0xffffu - (uint32_t)u);
           w.k16[((size_t)cell * G + h) * U15_MAX + u] = key;
         }
@@ -695,8 +695,8 @@ __global__ void __launch_bounds__(256) k_s2_score(Work w) {
   BFrag F;
   load_bfrag(w, cell, R_QS, lane, F);
   const int hA = t >> 1, hB = 2 + hA;
-  const double scA = pow2d(w.shift[(cell * 3 + R_QS) * G + hA]);
-  const double scB = pow2d(w.shift[(cell * 3 + R_QS) * G + hB]);
+  const Pow2 scA = pow2s(w.shift[(cell * 3 + R_QS) * G + hA]);
+  const Pow2 scB = pow2s(w.shift[(cell * 3 + R_QS) * G + hB]);
   const int rg = warp * 16 + g, r8 = rg + 8;
   const int tg = rg < nloc ? s_tok[rg] : 0, t8 = r8 < nloc ? s_tok[r8] : 0;
   const uint2 *pg = reinterpret_cast<const uint2 *>(c.prefix2 + (size_t)tg * 64);
@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(256) k_s2_score(Work w) {
     for (int k = 0; k < 2; ++k) {
       // 2*code8 - 255 = 16*(2*c4 - 15) + (2*r4 - 15)
       const long long dsum = 16LL * dh[k] + dl[k];
-      const uint32_t s = ord16(bf16_rne(exact_to_float(dsum, k ? scB : scA)));
+      const uint32_t s = ord16(bf16_score(exact_to_float(dsum, k ? scB : scA)));
       w.k2[((size_t)cell * G + (k ? hB : hA)) * CAND_MAX + lo_rank + row] = (s << 16) | (0xffffu - u);
     }
   }
