@@ -26,7 +26,7 @@ EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
     "skv_upload_kv", "skv_bind_query", "skv_run", "skv_sync", "skv_status", "skv_output",
     "skv_debug_ids", "skv_read_stage", "skv_traffic", "skv_profile_step", "skv_kernel_name",
-    "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name",
+    "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name", "skv_profile_ctas",
     "skv_shard_outputs", "skv_shard_merge", "skv_shard_attention", "skv_shard_combine",
     "skv_shard_setup", "skv_shard_connect", "skv_shard_ipc_handle_bytes", "skv_shard_gids",
 )
@@ -115,6 +115,9 @@ def load() -> ctypes.CDLL:
         lib.skv_profile_phases.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
         lib.skv_phase_name.restype = ctypes.c_char_p
+        lib.skv_profile_ctas.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
+                                         ctypes.POINTER(ctypes.c_float)]
         lib.skv_phase_name.argtypes = [ctypes.c_int32]
         lib.skv_shard_outputs.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
                                           ctypes.POINTER(ctypes.c_void_p)]
@@ -259,6 +262,20 @@ class Engine:
         check(self.lib.skv_profile_phases(self.handle, ctypes.c_void_p(stream or None), _ptr(tags), _ptr(cyc),
                                           128, ctypes.byref(n)), "skv_profile_phases")
         return [(self.lib.skv_phase_name(int(tags[i])).decode(), float(cyc[i])) for i in range(n.value)]
+
+    def profile_ctas(self, stream: int = 0) -> tuple[np.ndarray, np.ndarray, float]:
+        """One fused launch: per-CTA (entry, exit) global-timer ns relative to
+        the earliest entry, shaped [cells, 16], and the launch's event time (µs)."""
+        cap = 16 * 1024
+        s = np.zeros(cap, dtype=np.int64)
+        e = np.zeros(cap, dtype=np.int64)
+        n = ctypes.c_int32()
+        ms = ctypes.c_float()
+        check(self.lib.skv_profile_ctas(self.handle, ctypes.c_void_p(stream or None), _ptr(s), _ptr(e), cap,
+                                        ctypes.byref(n), ctypes.byref(ms)), "skv_profile_ctas")
+        s, e = s[:n.value], e[:n.value]
+        t0 = s.min()
+        return (s - t0).reshape(-1, 16), (e - t0).reshape(-1, 16), ms.value * 1e3
 
     def shard_outputs(self, slot: int = 0) -> tuple[int, int]:
         """Device addresses of this engine's Stage-II keys and shard-local ids [4][4][100]."""

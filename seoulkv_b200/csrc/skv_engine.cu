@@ -62,6 +62,7 @@ struct Engine {
   cudaGraphExec_t exec = nullptr;
   bool fused = false;             // one cluster kernel per step (else the staged kernels)
   long long *phase_ts = nullptr;  // fused phase timestamps (skv_profile_phases)
+  long long *cta_ts = nullptr;    // per-CTA entry/exit times (skv_profile_ctas)
   // sequence-sharded group over peer memory (skv_shard_setup / skv_shard_connect)
   struct {
     bool active = false;
@@ -268,6 +269,7 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(dalloc(e, &w.out, (size_t)d->n_slots * 16 * D));
   TRY(dalloc(e, &e->phase_ts, 2 * FUSED_MARKS));
   w.phase_ts = nullptr;
+  w.cta_ts = nullptr;
   e->fused = !(d->flags & SKV_FLAG_STAGED) && fused_supported(w);
   if (e->fused) TRY(prepare_fused_attributes() ? fail(SKV_E_CUDA, "fused kernel attributes") : 0);
 #undef TRY
@@ -848,6 +850,48 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
     ++n;
   }
   *n_marks = n;
+  return SKV_OK;
+}
+
+int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end_ns, int32_t max_ctas,
+                     int32_t *n_ctas, float *kernel_ms) {
+  Engine *e = as_engine(handle);
+  if (!e || !start_ns || !end_ns || !n_ctas || !kernel_ms) return fail(SKV_E_INVALID, "null engine or output");
+  if (!e->fused) return fail(SKV_E_STATE, "CTA timing needs the fused path");
+  if (e->link.active) return fail(SKV_E_STATE, "CTA timing of a connected shard group is not supported");
+  int rc = ready(e);
+  if (rc) return rc;
+  CK(cudaSetDevice(e->desc.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nct = e->n_cells * 16;
+  if (!e->cta_ts) {
+    rc = dalloc(e, &e->cta_ts, 2 * (size_t)nct);
+    if (rc) return rc;
+  }
+  Work w = e->work;
+  w.cta_ts = e->cta_ts;
+  cudaEvent_t ev[2];
+  CK(cudaEventCreate(&ev[0]));
+  CK(cudaEventCreate(&ev[1]));
+  cudaEventRecord(ev[0], st);
+  cudaError_t le = launch_fused(w, st);
+  cudaEventRecord(ev[1], st);
+  std::vector<long long> ts(2 * (size_t)nct, 0);
+  cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(ev[1]) : le;
+  if (se == cudaSuccess) se = cudaEventElapsedTime(kernel_ms, ev[0], ev[1]);
+  if (se == cudaSuccess)
+    se = cudaMemcpy(ts.data(), e->cta_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  if (se != cudaSuccess) return fail(SKV_E_CUDA, std::string("profile ctas: ") + cudaGetErrorString(se));
+  CK(cudaEventRecord(e->done, st));
+  e->ran = true;
+  const int n = std::min<int>(nct, max_ctas);
+  for (int i = 0; i < n; ++i) {
+    start_ns[i] = ts[2 * i];
+    end_ns[i] = ts[2 * i + 1];
+  }
+  *n_ctas = n;
   return SKV_OK;
 }
 

@@ -61,8 +61,8 @@ constexpr int SLICE_CHUNK = 128;                  // rows per bulk copy (8 KB)
 constexpr int NCHUNK = PER_MAX / SLICE_CHUNK;     // mbarriers
 constexpr int POS_MAX = 1024;                     // pool positions per CTA
 constexpr int BIG = PER_MAX * 64;                 // staging area (128 KB)
-constexpr int NPUB = 8;                           // exchange slots
-constexpr long long WAIT_POLLS = 1 << 20;         // mbarrier polls before giving up
+constexpr long long WAIT_POLLS = 1 << 20;         // mbarrier polls before giving up (slice copies)
+constexpr long long XWAIT_POLLS = 1 << 16;        // polls before giving up on other CTAs' pushes
 
 // Row strides (bytes) of gathered rows in the staging area: 16 bytes of
 // padding keep the 8-byte fragment loads of a warp on distinct banks.
@@ -71,22 +71,30 @@ constexpr int STRIDE_S2 = 272;     // prefix2 | residual2 | residual4
 constexpr int BATCH_FINE = (BIG / STRIDE_FINE) & ~15;
 constexpr int BATCH_S2 = (BIG / STRIDE_S2) & ~15;
 
-enum Pub { P_SURV = 0, P_SEL = 1, P_POOL = 2, P_U15 = 3, P_CAND = 4 };
-
 struct SelCtl {
   uint32_t prefix[4], mask[4], krem[4], th[4];
   int done[4];
   int own[4];    // this CTA holds the cluster's K-th largest key (its threshold is the global one)
 };
 
+// A selection round's outcome for one head, pushed by the head's owner to
+// every CTA: the resolved prefix and remaining count, this CTA's threshold
+// and flags (bit 0 done, bit 1 this CTA holds the K-th largest key, bits
+// 8-19 the tied key to pick, 1-based in local order, 0 for none).
+struct SelRes {
+  uint32_t pf, kr, th, flags;
+};
+
 struct FusedSmem {
   uint32_t frag[3 * FRAG_ROW];     // int8 digit fragments of the three operand rows
-  uint32_t hist[4 * 256];          // local histograms (selection rounds alternate with hist2)
-  uint32_t hist2[4 * 256];
-  alignas(16) uint32_t red[3][64]; // bins this CTA owns (three rotating buffers)
-  uint32_t tab[CL][64];            // the owned bins' counts per source CTA (last round of a 32-bit selection)
+  uint32_t hist[4 * 256];          // this CTA's selection histogram (4 heads x 256 bins)
+  alignas(16) uint32_t tab[CL][128];  // CTA h < 4: each source CTA's counts of head h's bins (16-bit pairs)
+  uint32_t sum[256];               // CTA h < 4: head h's bins summed over the cluster
+  alignas(16) SelRes res[4];       // the owners' results of the latest selection round
+  alignas(16) int xin[2][CL][4];   // exchange slots (consecutive exchanges alternate)
   unsigned long long mbar[NCHUNK];
-  int pub[NPUB][4];                // values published to the cluster
+  unsigned long long mb_in, mb_res, mb_x[2];  // selection inputs (owners), results, exchanges
+  int ph_in, ph_res, ph_x, ph_pad; // phases of mb_in / mb_res / exchanges completed so far
   int all[CL][4];                  // the cluster's values of the latest exchange
   SelCtl ctl;
   int shift[3][4];
@@ -146,6 +154,11 @@ struct Marker {
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -182,26 +195,13 @@ __device__ __forceinline__ uint32_t remote(const void *p, uint32_t rank) {
 }
 // Remote loads carry no "memory" clobber, so that several can be in flight;
 // the cluster barriers (which do) keep them after the writes they read.
-__device__ __forceinline__ uint32_t ld_remote(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
 __device__ __forceinline__ float ld_remote_f(uint32_t a) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
-__device__ __forceinline__ uint4 ld_remote_v4(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
 __device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
-}
-__device__ __forceinline__ void red_remote(uint32_t a, uint32_t v) {
-  asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
 __device__ __forceinline__ void mbar_init(void *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
@@ -236,6 +236,36 @@ __device__ __noinline__ bool mbar_wait(void *bar, uint32_t parity) {
     if (mbar_try(bar, parity)) return true;
   return false;
 }
+// As mbar_try for a phase that other CTAs' asynchronous stores complete: the
+// acquire at cluster scope makes their data visible to this thread.
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait of every thread of the CTA for such a phase; a wait that runs
+// out records ST_TIMEOUT in the CTA's status and returns.
+__device__ __noinline__ void mbar_wait_cluster(void *bar, uint32_t parity, int *status) {
+  const uint32_t a = smem_addr(bar);
+  for (long long i = 0; i < XWAIT_POLLS; ++i)
+    if (mbar_try_cluster(a, parity)) return;
+  atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
+}
+// Asynchronous 16-byte store into a CTA's shared memory (dst, from remote());
+// its arrival completes 16 bytes of the transaction count of that CTA's
+// mbarrier `bar` (also from remote()), with release semantics at cluster
+// scope, so that a wait on the phase sees the data.
+__device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t bar, uint4 v) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   dst),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+               : "memory");
+}
 // Orders this thread's earlier generic shared-memory accesses before later
 // async-proxy (bulk copy) writes to the same memory.
 __device__ __forceinline__ void cp16(void *dst, const void *src) {
@@ -255,20 +285,25 @@ __device__ __forceinline__ void load_frag(const FusedSmem &S, int row, int lane,
     }
 }
 
-// Every CTA publishes four ints; afterwards S.all[r][k] holds CTA r's values
-// in every CTA.  Contains a cluster barrier.
-__device__ __noinline__ void exchange(FusedSmem &S, int slot, int v0, int v1, int v2, int v3) {
-  if (threadIdx.x == 0) {
-    S.pub[slot][0] = v0;
-    S.pub[slot][1] = v1;
-    S.pub[slot][2] = v2;
-    S.pub[slot][3] = v3;
-  }
-  cluster_sync();
-  if (threadIdx.x < CL * 4) {
-    const int r = threadIdx.x >> 2, k = threadIdx.x & 3;
-    S.all[r][k] = (int)ld_remote(remote(&S.pub[slot][k], r));
-  }
+// Every CTA publishes four ints (uniform over its threads); afterwards
+// S.all[r][k] holds CTA r's values in every CTA.  Threads 0-15 push the
+// CTA's 16 bytes into every CTA's exchange slot with asynchronous stores that
+// complete the receiver's mbarrier; every CTA then waits (bounded) for the 16
+// arrivals.  Consecutive exchanges alternate slots and mbarriers: a CTA can
+// only start exchange k + 2 after every CTA has sent exchange k + 1, which
+// each does after its wait for exchange k.
+__device__ __noinline__ void exchange(FusedSmem &S, int v0, int v1, int v2, int v3) {
+  const int tid = threadIdx.x;
+  const int k = S.ph_x, b = k & 1;
+  const uint32_t rank = cluster_rank();
+  __syncthreads();  // every thread has read ph_x
+  if (tid == 0) S.ph_x = k + 1;
+  if (tid < CL)
+    st_async_v4(remote(&S.xin[b][rank][0], (uint32_t)tid), remote(&S.mb_x[b], (uint32_t)tid),
+                make_uint4((uint32_t)v0, (uint32_t)v1, (uint32_t)v2, (uint32_t)v3));
+  if (tid == 0) mbar_expect_tx(&S.mb_x[b], CL * 16);
+  mbar_wait_cluster(&S.mb_x[b], (uint32_t)(k >> 1) & 1u, &S.status);
+  if (tid < CL * 4) S.all[tid >> 2][tid & 3] = S.xin[b][tid >> 2][tid & 3];
   __syncthreads();
 }
 __device__ __forceinline__ int before(const FusedSmem &S, int k, int rank) {
@@ -388,24 +423,31 @@ __device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t 
 //                     th is 0 when K exceeds the number of keys or the K-th
 //                     largest key is 0, 0xffffffff when K == 0.
 // Two 8-bit radix rounds resolve the top 16 bits (for 32-bit keys the BF16
-// score).  Keys of 32 bits that share the boundary score are then resolved
-// by position, not by two more rounds: their low 16 bits order them by
-// position (KEY_FINE: ascending for a positive score, descending for a
-// negative one; KEY_S15 and KEY_S16: descending), and positions ascend with
+// score).  A round: every CTA histograms its own keys, pushes its 256 counts
+// of each live head h (16-bit pairs, 512 bytes) into CTA h's per-source
+// table with asynchronous stores that complete CTA h's input mbarrier; CTA h
+// (the head's owner) waits for the 16 tables, sums them, finds the boundary
+// bin and pushes a 16-byte result to every CTA, which waits for the results
+// of its live heads.  No cluster barrier: a CTA sends round n + 1 only after
+// it has every owner's result of round n, which each owner pushes after it
+// has read its table, so one table, one input and one result mbarrier per
+// CTA suffice.
+// Keys of 32 bits that share the boundary score are resolved by position in
+// the second round instead of by two more rounds: their low 16 bits order
+// them by position (KEY_FINE: ascending for a positive score, descending for
+// a negative one; KEY_S15 and KEY_S16: descending), and positions ascend with
 // the CTA rank, so the krem largest tied keys are the first krem tied keys
-// counted from the favoured end of the rank order.  In the second round
-// every CTA also stores its count of every bin into the bin owner's
-// per-source table; after the barrier the head's warp reads the boundary
-// bin's 16 per-source counts, takes this CTA's quota from the counts on the
-// favoured side, and the threshold is the quota-th largest of this CTA's own
-// tied keys (a ballot scan in local order).  The thresholds then differ
-// between CTAs but select the keys a global K-th largest key would;
-// S.ctl.own[h] marks the CTA whose threshold is the cluster's K-th largest
-// key.  One cluster barrier per round.
+// counted from the favoured end of the rank order.  The owner has every
+// source's count of the boundary bin, gives each CTA its quota, and the
+// CTA's threshold is the quota-th largest of its own tied keys (a ballot
+// scan in local order).  The thresholds then differ between CTAs but select
+// the keys a global K-th largest key would; S.ctl.own[h] marks the CTA whose
+// threshold is the cluster's K-th largest key.
 __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, int nbits, bool exact, int kind,
                                             int q0, Marker &mark) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = (int)cluster_rank();
+  int ph_in = S.ph_in, ph_res = S.ph_res;  // (read by every thread before the barrier below)
   if (tid < 4) {
     S.ctl.prefix[tid] = 0;
     S.ctl.mask[tid] = 0;
@@ -416,107 +458,140 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
   }
   for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
   __syncthreads();
-  int r = 0;  // round of this selection: local histograms alternate between hist and hist2
-  for (int sh = 24; sh >= 16; sh -= 8, ++r) {
-    if (S.ctl.done[0] && S.ctl.done[1] && S.ctl.done[2] && S.ctl.done[3]) break;
+  for (int sh = 24; sh >= 16; sh -= 8) {
+    int live[4], nlive = 0;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      live[h] = !S.ctl.done[h];
+      nlive += live[h];
+    }
+    if (nlive == 0) break;
     const bool ties = !exact && nbits == 32 && sh == 16;
-    const int buf = S.round % 3, nbuf = (S.round + 1) % 3;
-    uint32_t *lh = (r & 1) ? S.hist2 : S.hist, *other = (r & 1) ? S.hist : S.hist2;
-    // the four heads in one pass (independent chains per thread); a
-    // finished head matches no key
+    // the four heads in one pass; a finished head matches no key
     uint32_t pf[4], mk[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const bool live = !S.ctl.done[h];
-      pf[h] = live ? S.ctl.prefix[h] : 1u;
-      mk[h] = live ? S.ctl.mask[h] : 0u;
+      pf[h] = live[h] ? S.ctl.prefix[h] : 1u;
+      mk[h] = live[h] ? S.ctl.mask[h] : 0u;
     }
     switch (kind) {
-      case KEY_COARSE: hist_pass<KEY_COARSE>(lh, S, nloc, q0, pf, mk, sh); break;
-      case KEY_FINE: hist_pass<KEY_FINE>(lh, S, nloc, q0, pf, mk, sh); break;
-      case KEY_S15: hist_pass<KEY_S15>(lh, S, nloc, q0, pf, mk, sh); break;
-      default: hist_pass<KEY_S16>(lh, S, nloc, q0, pf, mk, sh); break;
+      case KEY_COARSE: hist_pass<KEY_COARSE>(S.hist, S, nloc, q0, pf, mk, sh); break;
+      case KEY_FINE: hist_pass<KEY_FINE>(S.hist, S, nloc, q0, pf, mk, sh); break;
+      case KEY_S15: hist_pass<KEY_S15>(S.hist, S, nloc, q0, pf, mk, sh); break;
+      default: hist_pass<KEY_S16>(S.hist, S, nloc, q0, pf, mk, sh); break;
     }
-    if (tid < 64) S.red[nbuf][tid] = 0;
     __syncthreads();
     mark(M_HIST);
-    for (int e = tid; e < 4 * 256; e += FT) {
-      const uint32_t c = lh[e];
-      const uint32_t owner = (uint32_t)(e >> 6);
-      if (c) red_remote(remote(&S.red[buf][e & 63], owner), c);
-      if (ties) st_remote(remote(&S.tab[rank][e & 63], owner), c);
-      other[e] = 0u;  // the next round's local histogram
+    // this CTA's counts (< 2^16: nloc <= 2048) of each live head to its owner
+    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+    const int sh_h = tid >> 5, sj = tid & 31;
+    if (tid < 128 && live[sh_h]) {
+      const uint32_t *c = S.hist + sh_h * 256 + 8 * sj;
+      pk = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
     }
-    cluster_sync();
-    mark(M_SYNC);
-    if (warp < 4 && !S.ctl.done[warp]) {
-      // head h's 256 reduced bins straight into registers: lane l reads bins
-      // 248 - 8l .. 255 - 8l (one owner, two 16-byte loads)
-      const int h = warp, e0 = h * 256 + 248 - 8 * lane;
-      const uint32_t a = remote(&S.red[buf][e0 & 63], (uint32_t)(e0 >> 6));
-      const uint4 lo4 = ld_remote_v4(a), hi4 = ld_remote_v4(a + 16);
-      const uint32_t c[8] = {hi4.w, hi4.z, hi4.y, hi4.x, lo4.w, lo4.z, lo4.y, lo4.x};  // bins 255-8l-j
-      int bin;
-      uint32_t above, cnt;
-      const bool found = warp_find_regs(c, S.ctl.krem[h], lane, bin, above, cnt);
-      const uint32_t pf = S.ctl.prefix[h] | ((uint32_t)bin << sh);
-      const uint32_t kr = S.ctl.krem[h] - above;
-      bool tie = false;
-      if (lane == 0) {
+    __syncthreads();  // counts read
+    if (tid < 128 && live[sh_h])
+      st_async_v4(remote(&S.tab[rank][4 * sj], (uint32_t)sh_h), remote(&S.mb_in, (uint32_t)sh_h), pk);
+    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0u;  // the next round's histogram
+    if (rank < 4 && live[rank]) {
+      // owner of head h = rank
+      const int h = rank;
+      if (tid == 0) mbar_expect_tx(&S.mb_in, CL * 512);
+      mbar_wait_cluster(&S.mb_in, (uint32_t)ph_in & 1u, &S.status);
+      ++ph_in;
+      if (tid < 256) {
+        uint32_t c = 0;
+#pragma unroll
+        for (int q = 0; q < CL; ++q) c += (S.tab[q][tid >> 1] >> (16 * (tid & 1))) & 0xffffu;
+        S.sum[tid] = c;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        uint32_t c[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[j] = S.sum[255 - 8 * lane - j];
+        int bin;
+        uint32_t above, cnt;
+        const uint32_t krem = S.ctl.krem[h];
+        const bool found = warp_find_regs(c, krem, lane, bin, above, cnt);
+        const uint32_t pfx = S.ctl.prefix[h] | ((uint32_t)bin << sh);
+        const uint32_t kr = krem - above;
+        // result for destination CTA d = lane (lanes < 16)
+        uint32_t th = 0u, flags = lane == 0 ? 2u : 0u;
         if (!found) {
-          S.ctl.done[h] = 1;
-          S.ctl.th[h] = 0u;
-        } else {
-          S.ctl.prefix[h] = pf;
-          S.ctl.mask[h] |= 255u << sh;
-          S.ctl.krem[h] = kr;
-          if (sh == 32 - nbits || (!exact && cnt == kr && pf != 0u)) {
-            S.ctl.done[h] = 1;
-            S.ctl.th[h] = pf;
-          } else if (ties) {
-            S.ctl.done[h] = 1;
-            S.ctl.th[h] = 0u;  // the K-th largest key is 0 (pf == 0); else set below
-          }
-        }
-      }
-      tie = found && ties && !(cnt == kr && pf != 0u) && pf != 0u;  // warp-uniform
-      if (tie) {
-        const uint32_t B = pf >> 16;
-        const int e = h * 256 + bin;
-        const bool up = kind == KEY_FINE && (B & 0x8000u);  // low 16 bits ascend with the position
-        const uint32_t cq = lane < CL ? ld_remote(remote(&S.tab[lane][e & 63], (uint32_t)(e >> 6))) : 0u;
-        const uint32_t pre = __reduce_add_sync(0xffffffffu, (up ? lane > rank : lane < rank) ? cq : 0u);
-        const uint32_t n = __shfl_sync(0xffffffffu, cq, rank);
-        const uint32_t quota = kr > pre ? min(kr - pre, n) : 0u;
-        uint32_t th = quota == 0 ? (B + 1u) << 16 : B << 16;  // none / all of the tied keys
-        if (quota > 0 && quota < n) {
-          // the pick-th tied key of this CTA in local order
-          const uint32_t pick = up ? n - quota + 1 : quota;
-          uint32_t seen = 0;
-          for (int base = 0; base < nloc; base += 32) {
-            const int i = base + lane;
-            const uint32_t v = i < nloc ? select_key(S, kind, h, i, q0) : 0u;
-            const bool f = i < nloc && (v >> 16) == B;
-            const unsigned bal = __ballot_sync(0xffffffffu, f);
-            const bool me = f && seen + (uint32_t)__popc(bal & ((1u << lane) - 1u)) + 1u == pick;
-            const unsigned hit = __ballot_sync(0xffffffffu, me);
-            if (hit) {
-              th = __shfl_sync(0xffffffffu, v, __ffs(hit) - 1);
-              break;
+          flags |= 1u;  // K exceeds the number of keys: th = 0
+        } else if (sh == 32 - nbits || (!exact && cnt == kr && pfx != 0u)) {
+          flags |= 1u;
+          th = pfx;
+        } else if (ties) {
+          flags |= 1u;
+          if (pfx != 0u) {
+            const uint32_t B = pfx >> 16;
+            const bool up = kind == KEY_FINE && (B & 0x8000u);  // low 16 bits ascend with the position
+            const uint32_t cq = lane < CL ? (S.tab[lane][bin >> 1] >> (16 * (bin & 1))) & 0xffffu : 0u;
+            uint32_t incl = cq;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+              if (lane >= o) incl += y;
             }
-            seen += (uint32_t)__popc(bal);
+            const uint32_t all = __shfl_sync(0xffffffffu, incl, 31);
+            const uint32_t pre = up ? all - incl : incl - cq;  // tied keys on the favoured side
+            const uint32_t quota = kr > pre ? min(kr - pre, cq) : 0u;
+            th = quota == 0 ? (B + 1u) << 16 : B << 16;  // none / all of the tied keys
+            const uint32_t pick = (quota > 0 && quota < cq) ? (up ? cq - quota + 1 : quota) : 0u;
+            flags = 1u | ((pre < kr && kr <= pre + cq) ? 2u : 0u) | (pick << 8);
           }
         }
-        if (lane == 0) {
-          S.ctl.th[h] = th;
-          S.ctl.own[h] = pre < kr && kr <= pre + n;
-        }
+        if (lane < CL)
+          st_async_v4(remote(&S.res[h], (uint32_t)lane), remote(&S.mb_res, (uint32_t)lane),
+                      make_uint4(pfx, kr, th, flags));
       }
     }
-    if (tid == 0) S.round++;
+    mark(M_SYNC);
+    if (tid == 0) mbar_expect_tx(&S.mb_res, 16u * (uint32_t)nlive);
+    mbar_wait_cluster(&S.mb_res, (uint32_t)ph_res & 1u, &S.status);
+    ++ph_res;
+    if (warp < 4 && live[warp]) {
+      const int h = warp;
+      const SelRes r = S.res[h];
+      uint32_t th = r.th;
+      const uint32_t pick = (r.flags >> 8) & 0xfffu;
+      if (pick) {
+        // the pick-th tied key of this CTA in local order
+        const uint32_t B = r.pf >> 16;
+        uint32_t seen = 0;
+        for (int base = 0; base < nloc; base += 32) {
+          const int i = base + lane;
+          const uint32_t v = i < nloc ? select_key(S, kind, h, i, q0) : 0u;
+          const bool f = i < nloc && (v >> 16) == B;
+          const unsigned bal = __ballot_sync(0xffffffffu, f);
+          const bool me = f && seen + (uint32_t)__popc(bal & ((1u << lane) - 1u)) + 1u == pick;
+          const unsigned hit = __ballot_sync(0xffffffffu, me);
+          if (hit) {
+            th = __shfl_sync(0xffffffffu, v, __ffs(hit) - 1);
+            break;
+          }
+          seen += (uint32_t)__popc(bal);
+        }
+      }
+      if (lane == 0) {
+        S.ctl.prefix[h] = r.pf;
+        S.ctl.mask[h] |= 255u << sh;
+        S.ctl.krem[h] = r.kr;
+        S.ctl.done[h] = (int)(r.flags & 1u);
+        S.ctl.th[h] = th;
+        S.ctl.own[h] = (int)((r.flags >> 1) & 1u);
+      }
+    }
     __syncthreads();
     mark(M_READ);
   }
+  if (tid == 0) {
+    S.ph_in = ph_in;
+    S.ph_res = ph_res;
+  }
+  __syncthreads();
 }
 
 // ----------------------------------------------------- tensor-core dots
@@ -696,6 +771,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   const int per = ((nc + CL * 32 - 1) / (CL * 32)) * 32;
   const int r0 = min(nc, rank * per), r1 = min(nc, r0 + per), nrows = r1 - r0;
   const uint32_t P = (uint32_t)c.nprobe;
+  if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank)] = (long long)global_ns();
   Marker mark{(w.phase_ts && cell == 0 && rank == 0 && tid == 0) ? w.phase_ts : nullptr, 0};
   int *counts = w.counts + cell * NCOUNT;
   mark(M_START);
@@ -734,9 +810,13 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       S.fscale[tid] = fs;
     }
   }
-  for (int i = tid; i < 3 * 64; i += FT) (&S.red[0][0])[i] = 0;
   if (tid == 0) {
     for (int k = 0; k < NCHUNK; ++k) mbar_init(&S.mbar[k], 1);
+    mbar_init(&S.mb_in, 1);
+    mbar_init(&S.mb_res, 1);
+    mbar_init(&S.mb_x[0], 1);
+    mbar_init(&S.mb_x[1], 1);
+    S.ph_in = S.ph_res = S.ph_x = 0;
     mbar_fence_init();
     for (int k = 0; k * SLICE_CHUNK < nrows; ++k) {
       const int rows = min(SLICE_CHUNK, nrows - k * SLICE_CHUNK);
@@ -744,7 +824,6 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       bulk_g2s(S.big + k * SLICE_CHUNK * 64, c.upper + (size_t)(r0 + k * SLICE_CHUNK) * 64, (uint32_t)rows * 64u,
                &S.mbar[k]);
     }
-    S.round = 0;
     S.status = 0;
   }
   __syncthreads();
@@ -907,7 +986,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         ++r;
       }
   }
-  exchange(S, P_SURV, nsurv, 0, 0, 0);
+  exchange(S, nsurv, 0, 0, 0);
   const int surv_base = before(S, 0, rank);
   for (int k = tid; k < nsurv; k += FT) {
     const int lr = S.sidx[k];
@@ -1028,7 +1107,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (tid == 0) S.b.s.ppre[nsel] = npost;
   }
   mark(M_SELLIST);
-  exchange(S, P_SEL, nsel, npost, 0, 0);  // also publishes the selected bitmap words
+  exchange(S, nsel, npost, 0, 0);  // also publishes the selected bitmap words
   const int sel_base = before(S, 0, rank), nsel_all = total(S, 0), npost_all = total(S, 1);
   for (int k = tid; k < nsel; k += FT)
     if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = r0 + S.b.s.slist[k];
@@ -1081,7 +1160,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     }
   }
   mark(M_KEEP);
-  exchange(S, P_POOL, nkept, 0, 0, 0);
+  exchange(S, nkept, 0, 0, 0);
   const int kept_base = before(S, 0, rank), npool = total(S, 0);
   {
     const int *klist = reinterpret_cast<const int *>(S.big);
@@ -1206,7 +1285,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         r += f[j];
       }
   }
-  exchange(S, P_U15, nu, 0, 0, 0);
+  exchange(S, nu, 0, 0, 0);
   const int u_base = before(S, 0, rank), nu_all = min(total(S, 0), U15_MAX);
   for (int i = tid; i < m15; i += FT) {
     if (!S.b.p.flag[i]) continue;
@@ -1248,7 +1327,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     for (int j = 0; j < 2; ++j)
       if (f[j]) S.b.p.clist[r++] = (uint16_t)(i0 + j);
   }
-  exchange(S, P_CAND, ncl, 0, 0, 0);
+  exchange(S, ncl, 0, 0, 0);
   const int c_base = before(S, 0, rank), ncand = min(total(S, 0), CAND_MAX);
   if (rank == 0 && tid == 0) counts[C_CAND] = ncand;
   // candidates: their union position; their Stage-II keys (8-bit scores of
@@ -1529,11 +1608,12 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   mark(M_ATTN);
   if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
   cluster_sync();  // no CTA leaves while its shared memory may still be read
+  if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank) + 1] = (long long)global_ns();
 }
 
 const char *const kMarkNames[M_NTAGS] = {
     "start", "issue", "qprep_exponents", "qprep", "cluster_start", "slice_landed", "coarse",
-    "select_histogram", "select_barrier", "select_readback", "coarse_select", "survivors",
+    "select_histogram", "select_reduce", "select_result", "coarse_select", "survivors",
     "fine_gather", "fine", "fine_select", "selected_list", "selected_exchange", "pool_keep", "pool",
     "s15_gather", "s15_score", "s15_select", "u15_union", "s16_score", "s16_select", "candidates",
     "s2_score", "s2_select", "attn_items", "attn_cta", "attention", "shard_list_exchange"};
