@@ -177,11 +177,14 @@ const char *skv_phase_name(int32_t tag);
 /* One launch of the fused kernel with every CTA's global-timer stamps (ns)
  * at entry and at exit: start_ns[i] / end_ns[i] for CTA i = cell * 16 +
  * cluster rank (n_ctas = cells * 16, at most max_ctas), and the launch's
- * event-timed duration in *kernel_ms.  Launch skew between clusters and the
- * tail of the slowest cell are read from it.  Fused path, unconnected engine
- * only.  No counterpart in the reference (profiling of this build). */
+ * event-timed duration in *kernel_ms.  With marks != NULL, also the phase
+ * marks of the 16 CTAs of cell 0: marks[(r * max_marks + j) * 2 + {0, 1}] =
+ * (tag, global-timer ns) of mark j of CTA r, tag -1 past the last (tags as
+ * skv_phase_name).  Launch skew, the tail of the slowest cell and the CTA on
+ * the critical path of each phase are read from it.  Fused path, unconnected
+ * engine only.  No counterpart in the reference (profiling of this build). */
 int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end_ns, int32_t max_ctas,
-                     int32_t *n_ctas, float *kernel_ms);
+                     int32_t *n_ctas, float *kernel_ms, int64_t *marks, int32_t max_marks);
 
 /* Sequence-sharded decode -- no counterpart in the reference (its decode is
  * single-device).  A long context is split into contiguous token ranges,

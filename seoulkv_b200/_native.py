@@ -117,7 +117,7 @@ def load() -> ctypes.CDLL:
         lib.skv_phase_name.restype = ctypes.c_char_p
         lib.skv_profile_ctas.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
-                                         ctypes.POINTER(ctypes.c_float)]
+                                         ctypes.POINTER(ctypes.c_float), ctypes.c_void_p, ctypes.c_int32]
         lib.skv_phase_name.argtypes = [ctypes.c_int32]
         lib.skv_shard_outputs.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
                                           ctypes.POINTER(ctypes.c_void_p)]
@@ -263,19 +263,25 @@ class Engine:
                                           128, ctypes.byref(n)), "skv_profile_phases")
         return [(self.lib.skv_phase_name(int(tags[i])).decode(), float(cyc[i])) for i in range(n.value)]
 
-    def profile_ctas(self, stream: int = 0) -> tuple[np.ndarray, np.ndarray, float]:
+    def profile_ctas(self, stream: int = 0):
         """One fused launch: per-CTA (entry, exit) global-timer ns relative to
-        the earliest entry, shaped [cells, 16], and the launch's event time (µs)."""
-        cap = 16 * 1024
+        the earliest entry, shaped [cells, 16]; the launch's event time (µs);
+        and the phase marks of cell 0's 16 CTAs as {rank: [(name, ns), ...]}
+        on the same time base."""
+        cap, mm = 16 * 1024, 128
         s = np.zeros(cap, dtype=np.int64)
         e = np.zeros(cap, dtype=np.int64)
+        marks = np.zeros(16 * mm * 2, dtype=np.int64)
         n = ctypes.c_int32()
         ms = ctypes.c_float()
         check(self.lib.skv_profile_ctas(self.handle, ctypes.c_void_p(stream or None), _ptr(s), _ptr(e), cap,
-                                        ctypes.byref(n), ctypes.byref(ms)), "skv_profile_ctas")
+                                        ctypes.byref(n), ctypes.byref(ms), _ptr(marks), mm), "skv_profile_ctas")
         s, e = s[:n.value], e[:n.value]
         t0 = s.min()
-        return (s - t0).reshape(-1, 16), (e - t0).reshape(-1, 16), ms.value * 1e3
+        marks = marks.reshape(16, mm, 2)
+        per = {r: [(self.lib.skv_phase_name(int(tag)).decode(), int(ns - t0)) for tag, ns in marks[r] if tag >= 0]
+               for r in range(16)}
+        return (s - t0).reshape(-1, 16), (e - t0).reshape(-1, 16), ms.value * 1e3, per
 
     def shard_outputs(self, slot: int = 0) -> tuple[int, int]:
         """Device addresses of this engine's Stage-II keys and shard-local ids [4][4][100]."""

@@ -154,7 +154,8 @@ struct Work {
   uint32_t *hist;           // [cell][4 stages][4 heads][4096] first-pass histograms (step)
   uint16_t *out;            // [n_slots][16][256] BF16
   long long *phase_ts;      // [FUSED_MARKS][2] (tag, SM clock) marks of cell 0, or null
-  long long *cta_ts;        // [cell][16][2] global timer (ns) at CTA entry and exit (fused), or null
+  long long *cta_ts;        // [cell][16][2] global timer (ns) at CTA entry and exit, then [16][FUSED_MARKS][2]
+                            // (tag, ns) phase marks of cell 0's CTAs (fused), or null
   const ShardLinkDev *link; // sequence-sharded group (device copy), or null
   int32_t *shard_gids;      // [4][4][TOPK] the group's global winners (with link)
 };

@@ -854,7 +854,7 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
 }
 
 int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end_ns, int32_t max_ctas,
-                     int32_t *n_ctas, float *kernel_ms) {
+                     int32_t *n_ctas, float *kernel_ms, int64_t *marks, int32_t max_marks) {
   Engine *e = as_engine(handle);
   if (!e || !start_ns || !end_ns || !n_ctas || !kernel_ms) return fail(SKV_E_INVALID, "null engine or output");
   if (!e->fused) return fail(SKV_E_STATE, "CTA timing needs the fused path");
@@ -864,10 +864,12 @@ int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end
   CK(cudaSetDevice(e->desc.device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nct = e->n_cells * 16;
+  const size_t nts = 2 * (size_t)nct + 16 * 2 * (size_t)FUSED_MARKS;
   if (!e->cta_ts) {
-    rc = dalloc(e, &e->cta_ts, 2 * (size_t)nct);
+    rc = dalloc(e, &e->cta_ts, nts);
     if (rc) return rc;
   }
+  CK(cudaMemsetAsync(e->cta_ts, 0xff, nts * sizeof(long long), st));  // unused marks read as tag -1
   Work w = e->work;
   w.cta_ts = e->cta_ts;
   cudaEvent_t ev[2];
@@ -876,11 +878,10 @@ int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end
   cudaEventRecord(ev[0], st);
   cudaError_t le = launch_fused(w, st);
   cudaEventRecord(ev[1], st);
-  std::vector<long long> ts(2 * (size_t)nct, 0);
+  std::vector<long long> ts(nts, 0);
   cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(ev[1]) : le;
   if (se == cudaSuccess) se = cudaEventElapsedTime(kernel_ms, ev[0], ev[1]);
-  if (se == cudaSuccess)
-    se = cudaMemcpy(ts.data(), e->cta_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost);
+  if (se == cudaSuccess) se = cudaMemcpy(ts.data(), e->cta_ts, nts * sizeof(long long), cudaMemcpyDeviceToHost);
   cudaEventDestroy(ev[0]);
   cudaEventDestroy(ev[1]);
   if (se != cudaSuccess) return fail(SKV_E_CUDA, std::string("profile ctas: ") + cudaGetErrorString(se));
@@ -892,6 +893,13 @@ int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end
     end_ns[i] = ts[2 * i + 1];
   }
   *n_ctas = n;
+  if (marks && max_marks > 0) {
+    for (int r = 0; r < 16; ++r)
+      for (int j = 0; j < max_marks; ++j)
+        for (int k = 0; k < 2; ++k)
+          marks[((size_t)r * max_marks + j) * 2 + k] =
+              j < FUSED_MARKS ? ts[2 * (size_t)nct + ((size_t)r * FUSED_MARKS + j) * 2 + k] : -1;
+  }
   return SKV_OK;
 }
 

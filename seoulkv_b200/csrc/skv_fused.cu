@@ -94,6 +94,7 @@ struct FusedSmem {
   alignas(16) int xin[2][CL][4];   // exchange slots (consecutive exchanges alternate)
   unsigned long long mbar[NCHUNK];
   unsigned long long mb_in, mb_res, mb_x[2];  // selection inputs (owners), results, exchanges
+  unsigned long long mb_sh;        // the survivor share (once per step)
   int ph_in, ph_res, ph_x, ph_pad; // phases of mb_in / mb_res / exchanges completed so far
   int all[CL][4];                  // the cluster's values of the latest exchange
   SelCtl ctl;
@@ -119,10 +120,10 @@ struct FusedSmem {
   int offs[PER_MAX + 1];           // CSR offsets of the slice's clusters
   uint16_t resid[PER_MAX];         // residual norms of the slice (BF16)
   float scale4[PER_MAX / 32];
-  float fscale[PER_MAX / 32];
+  float fsc[CL * PER_MAX / 32];    // the cell's Fine scales (one per 32 centroids)
   uint16_t sidx[PER_MAX];          // survivors: slice row
   uint8_t smask[PER_MAX];          // survivors: head mask (bits 0-3), selected (bit 4)
-  uint32_t selw[PER_MAX / 32];
+  uint32_t shin[PER_MAX];          // this CTA's share of the survivors: global row | head mask << 16 | selected << 24
   alignas(128) uint8_t big[BIG];
 };
 
@@ -137,13 +138,20 @@ enum MarkTag {
   M_U15, M_S16, M_S16SEL, M_CAND, M_S2, M_S2SEL, M_ATTN_ITEMS, M_ATTN_CTA, M_ATTN, M_XLIST, M_NTAGS
 };
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 struct Marker {
   long long *ts;
   int n;
+  bool global;  // global-timer ns (comparable across SMs) instead of SM clocks
   __device__ __forceinline__ void operator()(int tag) {
     if (ts && n < FUSED_MARKS) {
       ts[2 * n] = tag;
-      ts[2 * n + 1] = clock64();
+      ts[2 * n + 1] = global ? (long long)global_ns() : clock64();
       ++n;
     }
   }
@@ -153,11 +161,6 @@ struct Marker {
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -260,6 +263,11 @@ __device__ __noinline__ void mbar_wait_cluster(void *bar, uint32_t parity, int *
 // its arrival completes 16 bytes of the transaction count of that CTA's
 // mbarrier `bar` (also from remote()), with release semantics at cluster
 // scope, so that a wait on the phase sees the data.
+__device__ __forceinline__ void st_async_b32(uint32_t dst, uint32_t bar, uint32_t v) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst), "r"(v),
+               "r"(bar)
+               : "memory");
+}
 __device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t bar, uint4 v) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
                    dst),
@@ -772,7 +780,14 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   const int r0 = min(nc, rank * per), r1 = min(nc, r0 + per), nrows = r1 - r0;
   const uint32_t P = (uint32_t)c.nprobe;
   if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank)] = (long long)global_ns();
-  Marker mark{(w.phase_ts && cell == 0 && rank == 0 && tid == 0) ? w.phase_ts : nullptr, 0};
+  // marks: SM clocks of CTA 0 of cell 0 (Work::phase_ts), or global-timer
+  // marks of every CTA of cell 0 after the entry/exit stamps (Work::cta_ts)
+  long long *mts = nullptr;
+  if (tid == 0 && cell == 0) {
+    if (w.phase_ts) mts = rank == 0 ? w.phase_ts : nullptr;
+    else if (w.cta_ts) mts = w.cta_ts + 2 * (size_t)w.n_cells * CL + (size_t)rank * 2 * FUSED_MARKS;
+  }
+  Marker mark{mts, 0, !w.phase_ts};
   int *counts = w.counts + cell * NCOUNT;
   mark(M_START);
 
@@ -785,7 +800,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     const uint16_t *qsrc = w.q + ((size_t)slot * 16 + g * 4) * D;
     uint16_t qv[2], rv[4];
     int ov[5];
-    float ks = 0.0f, s4 = 0.0f, fs = 0.0f;
+    float ks = 0.0f, s4 = 0.0f, fs[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) qv[k] = qsrc[tid + k * FT];
     if (tid < D) ks = c.key_scale[tid];
@@ -793,10 +808,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     for (int k = 0; k < 4; ++k) rv[k] = tid + k * FT < nrows ? c.resid[r0 + tid + k * FT] : (uint16_t)0;
 #pragma unroll
     for (int k = 0; k < 5; ++k) ov[k] = tid + k * FT <= nrows ? c.offsets[r0 + tid + k * FT] : 0;
-    if (tid < (nrows >> 5)) {
-      s4 = c.coarse_scale4[(r0 >> 5) + tid];
-      fs = c.fine_scale[(r0 >> 5) + tid];
-    }
+    if (tid < (nrows >> 5)) s4 = c.coarse_scale4[(r0 >> 5) + tid];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) fs[k] = tid + k * FT < (nc >> 5) ? c.fine_scale[tid + k * FT] : 0.0f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) S.sx[tid + k * FT] = bf16f(qv[k]);
     if (tid < D) S.kscale[tid] = ks;
@@ -805,10 +819,11 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 #pragma unroll
     for (int k = 0; k < 5; ++k)
       if (tid + k * FT <= PER_MAX) S.offs[tid + k * FT] = ov[k];
-    if (tid < PER_MAX / 32) {
-      S.scale4[tid] = s4;
-      S.fscale[tid] = fs;
-    }
+    if (tid < PER_MAX / 32) S.scale4[tid] = s4;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) S.fsc[tid + k * FT] = fs[k];
+    // the slice's selected-cluster bits, set by whichever CTA scores a survivor (P5)
+    if (tid < (nrows >> 5)) w.selbits[(size_t)cell * (nc >> 5) + (r0 >> 5) + tid] = 0u;
   }
   if (tid == 0) {
     for (int k = 0; k < NCHUNK; ++k) mbar_init(&S.mbar[k], 1);
@@ -816,6 +831,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     mbar_init(&S.mb_res, 1);
     mbar_init(&S.mb_x[0], 1);
     mbar_init(&S.mb_x[1], 1);
+    mbar_init(&S.mb_sh, 1);
     S.ph_in = S.ph_res = S.ph_x = 0;
     mbar_fence_init();
     for (int k = 0; k * SLICE_CHUNK < nrows; ++k) {
@@ -986,13 +1002,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         ++r;
       }
   }
-  exchange(S, nsurv, 0, 0, 0);
-  const int surv_base = before(S, 0, rank);
+  // posting lists a survivor would bring into the pool (into L2)
   for (int k = tid; k < nsurv; k += FT) {
-    const int lr = S.sidx[k];
-    w.tags[(size_t)cell * nc + surv_base + k] = (uint32_t)(r0 + lr) | ((uint32_t)S.smask[k] << 28);
-    // posting lists a survivor would bring into the pool
-    const int b = S.offs[lr], e = S.offs[lr + 1];
+    const int lr = S.sidx[k], b = S.offs[lr], e = S.offs[lr + 1];
     if (e > b) {
       prefetch_l2(c.values + b);
       prefetch_l2(c.mates + b);
@@ -1002,7 +1014,23 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       }
     }
   }
-  if (rank == 0 && tid == 0) counts[C_TAGS] = total(S, 0);
+  exchange(S, nsurv, 0, 0, 0);
+  const int surv_base = before(S, 0, rank), nsurv_all = total(S, 0);
+  // The Fine work is balanced over the cluster: CTA r scores the survivors at
+  // global positions [r L, r L + L), L = ceil(survivors / 16) (positions stay
+  // ascending with the rank, as the selection's tie rule needs); every CTA
+  // pushes each of its survivors into the slot of the CTA that scores it.
+  const int L = max(1, (nsurv_all + CL - 1) / CL);
+  const int s0 = min(nsurv_all, rank * L), nsh = min(nsurv_all, s0 + L) - s0;
+  for (int k = tid; k < nsurv; k += FT) {
+    const int lr = S.sidx[k], p = surv_base + k, d = p / L;
+    const uint32_t m = S.smask[k];
+    w.tags[(size_t)cell * nc + p] = (uint32_t)(r0 + lr) | (m << 28);
+    st_async_b32(remote(&S.shin[p - d * L], (uint32_t)d), remote(&S.mb_sh, (uint32_t)d), (uint32_t)(r0 + lr) | (m << 16));
+  }
+  if (tid == 0) mbar_expect_tx(&S.mb_sh, (uint32_t)nsh * 4u);
+  mbar_wait_cluster(&S.mb_sh, 0u, &S.status);
+  if (rank == 0 && tid == 0) counts[C_TAGS] = nsurv_all;
   mark(M_SURV);
 
   // ---------------------------------------------------------------- P4
@@ -1010,11 +1038,11 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     BFrag F;
     load_frag(S, R_Q, lane, F);
     const Pow2 scA = pow2s(S.shift[R_Q][hA]), scB = pow2s(S.shift[R_Q][hB]);
-    for (int b0 = 0; b0 < nsurv; b0 += BATCH_FINE) {
-      const int nb = min(BATCH_FINE, nsurv - b0);
+    for (int b0 = 0; b0 < nsh; b0 += BATCH_FINE) {
+      const int nb = min(BATCH_FINE, nsh - b0);
       __syncthreads();
       for (int q = tid; q < nb * 8; q += FT) {
-        const int rr = q >> 3, part = q & 7, cid = r0 + S.sidx[b0 + rr];
+        const int rr = q >> 3, part = q & 7, cid = (int)(S.shin[b0 + rr] & 0xffffu);
         const uint8_t *src = (part < 4 ? c.upper : c.lower) + (size_t)cid * 64 + (part & 3) * 16;
         cp16(S.big + rr * STRIDE_FINE + part * 16, src);
       }
@@ -1030,8 +1058,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         dsum[1] = 2 * dsum[1] - 15 * S.sxsum[R_Q][hB];
         const int row = (t & 1) ? r8 : rg;
         if (row < nb) {
-          const int k = b0 + row, lr = S.sidx[k], mk = S.smask[k], pos = surv_base + k;
-          const float fs = S.fscale[lr >> 5];
+          const int k = b0 + row, sv = (int)S.shin[k], cid = sv & 0xffff, mk = (sv >> 16) & 15, pos = s0 + k;
+          const float fs = S.fsc[cid >> 5];
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk) {
             const int h = kk ? hB : hA;
@@ -1049,7 +1077,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // ---------------------------------------------------------------- P5
   {
-    cluster_select(S, nsurv, P, 32, false, KEY_FINE, 0, mark);
+    cluster_select(S, nsh, P, 32, false, KEY_FINE, 0, mark);
   }
   mark(M_FSEL);
   uint32_t st = 0;
@@ -1061,18 +1089,18 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       if (tf[h] == 0u) { tf[h] = 0xffffffffu; st |= ST_FINE_SHORT; }
     }
     if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_FINE * G + tid] = tf[tid];
-    for (int k = tid; k < nsurv; k += FT) {
+    uint32_t *selbits = w.selbits + (size_t)cell * (nc >> 5);
+    for (int k = tid; k < nsh; k += FT) {
       bool s = false;
 #pragma unroll
       for (int h = 0; h < 4; ++h) s |= S.b.fkey[h][k] >= tf[h];
-      if (s) S.smask[k] |= 0x10;
+      if (s) {
+        const uint32_t cid = S.shin[k] & 0xffffu;
+        S.shin[k] |= 1u << 24;
+        atomicOr(selbits + (cid >> 5), 1u << (cid & 31));
+      }
     }
-    for (int i = tid; i < PER_MAX / 32; i += FT) S.selw[i] = 0;
-    __syncthreads();
-    for (int k = tid; k < nsurv; k += FT)
-      if (S.smask[k] & 0x10) atomicOr(&S.selw[S.sidx[k] >> 5], 1u << (S.sidx[k] & 31));
-    __syncthreads();
-    for (int i = tid; i < (nrows >> 5); i += FT) w.selbits[(size_t)cell * (nc >> 5) + (r0 >> 5) + i] = S.selw[i];
+    __syncthreads();  // selected flags complete
   }
   // selected clusters in ascending order with their posting ranges
   int nsel, npost;
@@ -1081,7 +1109,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     int f[4], cnt = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      f[j] = (i0 + j < nsurv) && (S.smask[i0 + j] & 0x10);
+      f[j] = (i0 + j < nsh) && ((S.shin[i0 + j] >> 24) & 1u);
       cnt += f[j];
     }
     int r = block_exclusive_scan(cnt, &nsel);  // (all reads of fkey precede this barrier)
@@ -1090,10 +1118,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     for (int j = 0; j < 4; ++j) {
       len[j] = 0;
       if (f[j]) {
-        const int lr = S.sidx[i0 + j];
-        const int b = S.offs[lr];
-        len[j] = S.offs[lr + 1] - b;
-        S.b.s.slist[r] = (uint16_t)lr;
+        const int cid = (int)(S.shin[i0 + j] & 0xffffu);
+        const int b = __ldg(c.offsets + cid);
+        len[j] = __ldg(c.offsets + cid + 1) - b;
+        S.b.s.slist[r] = (uint16_t)cid;
         S.b.s.soff[r] = b;
         psum += len[j];
         ++r;
@@ -1107,10 +1135,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (tid == 0) S.b.s.ppre[nsel] = npost;
   }
   mark(M_SELLIST);
-  exchange(S, nsel, npost, 0, 0);  // also publishes the selected bitmap words
+  exchange(S, nsel, npost, 0, 0);  // (also orders the selected bits before the mate rule reads them)
   const int sel_base = before(S, 0, rank), nsel_all = total(S, 0), npost_all = total(S, 1);
   for (int k = tid; k < nsel; k += FT)
-    if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = r0 + S.b.s.slist[k];
+    if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = S.b.s.slist[k];
   mark(M_SELX);
 
   // ---------------------------------------------------------------- P6
@@ -1132,7 +1160,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
             const int mid = (lo + hi + 1) >> 1;
             if (S.b.s.ppre[mid] <= p) lo = mid; else hi = mid - 1;
           }
-          cid[j] = r0 + S.b.s.slist[lo];
+          cid[j] = S.b.s.slist[lo];
           jj[j] = S.b.s.soff[lo] + (p - S.b.s.ppre[lo]);
         }
       }
