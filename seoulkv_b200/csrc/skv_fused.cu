@@ -95,6 +95,8 @@ struct FusedSmem {
   unsigned long long mbar[NCHUNK];
   unsigned long long mb_in, mb_res, mb_x[2];  // selection inputs (owners), results, exchanges
   unsigned long long mb_sh;        // the survivor share (once per step)
+  unsigned long long mb_pool, mb_s2, mb_win, mb_attn;  // pool share, Stage-II keys, winners, attention partials
+  alignas(16) int win[G][TOPK];    // the step's top-100 tokens per head (pushed by CTA h)
   int ph_in, ph_res, ph_x, ph_pad; // phases of mb_in / mb_res / exchanges completed so far
   int all[CL][4];                  // the cluster's values of the latest exchange
   SelCtl ctl;
@@ -195,16 +197,6 @@ __device__ __forceinline__ uint32_t remote(const void *p, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
   return r;
-}
-// Remote loads carry no "memory" clobber, so that several can be in flight;
-// the cluster barriers (which do) keep them after the writes they read.
-__device__ __forceinline__ float ld_remote_f(uint32_t a) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
 __device__ __forceinline__ void mbar_init(void *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
@@ -832,6 +824,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     mbar_init(&S.mb_x[0], 1);
     mbar_init(&S.mb_x[1], 1);
     mbar_init(&S.mb_sh, 1);
+    mbar_init(&S.mb_pool, 1);
+    mbar_init(&S.mb_s2, 1);
+    mbar_init(&S.mb_win, 1);
+    mbar_init(&S.mb_attn, 1);
     S.ph_in = S.ph_res = S.ph_x = 0;
     mbar_fence_init();
     for (int k = 0; k * SLICE_CHUNK < nrows; ++k) {
@@ -1190,11 +1186,22 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   mark(M_KEEP);
   exchange(S, nkept, 0, 0, 0);
   const int kept_base = before(S, 0, rank), npool = total(S, 0);
+  // P7's balanced shares of the pool positions: every kept token goes into
+  // the Stage-1.5 token slot of the CTA that scores its position
+  const int n15 = min(npool, cap);
+  const int pc = ((n15 + CL * 32 - 1) / (CL * 32)) * 32;
+  const int q0 = min(n15, rank * pc), m15 = min(n15, q0 + pc) - q0;
   {
     const int *klist = reinterpret_cast<const int *>(S.big);
     int32_t *pool = w.pool + (size_t)cell * cap;
-    for (int k = tid; k < nkept && k < BIG / 4; k += FT)
-      if (kept_base + k < cap) pool[kept_base + k] = klist[k];
+    for (int k = tid; k < nkept && k < BIG / 4; k += FT) {
+      const int p = kept_base + k;
+      if (p < cap) pool[p] = klist[k];
+      if (p < n15) {
+        const int d = p / pc;
+        st_async_b32(remote(&S.b.p.tok[p - d * pc], (uint32_t)d), remote(&S.mb_pool, (uint32_t)d), (uint32_t)klist[k]);
+      }
+    }
   }
   if (npool > cap) st |= ST_POOL_OVER;
   if (npool < M15_MIN) st |= ST_POOL_UNDER;
@@ -1204,7 +1211,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     counts[C_POSTINGS] = npost_all;
     counts[C_STATUS] = (int)st;
   }
-  cluster_sync();  // the pool is complete in global memory
+  if (tid == 0) mbar_expect_tx(&S.mb_pool, (uint32_t)m15 * 4u);
+  mbar_wait_cluster(&S.mb_pool, 0u, &S.status);
   mark(M_POOL);
 
   // ---------------------------------------------------------------- P7
@@ -1213,18 +1221,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   // breaks ties by the lower union position, which orders members like
   // their pool position does, so its keys carry the pool position and the
   // rows need no second gather.
-  const int n15 = min(npool, cap);
-  const int pc = ((n15 + CL * 32 - 1) / (CL * 32)) * 32;
-  const int q0 = min(n15, rank * pc), m15 = min(n15, q0 + pc) - q0;
   {
-    {
-      static_assert(POS_MAX == 2 * FT, "two pool positions per thread");
-      const int32_t *src = w.pool + (size_t)cell * cap + q0;
-      const int t0v = tid < m15 ? __ldcg(src + tid) : 0, t1v = tid + FT < m15 ? __ldcg(src + tid + FT) : 0;
-      if (tid < m15) S.b.p.tok[tid] = t0v;
-      if (tid + FT < m15) S.b.p.tok[tid + FT] = t1v;
-    }
-    __syncthreads();
+    static_assert(POS_MAX == 2 * FT, "two pool positions per thread");
     for (int b0 = 0; b0 < m15; b0 += BATCH_FINE) {
       const int nb = min(BATCH_FINE, m15 - b0);
       __syncthreads();
@@ -1360,7 +1358,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   if (rank == 0 && tid == 0) counts[C_CAND] = ncand;
   // candidates: their union position; their Stage-II keys (8-bit scores of
   // a small gather) and tokens for head h are pushed to CTA h (slot =
-  // candidate rank), into the Stage-1.5 score area, which is dead by now
+  // candidate rank, asynchronous stores completing CTA h's mb_s2), into the
+  // Stage-1.5 score area, which every CTA is done with once the candidate
+  // exchange has completed
   uint32_t *k2 = reinterpret_cast<uint32_t *>(&S.b.p.sc15[0][0]);
   int *t2 = reinterpret_cast<int *>(&S.b.p.sc15[0][0]) + CAND_MAX;
   for (int k = tid; k < ncl; k += FT) {
@@ -1402,14 +1402,13 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
             // weights 2*code8 - 255 = 16*(2*c4 - 15) + (2*r4 - 15)
             const long long dsum = 32 * dh[k] + 2 * dl[k] - 255 * S.sxsum[R_QS][h];
             const uint32_t key = (ord16(bf16_score(exact_to_float(dsum, k ? s2B : s2A))) << 16) | (0xffffu - u);
-            st_remote(remote(k2 + cr, (uint32_t)h), key);
-            st_remote(remote(t2 + cr, (uint32_t)h), (uint32_t)S.b.p.tok[i]);
+            st_async_b32(remote(k2 + cr, (uint32_t)h), remote(&S.mb_s2, (uint32_t)h), key);
+            st_async_b32(remote(t2 + cr, (uint32_t)h), remote(&S.mb_s2, (uint32_t)h), (uint32_t)S.b.p.tok[i]);
           }
         }
       }
     }
   }
-  cluster_sync();  // Stage-II keys of all candidates are in CTAs 0-3
   mark(M_S2);
 
   // --------------------------------------------------------------- P12
@@ -1419,6 +1418,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     const int h = rank;
     uint32_t *wkey = reinterpret_cast<uint32_t *>(S.big);
     int *widx = reinterpret_cast<int *>(S.big) + TOPK;
+    int *wtok = reinterpret_cast<int *>(S.big) + 2 * TOPK;
+    if (tid == 0) mbar_expect_tx(&S.mb_s2, (uint32_t)ncand * 8u);
+    mbar_wait_cluster(&S.mb_s2, 0u, &S.status);
     const uint32_t v[2] = {tid < ncand ? k2[tid] : 0u, tid + FT < ncand ? k2[tid + FT] : 0u};
     const uint32_t K = (uint32_t)min(TOPK, ncand);
     uint32_t prefix = 0, mask = 0, krem = K;
@@ -1466,15 +1468,33 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       fpos[rk] = (int)(0xffffu - (key & 0xffffu));
       fids[rk] = t2[widx[tid]];
       fkeys[rk] = key;
+      wtok[rk] = t2[widx[tid]];
     } else if (tid < TOPK) {
       // fewer than 100 candidates: a failed step the status word reports
       fpos[tid] = -1;
       fids[tid] = 0;
       fkeys[tid] = 0u;
+      wtok[tid] = 0;
     }
-    if (w.link) shard_lists(w, S, cell, h, fkeys, fids, mark);
+    if (w.link) {
+      shard_lists(w, S, cell, h, fkeys, fids, mark);
+    } else {
+      // head h's winners, in rank order, into every CTA's S.win[h]
+      __syncthreads();
+      if (tid < CL * (TOPK / 4)) {
+        const int d = tid / (TOPK / 4), q = tid - d * (TOPK / 4);
+        const uint4 v = make_uint4((uint32_t)wtok[4 * q], (uint32_t)wtok[4 * q + 1], (uint32_t)wtok[4 * q + 2],
+                                   (uint32_t)wtok[4 * q + 3]);
+        st_async_v4(remote(&S.win[h][4 * q], (uint32_t)d), remote(&S.mb_win, (uint32_t)d), v);
+      }
+    }
   }
-  cluster_sync();  // final ids (and, sharded, the group's global winners) complete in global memory
+  if (w.link) {
+    cluster_sync();  // the group's global winners are complete in global memory
+  } else {
+    if (tid == 0) mbar_expect_tx(&S.mb_win, G * TOPK * 4);
+    mbar_wait_cluster(&S.mb_win, 0u, &S.status);
+  }
   mark(M_S2SEL);
 
   // --------------------------------------------------------------- P13
@@ -1500,7 +1520,6 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
     }
     const int nw = CL * FW, gw = rank * FW + warp;
-    const int32_t *fids = w.final_ids + (size_t)cell * G * TOPK;
     // this warp's items are gw, gw + nw, ...: lane j holds item j's token and
     // head (-1: dense key shared by the four heads); records are loaded one
     // item ahead of the one being folded in
@@ -1521,7 +1540,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
           if (gid >= 0) my_tok = gid;
           else my_head = -2;
         } else {
-          my_tok = __ldcg(fids + r);
+          my_tok = S.win[r / TOPK][r - (r / TOPK) * TOPK];
         }
       }
     }
@@ -1606,20 +1625,32 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       part[h * PART + 4 + d2 + 1] = O1;
       if ((tid & 127) == 0) { part[h * PART] = M; part[h * PART + 1] = L; }
     }
-    cluster_sync();
+    __syncthreads();
+    // this CTA's (m, l) and 16 output dimensions of each head to the CTA that
+    // finishes those dimensions (320 bytes each, asynchronous stores into its
+    // staging area, which every CTA is done gathering into by now)
+    float *pin = reinterpret_cast<float *>(S.big + 80 * 1024);  // [source CTA][head][20]: m, l, -, -, o[16]
+    if (tid < CL * G * 5) {
+      const int d = tid / (G * 5), hh = (tid / 5) % G, ch = tid % 5;
+      const float *src = ch == 0 ? part + hh * PART : part + hh * PART + 4 + 16 * d + 4 * (ch - 1);
+      const uint4 v = make_uint4(__float_as_uint(src[0]), __float_as_uint(src[1]), ch ? __float_as_uint(src[2]) : 0u,
+                                 ch ? __float_as_uint(src[3]) : 0u);
+      st_async_v4(remote(pin + (rank * G + hh) * 20 + 4 * ch, (uint32_t)d), remote(&S.mb_attn, (uint32_t)d), v);
+    }
+    if (tid == 0) mbar_expect_tx(&S.mb_attn, CL * G * 5 * 16);
+    mbar_wait_cluster(&S.mb_attn, 0u, &S.status);
     mark(M_ATTN_CTA);
     // CTA `rank` finishes output dimensions [16 rank, 16 rank + 16) of the four heads
     float M = -INFINITY, L = 0.0f, O = 0.0f;
     if (tid < G * 16) {
       const int h = tid >> 4, d = 16 * rank + (tid & 15);
-      // the 16 CTA partials, all loads in flight at once, then the
-      // log-sum-exp merge (log2 domain)
+      // the 16 CTA partials, then the log-sum-exp merge (log2 domain)
       float ms[CL], ls[CL], os[CL];
 #pragma unroll
       for (int r = 0; r < CL; ++r) {
-        ms[r] = ld_remote_f(remote(part + h * PART, (uint32_t)r));
-        ls[r] = ld_remote_f(remote(part + h * PART + 1, (uint32_t)r));
-        os[r] = ld_remote_f(remote(part + h * PART + 4 + d, (uint32_t)r));
+        ms[r] = pin[(r * G + h) * 20];
+        ls[r] = pin[(r * G + h) * 20 + 1];
+        os[r] = pin[(r * G + h) * 20 + 4 + (d - 16 * rank)];
       }
 #pragma unroll
       for (int r = 0; r < CL; ++r) M = fmaxf(M, ms[r]);
