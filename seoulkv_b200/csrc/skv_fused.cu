@@ -416,6 +416,8 @@ __device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t 
 
 // K-th largest of the cluster's keys (select_key of `kind`) for each of the
 // four heads; nbits (16 or 32) top bits of the 32-bit keys are significant.
+// With `pre`, S.hist already holds this CTA's first-round histogram (all
+// keys, built while the keys were computed).
 // On return S.ctl.th[h] holds a threshold: the keys >= it, over the whole
 // cluster, are
 //   exact (16 bits):  those >= the K-th largest key;
@@ -444,7 +446,7 @@ __device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t 
 // the keys a global K-th largest key would; S.ctl.own[h] marks the CTA whose
 // threshold is the cluster's K-th largest key.
 __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, int nbits, bool exact, int kind,
-                                            int q0, Marker &mark) {
+                                            int q0, Marker &mark, bool pre = false) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = (int)cluster_rank();
   int ph_in = S.ph_in, ph_res = S.ph_res;  // (read by every thread before the barrier below)
@@ -456,7 +458,8 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     S.ctl.th[tid] = K == 0 ? 0xffffffffu : 0u;
     S.ctl.own[tid] = rank == 0;
   }
-  for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
+  if (!pre)
+    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
   __syncthreads();
   for (int sh = 24; sh >= 16; sh -= 8) {
     int live[4], nlive = 0;
@@ -474,7 +477,7 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
       pf[h] = live[h] ? S.ctl.prefix[h] : 1u;
       mk[h] = live[h] ? S.ctl.mask[h] : 0u;
     }
-    switch (kind) {
+    if (!(pre && sh == 24)) switch (kind) {
       case KEY_COARSE: hist_pass<KEY_COARSE>(S.hist, S, nloc, q0, pf, mk, sh); break;
       case KEY_FINE: hist_pass<KEY_FINE>(S.hist, S, nloc, q0, pf, mk, sh); break;
       case KEY_S15: hist_pass<KEY_S15>(S.hist, S, nloc, q0, pf, mk, sh); break;
@@ -817,6 +820,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     // the slice's selected-cluster bits, set by whichever CTA scores a survivor (P5)
     if (tid < (nrows >> 5)) w.selbits[(size_t)cell * (nc >> 5) + (r0 >> 5) + tid] = 0u;
   }
+  for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0u;  // (P1 adds the coarse first round)
   if (tid == 0) {
     for (int k = 0; k < NCHUNK; ++k) mbar_init(&S.mbar[k], 1);
     mbar_init(&S.mb_in, 1);
@@ -953,6 +957,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         const uint16_t lo = (uint16_t)ord16(bf16_score(__fsub_rn(v, margin)));
         const uint16_t hi = (uint16_t)ord16(bf16_score(__fadd_rn(v, margin)));
         S.b.c.lo[h][lr] = lo;
+        atomicAdd(&S.hist[h * 256 + (lo >> 8)], 1u);  // the coarse selection's first round
         S.b.c.hi[h][lr] = hi;
         glo[(size_t)h * nc + row] = lo;
         ghi[(size_t)h * nc + row] = hi;
@@ -965,7 +970,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   // ---------------------------------------------------------------- P2
   cluster_wait();
   {
-    cluster_select(S, nrows, P, 16, true, KEY_COARSE, 0, mark);
+    cluster_select(S, nrows, P, 16, true, KEY_COARSE, 0, mark, true);
   }
   uint32_t tco[4];
 #pragma unroll
