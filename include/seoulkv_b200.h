@@ -103,8 +103,12 @@ int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells);
 int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t *v,
                   int32_t on_device);
 
-/* Q: BF16 bit patterns [n_slots][16][256], host or device memory.  Host
- * memory is staged through a pinned buffer; the copy is ordered on `stream`. */
+/* Q: BF16 bit patterns [n_slots][16][256], host or device memory.  Device
+ * memory is copied on `stream` now.  Host memory is copied into a pinned
+ * staging buffer now and reaches the device inside the next skv_run's step
+ * graph, which then also copies the output and the counters back into pinned
+ * host memory (skv_output to host and skv_status read them from there): a
+ * host-I/O step costs one graph launch and one wait. */
 int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *stream);
 
 /* Enqueue the whole funnel for every slot on `stream` (no host sync). */

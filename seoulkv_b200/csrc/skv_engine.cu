@@ -60,6 +60,15 @@ struct Engine {
   bool q_pending = false, ran = false;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // host-I/O steps: a query bound from host memory is copied in by the step
+  // graph itself, which also copies the output and the counters back into
+  // pinned host memory, so that a step costs one launch and one wait
+  uint16_t *out_pinned = nullptr;
+  int32_t *counts_pinned = nullptr;
+  cudaGraph_t graph_host = nullptr;
+  cudaGraphExec_t exec_host = nullptr;
+  bool q_host = false;   // the bound query is in q_pinned
+  bool host_io = false;  // the last launch was a host-I/O step (its output and counters are in pinned memory)
   bool fused = false;             // one cluster kernel per step (else the staged kernels)
   long long *phase_ts = nullptr;  // fused phase timestamps (skv_profile_phases)
   long long *cta_ts = nullptr;    // per-CTA entry/exit times (skv_profile_ctas)
@@ -159,8 +168,19 @@ int sync_done(Engine *e) {
 
 int read_counts(Engine *e, std::vector<int32_t> &c) {
   c.assign((size_t)e->n_cells * NCOUNT, 0);
+  if (e->host_io) {
+    std::memcpy(c.data(), e->counts_pinned, c.size() * sizeof(int32_t));
+    return SKV_OK;
+  }
   CK(cudaMemcpy(c.data(), e->work.counts, c.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
   return SKV_OK;
+}
+
+void drop_graphs(Engine *e) {
+  if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = nullptr; }
+  if (e->graph) { cudaGraphDestroy(e->graph); e->graph = nullptr; }
+  if (e->exec_host) { cudaGraphExecDestroy(e->exec_host); e->exec_host = nullptr; }
+  if (e->graph_host) { cudaGraphDestroy(e->graph_host); e->graph_host = nullptr; }
 }
 
 }  // namespace
@@ -211,6 +231,10 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming) ? fail(SKV_E_CUDA, "event") : 0);
   TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->q_pinned), (size_t)d->n_slots * 16 * D * 2,
                     cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned query buffer") : 0);
+  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->out_pinned), (size_t)d->n_slots * 16 * D * 2,
+                    cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned output buffer") : 0);
+  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->counts_pinned), (size_t)d->n_slots * G * NCOUNT * 4,
+                    cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned counter buffer") : 0);
   TRY(prepare_funnel_attributes() ? fail(SKV_E_CUDA, "kernel attributes") : 0);
   e->bufs.resize(e->n_cells);
   e->hcells.assign(e->n_cells, CellDev{});
@@ -289,11 +313,12 @@ void skv_destroy(void *handle) {
     for (void *p : row)
       if (p) cudaIpcCloseMemHandle(p);
   if (e->link.region) cudaFree(e->link.region);
-  if (e->exec) cudaGraphExecDestroy(e->exec);
-  if (e->graph) cudaGraphDestroy(e->graph);
+  drop_graphs(e);
   for (auto &b : e->bufs) free_cell(b, true, true);
   for (void *p : e->allocs) cudaFree(p);
   if (e->q_pinned) cudaFreeHost(e->q_pinned);
+  if (e->out_pinned) cudaFreeHost(e->out_pinned);
+  if (e->counts_pinned) cudaFreeHost(e->counts_pinned);
   if (e->q_copied) cudaEventDestroy(e->q_copied);
   if (e->done) cudaEventDestroy(e->done);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -433,14 +458,15 @@ int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *str
   uint16_t *dq = const_cast<uint16_t *>(e->work.q);
   if (on_device) {
     CK(cudaMemcpyAsync(dq, q, bytes, cudaMemcpyDeviceToDevice, st));
+    e->q_host = false;
     return SKV_OK;
   }
-  // the pinned staging buffer may still feed the previous copy
+  // the pinned staging buffer may still feed the previous host-I/O step;
+  // the next skv_run copies it in as the first node of its graph
   if (e->q_pending) CK(cudaEventSynchronize(e->q_copied));
+  e->q_pending = false;
   std::memcpy(e->q_pinned, q, bytes);
-  CK(cudaMemcpyAsync(dq, e->q_pinned, bytes, cudaMemcpyHostToDevice, st));
-  CK(cudaEventRecord(e->q_copied, st));
-  e->q_pending = true;
+  e->q_host = true;
   return SKV_OK;
 }
 
@@ -451,7 +477,9 @@ int skv_run(void *handle, void *stream) {
   if (rc) return rc;
   CK(cudaSetDevice(e->desc.device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: legacy default stream
-  if (!e->exec) {
+  const bool host = e->q_host;
+  cudaGraphExec_t &exec = host ? e->exec_host : e->exec;
+  if (!exec) {
     CK(cudaStreamSynchronize(e->stream));
     CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
     // only the step graph carries the group; profiling launches run the funnel alone
@@ -460,7 +488,15 @@ int skv_run(void *handle, void *stream) {
       w.link = e->link.dev;
       w.shard_gids = e->link.gids;
     }
-    cudaError_t le = launch_step(e, w, e->stream);
+    const size_t qbytes = (size_t)e->desc.n_slots * 16 * D * sizeof(uint16_t);
+    cudaError_t le = cudaSuccess;
+    if (host) le = cudaMemcpyAsync(const_cast<uint16_t *>(w.q), e->q_pinned, qbytes, cudaMemcpyHostToDevice, e->stream);
+    if (le == cudaSuccess) le = launch_step(e, w, e->stream);
+    if (host && le == cudaSuccess)
+      le = cudaMemcpyAsync(e->out_pinned, w.out, qbytes, cudaMemcpyDeviceToHost, e->stream);
+    if (host && le == cudaSuccess)
+      le = cudaMemcpyAsync(e->counts_pinned, w.counts, (size_t)e->n_cells * NCOUNT * sizeof(int32_t),
+                           cudaMemcpyDeviceToHost, e->stream);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (le != cudaSuccess) {
@@ -468,10 +504,15 @@ int skv_run(void *handle, void *stream) {
       return fail(SKV_E_CUDA, std::string("funnel launch: ") + cudaGetErrorString(le));
     }
     if (ce != cudaSuccess) return fail(SKV_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
-    e->graph = g;
-    CK(cudaGraphInstantiate(&e->exec, g, 0));
+    (host ? e->graph_host : e->graph) = g;
+    CK(cudaGraphInstantiate(&exec, g, 0));
   }
-  CK(cudaGraphLaunch(e->exec, st));
+  CK(cudaGraphLaunch(exec, st));
+  if (host) {
+    CK(cudaEventRecord(e->q_copied, st));
+    e->q_pending = true;
+  }
+  e->host_io = host;
   CK(cudaEventRecord(e->done, st));
   e->ran = true;
   return SKV_OK;
@@ -531,6 +572,10 @@ int skv_output(void *handle, void *out, int32_t to_host) {
   }
   int rc = sync_done(e);
   if (rc) return rc;
+  if (e->host_io) {
+    std::memcpy(out, e->out_pinned, (size_t)e->desc.n_slots * 16 * D * 2);
+    return SKV_OK;
+  }
   CK(cudaMemcpy(out, e->work.out, (size_t)e->desc.n_slots * 16 * D * 2, cudaMemcpyDeviceToHost));
   return SKV_OK;
 }
@@ -668,6 +713,7 @@ int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, 
   if (rc) return rc;
   CK(cudaSetDevice(e->desc.device));
   CK(launch_shard_attention(e->work, gids, token_begin, partials, static_cast<cudaStream_t>(stream)));
+  e->host_io = false;
   return SKV_OK;
 }
 
@@ -733,9 +779,8 @@ int skv_shard_connect(void *handle, const void *ipc_handles) {
   const ShardLinkDev view = link_view(e);
   CK(cudaMemcpy(e->link.dev, &view, sizeof(view), cudaMemcpyHostToDevice));
   e->link.active = true;
-  // the step graph is captured again with the merge/attention/combine kernels
-  if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = nullptr; }
-  if (e->graph) { cudaGraphDestroy(e->graph); e->graph = nullptr; }
+  // the step graphs are captured again with the group's exchanges
+  drop_graphs(e);
   return SKV_OK;
 }
 
@@ -794,6 +839,7 @@ int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_k
   std::vector<cudaEvent_t> ev(nk + 1, nullptr);
   for (auto &x : ev) CK(cudaEventCreate(&x));
   cudaError_t le;
+  e->host_io = false;
   if (e->fused) {
     cudaEventRecord(ev[0], st);
     le = launch_fused(e->work, st);
@@ -836,6 +882,7 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
     w.link = e->link.dev;
     w.shard_gids = e->link.gids;
   }
+  e->host_io = false;
   CK(launch_fused(w, st));
   if (e->link.active) CK(launch_shard_epoch(e->link.dev, st));
   CK(cudaMemcpyAsync(ts.data(), e->phase_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost, st));
@@ -875,6 +922,7 @@ int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end
   cudaEvent_t ev[2];
   CK(cudaEventCreate(&ev[0]));
   CK(cudaEventCreate(&ev[1]));
+  e->host_io = false;
   cudaEventRecord(ev[0], st);
   cudaError_t le = launch_fused(w, st);
   cudaEventRecord(ev[1], st);
