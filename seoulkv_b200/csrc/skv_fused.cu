@@ -3,48 +3,54 @@
 //
 // A cell (slot x KV head) is decoded by a cluster of CL = 16 CTAs, one CTA
 // per SM; one launch covers every cell of the step.  The stages of the
-// staged path (skv_kernels.cu) become phases of a single kernel separated by
-// hardware cluster barriers (barrier.cluster, ~0.25 us) instead of kernel
-// boundaries, and the data a phase hands to the next stays in shared memory:
+// staged path (skv_kernels.cu) become phases of a single kernel, and what a
+// phase hands to the next stays in shared memory or is pushed into the
+// shared memory of the CTA that consumes it:
 //
 //   P0  query operands: every CTA derives the 12 operand rows itself
 //   P1  coarse: the CTA's contiguous slice of the upper plane arrives by TMA
 //       bulk copies (8 KB each, one mbarrier each) and is scored on int8
-//       tensor cores; lo/hi stay in shared memory
+//       tensor cores; lo/hi stay in shared memory, and the coarse
+//       selection's first-round histogram is built on the way
 //   P2  coarse threshold: cluster radix select, two 8-bit rounds
-//   P3  survivors: head masks, cluster prefix scan -> global positions
-//   P4  fine: upper+lower rows of the survivors gathered with cp.async
-//   P5  fine top-nprobe per head (cluster radix select), selected bitmap
-//   P6  pool: postings of the selected clusters, spill-2 mate rule, cluster
-//       prefix scan -> pool positions
-//   P7  Stage-1.5 scores over a balanced share of the pool positions
-//   P8  top-1600 per head, ascending union (cluster scan)
-//   P9  Stage-1.6 scores of this CTA's union members
-//   P10 top-256 per head, candidates (cluster scan)
+//   P3  survivors: head masks, exchange -> global positions; every CTA
+//       pushes its survivors into equal shares of the global order
+//   P4  fine: upper+lower rows of this CTA's share gathered with cp.async
+//   P5  fine top-nprobe per head (cluster select), selected bitmap
+//   P6  pool: postings of the selected clusters, spill-2 mate rule,
+//       exchange -> pool positions; kept tokens pushed into P7's shares
+//   P7  Stage-1.5 and 1.6 scores over a balanced share of the pool
+//   P8  top-1600 per head, ascending union (exchange)
+//   P10 top-256 per head, candidates (exchange)
 //   P11 Stage-II scores of this CTA's candidates (small gather), pushed to
 //       CTA h for head h
-//   P12 exact top-100 per head (CTA h of the cluster), rank order
-//   P13 attention: sink + local + top-100 partials per CTA, combined across
-//       the cluster through distributed shared memory
+//   P12 exact top-100 per head (CTA h), rank order, pushed to every CTA
+//   P13 attention: sink + local + top-100 partials per CTA, each CTA's
+//       share of the output dimensions pushed to the CTA finishing them
 //
-// Cluster radix select (P2, P5, P8, P10): every CTA histograms its own keys
-// with shared-memory atomics, adds the non-zero bins into the owning CTA's
-// bins (bin b of head h belongs to CTA (256 h + b) / 64) with
-// red.shared::cluster, and after one cluster barrier every CTA reads the
-// 1024 reduced bins back and derives the same boundary bin.  The owners'
-// bins rotate over three buffers, which makes one barrier per round enough:
-// a buffer is cleared two rounds after it was read and one round before it
-// is added to again.
+// Communication inside the cluster is by asynchronous stores into the
+// receiver's shared memory (st.async ... mbarrier::complete_tx), each
+// completing a transaction count on the receiver's mbarrier, which the
+// receiver waits on with acquire at cluster scope; the expected byte counts
+// follow from counts every CTA knows at that point (exchanged four-int
+// records, or fixed shapes).  Cluster selection (P2, P5, P8, P10): every CTA
+// histograms its keys, pushes its counts of head h into CTA h's per-source
+// table; CTA h sums them, finds the boundary bin and pushes the round's
+// result (and, in the last round of a 32-bit selection, each CTA's share of
+// the tied keys) back; see cluster_select.
 //
 // Every intermediate the staged path exposes (lo/hi, thresholds, survivor
 // tags, selected clusters, pool, unions, final ranks and ids, counters) is
 // written to the same Work buffers in the same format, so both paths are
 // checked by the same stage-by-stage parity tests.
 //
-// Waits: the only waits are cluster barriers (all threads of all CTAs reach
-// each one: control flow is uniform by construction) and the coarse-slice
-// mbarriers, which poll a bounded number of times and then record
-// ST_TIMEOUT in the cell's status instead of waiting on.
+// Waits: every wait on another CTA is a bounded poll of an mbarrier phase
+// (XWAIT_POLLS) that records ST_TIMEOUT in the cell's status and returns
+// instead of waiting on; the coarse-slice copies likewise (WAIT_POLLS).  The
+// cluster barriers left (the start, the sequence-sharded exchanges and the
+// end, where no CTA may leave while its shared memory can still be read) are
+// reached by all threads of all CTAs: control flow is uniform by
+// construction.
 #include <cuda_fp8.h>
 
 #include "skv_device.cuh"
