@@ -53,6 +53,12 @@ def parse():
     p.add_argument("--cpu-steps", type=int, default=2)
     p.add_argument("--components", type=int, default=256, help="mixture components per KV head")
     p.add_argument("--staged", action="store_true", help="run the 14-kernel staged path instead of the fused one")
+    p.add_argument("--layers", type=int, default=0,
+                   help="decode-stack mode: L independent layers of --context tokens (BASELINE configs[2])")
+    p.add_argument("--requests", type=int, default=0,
+                   help="batched mode: R independent requests of --context tokens, split over the GPUs "
+                        "(BASELINE configs[4]); sweeps --sweep nprobe values")
+    p.add_argument("--sweep", default="16,64,128,256,384,512", help="nprobe values of the batched mode")
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="sharded exchange: peer memory inside the step graph, or NCCL all-gathers")
     return p.parse_args()
@@ -390,6 +396,173 @@ def run_sharded(args, world, rank, local, device):
     dist.destroy_process_group()
 
 
+def _timed_steps(args, device, flush, step_fn):
+    """W untimed steps, then K steps each after an L2 flush, CUDA events around
+    each step on the current stream; returns the per-step times (us)."""
+    stream = torch.cuda.current_stream(device)
+    for i in range(args.warmup):
+        flush.zero_()
+        step_fn(i)
+    torch.cuda.synchronize(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step_fn(args.warmup + i)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(device)
+    return np.array([a.elapsed_time(b) * 1e3 for a, b in ev])
+
+
+def run_stack(args, device):
+    """a stack of independent layers on one GPU.  Per
+    token: every layer decodes its own query.  Timed two ways: the drop-in
+    use (one SeoulKV4 per layer, run one after the other) and one
+    SeoulKV4Batch over all layers (one launch per token).  Reports the
+    per-token latency summed over layers and the HBM footprint."""
+    from seoulkv_b200 import SeoulKV4, SeoulKV4Batch, SeoulKV4Config, synthetic
+
+    L = args.layers
+    cfg = SeoulKV4Config(debug=True)
+    # engines allocate with cudaMalloc: their footprint is the drop in free
+    # device memory minus what PyTorch's allocator reserved meanwhile
+    def engine_bytes():
+        return torch.cuda.mem_get_info(device)[0] + torch.cuda.memory_reserved(device)
+
+    free0 = engine_bytes()
+    caches, qs, singles = [], [], []
+    for layer in range(L):
+        seed = 2 * 1000 + layer
+        k, v, mixes = synthetic.make_kv(args.context, seed=seed, components=args.components)
+        from seoulkv_b200 import SeoulKV4Index
+        index = SeoulKV4Index.build(k, v, sink=128, local=256, nprobe=args.nprobe, build_device=str(device))
+        qs.append(torch.stack([synthetic.make_query(args.context, mixes, seed=seed * 7919 + i).reshape(1, 16, 256)
+                               for i in range(args.warmup + args.steps)]).to(device))
+        kd, vd = k.to(device), v.to(device)
+        caches.append((kd, vd, index))
+        a = SeoulKV4(device=device, k=kd, v=vd, index=index, config=cfg)
+        a.run(qs[-1][0].unsqueeze(0))
+        a.synchronize()
+        singles.append(a)
+    torch.cuda.synchronize(device)
+    free1 = engine_bytes()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+
+    def seq_step(i):
+        for layer in range(L):
+            singles[layer].run(qs[layer][i].unsqueeze(0))
+
+    t_seq = _timed_steps(args, device, flush, seq_step)
+    ids_seq = [a.debug_snapshot()["selected_ids"] for a in singles]
+    for a in singles:
+        a.close()
+    free2 = engine_bytes()
+    batch = SeoulKV4Batch(device=device, caches=caches, config=cfg)
+    q_all = torch.cat(qs, 1)  # [steps, L, 16, 256]
+    batch.run(q_all[0].unsqueeze(1))
+    batch.synchronize()
+    free3 = engine_bytes()
+    t_bat = _timed_steps(args, device, flush, lambda i: batch.run(q_all[i].unsqueeze(1)))
+    ids_bat = batch.debug_snapshot()["selected_ids"]
+    same = all(torch.equal(ids_bat[layer], ids_seq[layer]) for layer in range(L))
+    batch.close()
+    line = {
+        "metric": f"us/token, {L}-layer decode stack at {args.context // 1024}K ctx (per-token latency summed over "
+                  "layers)",
+        "value": float(np.mean(t_bat)), "unit": "us/token", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": False, "data": "synthetic (BASELINE generator, one seed per "
+                                                                  "layer), fresh Q per layer and token",
+        "config": {"workload": f"{L} independent layers, T={args.context}, 4 KV / 16 Q heads, d=256, "
+                               f"nprobe={args.nprobe}", "l2": "flushed before every token"},
+        "batched_one_launch_us": float(np.mean(t_bat)), "batched_p50_us": float(np.median(t_bat)),
+        "sequential_layers_us": float(np.mean(t_seq)), "sequential_p50_us": float(np.median(t_seq)),
+        "us_per_layer_batched": float(np.mean(t_bat)) / L, "us_per_layer_sequential": float(np.mean(t_seq)) / L,
+        "hbm_footprint_gb": {"engines_one_instance_per_layer": (free0 - free1) / 1e9,
+                             "engine_batched": (free2 - free3) / 1e9,
+                             "bf16_kv_kept_by_the_benchmark": 2 * L * args.context * 4 * 256 * 2 / 1e9},
+        "ids_same_sequential_and_batched": same,
+    }
+    print(json.dumps(line))
+
+
+def run_requests(args, world, rank, device):
+    """independent requests (one query token each) split
+    contiguously over the GPUs (no collective on the data path), decoded as one
+    SeoulKV4Batch per GPU; nprobe swept; top-100 recall against the exact dense
+    top-100 of q.k over each request's retrieval tokens."""
+    from seoulkv_b200 import SeoulKV4Batch, SeoulKV4Config, SeoulKV4Index, synthetic
+
+    R = args.requests
+    lo, hi = R * rank // world, R * (rank + 1) // world
+    caches, qs = [], []
+    for r in range(lo, hi):
+        seed = 4 * 1000 + r
+        k, v, mixes = synthetic.make_kv(args.context, seed=seed, components=args.components)
+        index = SeoulKV4Index.build(k, v, sink=128, local=256, nprobe=max(int(x) for x in args.sweep.split(",")),
+                                    build_device=str(device))
+        caches.append((k.to(device), v.to(device), index))
+        qs.append(torch.stack([synthetic.make_query(args.context, mixes, seed=seed * 7919 + i).reshape(1, 16, 256)
+                               for i in range(args.warmup + args.steps)]).to(device))
+    q_all = torch.cat(qs, 1)  # [steps, n, 16, 256]
+    n = hi - lo
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    T = args.context
+    sweep = []
+    for p in (int(x) for x in args.sweep.split(",")):
+        batch = SeoulKV4Batch(device=device, caches=caches, config=SeoulKV4Config(nprobe=p, debug=True))
+        try:
+            batch.run(q_all[0].unsqueeze(1))
+            batch.synchronize()
+            ok = torch.ones(1, device=device)
+        except (ValueError, RuntimeError) as exc:
+            # the reference's first run raises the same way (a Stage-1.5 pool
+            # below 2048 keys or above capacity): this nprobe does not apply
+            ok = torch.zeros(1, device=device)
+            err = str(exc).split(";")[0]
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if ok.item() == 0:
+            batch.close()
+            sweep.append({"nprobe": p, "not_applicable": err if "err" in locals() else "another GPU's first run failed"})
+            continue
+        t = _timed_steps(args, device, flush, lambda i: batch.run(q_all[i].unsqueeze(1)))
+        # recall of the last step's ids against the exact dense top-100 (retrieval zone)
+        ids = batch.debug_snapshot()["selected_ids"].to(device)  # [n, 4, 4, 100]
+        qlast = q_all[args.warmup + args.steps - 1].float()       # [n, 16, 256]
+        hits = 0
+        for j, (k, _, _) in enumerate(caches):
+            kz = k[:, 128:T - 256].float()                          # [4, R, 256]
+            sc = torch.einsum("ghd,grd->ghr", qlast[j].view(4, 4, 256), kz)
+            top = sc.topk(100, dim=-1).indices + 128                # [4, 4, 100]
+            for g in range(4):
+                for h in range(4):
+                    hits += int(torch.isin(ids[j, g, h], top[g, h]).sum())
+        batch.close()
+        step_us = torch.tensor([float(np.mean(t))], device=device)
+        hit_t = torch.tensor([float(hits), float(n * 16 * 100)], device=device)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(step_us, op=dist.ReduceOp.MAX)
+            dist.all_reduce(hit_t)
+        sweep.append({"nprobe": p, "us_per_step": float(step_us.item()), "tokens_per_s": R / step_us.item() * 1e6,
+                      "recall_at_100": float(hit_t[0] / hit_t[1])})
+    if rank == 0:
+        ran = [x for x in sweep if "tokens_per_s" in x]
+        best = max(ran, key=lambda x: x["tokens_per_s"]) if ran else {"tokens_per_s": 0.0}
+        line = {
+            "metric": f"tokens/s batched decode, {R} requests x {T // 1024}K ctx; top-100 recall vs exact dense",
+            "value": best["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "data": "synthetic (BASELINE generator, one seed per request), fresh Q per step",
+            "config": {"workload": f"{R} independent requests, T={T}, 4 KV / 16 Q heads, d=256, one query token "
+                                   f"each, requests split contiguously over {world} GPU(s)",
+                       "l2": "flushed before every step"},
+            "sweep": sweep,
+        }
+        print(json.dumps(line))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -407,6 +580,12 @@ def main():
     from seoulkv_b200 import _native
 
     _native.FORCE_STAGED = args.staged
+    if args.requests:
+        run_requests(args, world, rank, device)
+        return
+    if args.layers:
+        run_stack(args, device)
+        return
     if world > 1:
         run_sharded(args, world, rank, local, device)
         return

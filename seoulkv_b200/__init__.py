@@ -10,8 +10,9 @@ Drop-in for the reference's Python operator API::
 """
 
 from seoulkv_b200.api import SeoulKV4
+from seoulkv_b200.batched import BatchResult, SeoulKV4Batch
 from seoulkv_b200.config import SeoulKV4Config
 from seoulkv_b200.index import SeoulKV4Index
 from seoulkv_b200.result import DecodeResult
 
-__all__ = ["DecodeResult", "SeoulKV4", "SeoulKV4Config", "SeoulKV4Index"]
+__all__ = ["BatchResult", "DecodeResult", "SeoulKV4", "SeoulKV4Batch", "SeoulKV4Config", "SeoulKV4Index"]

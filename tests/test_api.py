@@ -121,3 +121,34 @@ def test_result_liveness():
     r = DecodeResult(o, 1)
     with pytest.raises(RuntimeError):
         r.to_torch()
+
+
+def test_batch_validation_and_lifecycle(case):
+    """SeoulKV4Batch: the per-cache checks of SeoulKV4, plus shared shapes across caches."""
+    from seoulkv_b200 import SeoulKV4Batch
+
+    with pytest.raises(ValueError):
+        SeoulKV4Batch(device="cuda:0", caches=[])
+    with pytest.raises(TypeError):
+        SeoulKV4Batch(device="cuda:0", caches=[(case.k, case.v, None)])
+    with pytest.raises(ValueError):
+        SeoulKV4Batch(device="cuda:0", caches=[(case.k, case.v[:, :4096], case.index)])
+    other = Case(context=12288, nprobe=64, seed=32)
+    with pytest.raises(ValueError, match="share the context"):
+        SeoulKV4Batch(device="cuda:0", caches=[(case.k, case.v, case.index), (other.k, other.v, other.index)])
+    bad = case.k.clone()
+    bad[1, 5, 9] += 1
+    with pytest.raises(ValueError, match="fingerprint"):
+        SeoulKV4Batch(device="cuda:0", caches=[(case.k, case.v, case.index), (bad, case.v, case.index)])
+    b = SeoulKV4Batch(device="cuda:0", caches=[(case.k, case.v, case.index)] * 2,
+                      config=SeoulKV4Config(nprobe=64))
+    meta = b.metadata()
+    assert meta["caches"] == 2 and meta["initialized"] is False and meta["nprobe"] == [[64] * 4, [64] * 4]
+    with pytest.raises(ValueError):
+        b.run(torch.zeros(1, 1, 16, 256, dtype=torch.bfloat16))  # one query per cache
+    with pytest.raises(RuntimeError):
+        b.debug_snapshot()
+    b.close()
+    b.close()
+    with pytest.raises(RuntimeError):
+        b.run(torch.zeros(2, 1, 16, 256, dtype=torch.bfloat16))
