@@ -111,7 +111,11 @@ int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t 
  * host-I/O step costs one graph launch and one wait. */
 int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *stream);
 
-/* Enqueue the whole funnel for every slot on `stream` (no host sync). */
+/* Enqueue the whole funnel for every slot on `stream` (no host sync), as a
+ * replay of the engine's own step graph.  While `stream` is capturing (the
+ * caller records its own CUDA graph, e.g. a model's decode step), the step's
+ * kernels are captured into the caller's graph instead; the query must then
+ * be device-resident (SKV_E_STATE otherwise). */
 int skv_run(void *handle, void *stream);
 
 /* Wait for all work of this engine, then check the device status words:

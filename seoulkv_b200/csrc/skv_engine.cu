@@ -477,6 +477,23 @@ int skv_run(void *handle, void *stream) {
   if (rc) return rc;
   CK(cudaSetDevice(e->desc.device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL: legacy default stream
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(st, &cap));
+  if (cap != cudaStreamCaptureStatusNone) {
+    // the caller is capturing its own graph (e.g. a model's decode step):
+    // the step's kernels go into that graph directly; the query must already
+    // be on the device (a host query's pinned staging copy is not capturable
+    // as a step of the caller's graph)
+    if (e->q_host) return fail(SKV_E_STATE, "a captured run needs a device-resident query");
+    Work w = e->work;
+    if (e->link.active) {
+      w.link = e->link.dev;
+      w.shard_gids = e->link.gids;
+    }
+    CK(launch_step(e, w, st));
+    e->host_io = false;
+    return SKV_OK;
+  }
   const bool host = e->q_host;
   cudaGraphExec_t &exec = host ? e->exec_host : e->exec;
   if (!exec) {
