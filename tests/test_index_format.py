@@ -74,6 +74,7 @@ def test_load_rejects_corrupt_files(case, tmp_path):
 
 
 @pytest.mark.skipif(not HAVE_REF, reason="reference package not importable here")
+@pytest.mark.skipif(not HAVE_REF, reason="needs the reference package")
 def test_reference_loads_our_dump_and_we_load_theirs(case, tmp_path):
     sys.path.insert(0, REF)
     from seoulkv4 import SeoulKV4Index as RefIndex
@@ -90,3 +91,36 @@ def test_reference_loads_our_dump_and_we_load_theirs(case, tmp_path):
     for a, b in zip(built._cells, back.cells()):
         _cells_equal(a, b)
     assert back.metadata() == built.metadata()
+
+
+@pytest.mark.skipif(not HAVE_REF, reason="needs the reference package (its fixture writer)")
+def test_legacy_v3_grouped_fixture_loads(case, tmp_path):
+    """A version-3 grouped fixture (the index cells plus a diagnostic replay
+    query), written by the reference's own ``save_fixture``, opens as an index:
+    the query fields are dropped and every index array equals the source's."""
+    sys.path.insert(0, REF)
+    from seoulkv4._codecs import index as ref_codec
+
+    cells = []
+    g = torch.Generator().manual_seed(5)
+    for c in case.index.cells():
+        nc = int(c["centroids"].shape[0])
+        f = dict(c)
+        f["q"] = torch.randn(4, 256, generator=g).bfloat16()
+        f["coarse_ids"] = torch.arange(nc, dtype=torch.int32)
+        f["head_mask"] = torch.full((nc,), 15, dtype=torch.int32)
+        cells.append(f)
+    path = tmp_path / "grouped_v3.npz"
+    ref_codec.save_fixture(path, cells, {"source": "test"})
+    loaded, meta = _codecs.load_index(path)
+    assert meta["version"] == 3
+    for src, got in zip(case.index.cells(), loaded):
+        assert not ({"q", "coarse_ids", "head_mask"} & got.keys())
+        for name, value in src.items():
+            if isinstance(value, torch.Tensor):
+                ref = value.float() if value.dtype == torch.bfloat16 else value  # v3 stores BF16 as FP32
+                assert torch.equal(got[name].to(ref.dtype), ref), name
+            else:
+                assert got[name] == value, name
+    idx = SeoulKV4Index.load(path, nprobe=64)
+    assert idx.nprobe == (64, 64, 64, 64)
