@@ -103,7 +103,7 @@ struct FusedSmem {
   unsigned long long mb_sh;        // the survivor share (once per step)
   unsigned long long mb_pool, mb_s2, mb_win, mb_attn;  // pool share, Stage-II keys, winners, attention partials
   alignas(16) int win[G][TOPK];    // the step's top-100 tokens per head (pushed by CTA h)
-  int ph_in, ph_res, ph_x, ph_pad; // phases of mb_in / mb_res / exchanges completed so far
+  int ph_in, ph_res, ph_x, ph_pend; // phases of mb_in / mb_res / exchanges started so far; the pending exchange
   int all[CL][4];                  // the cluster's values of the latest exchange
   SelCtl ctl;
   int shift[3][4];
@@ -298,19 +298,32 @@ __device__ __forceinline__ void load_frag(const FusedSmem &S, int row, int lane,
 // arrivals.  Consecutive exchanges alternate slots and mbarriers: a CTA can
 // only start exchange k + 2 after every CTA has sent exchange k + 1, which
 // each does after its wait for exchange k.
-__device__ __noinline__ void exchange(FusedSmem &S, int v0, int v1, int v2, int v3) {
+__device__ __noinline__ void exchange_send(FusedSmem &S, int v0, int v1, int v2, int v3) {
   const int tid = threadIdx.x;
   const int k = S.ph_x, b = k & 1;
   const uint32_t rank = cluster_rank();
   __syncthreads();  // every thread has read ph_x
-  if (tid == 0) S.ph_x = k + 1;
+  if (tid == 0) {
+    S.ph_x = k + 1;
+    S.ph_pend = k;
+  }
   if (tid < CL)
     st_async_v4(remote(&S.xin[b][rank][0], (uint32_t)tid), remote(&S.mb_x[b], (uint32_t)tid),
                 make_uint4((uint32_t)v0, (uint32_t)v1, (uint32_t)v2, (uint32_t)v3));
   if (tid == 0) mbar_expect_tx(&S.mb_x[b], CL * 16);
+}
+// The second half of exchange(): independent work may run between the two.
+__device__ __noinline__ void exchange_wait(FusedSmem &S) {
+  const int tid = threadIdx.x;
+  __syncthreads();  // ph_pend is set
+  const int k = S.ph_pend, b = k & 1;
   mbar_wait_cluster(&S.mb_x[b], (uint32_t)(k >> 1) & 1u, &S.status);
   if (tid < CL * 4) S.all[tid >> 2][tid & 3] = S.xin[b][tid >> 2][tid & 3];
   __syncthreads();
+}
+__device__ __forceinline__ void exchange(FusedSmem &S, int v0, int v1, int v2, int v3) {
+  exchange_send(S, v0, v1, v2, v3);
+  exchange_wait(S);
 }
 __device__ __forceinline__ int before(const FusedSmem &S, int k, int rank) {
   int s = 0;
@@ -1264,7 +1277,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
           }
         }
       }
-      {
+      if (m15 > BATCH_FINE) {
+        // the share spans several staging batches: Stage-1.6 scores of every
+        // position now (a single batch keeps its rows, and P8 scores only
+        // the union members)
         BFrag F;
         load_frag(S, R_QS, lane, F);
         const Pow2 s16A = pow2s(S.shift[R_QS][hA] + 4), s16B = pow2s(S.shift[R_QS][hB] + 4);
@@ -1322,7 +1338,37 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         r += f[j];
       }
   }
-  exchange(S, nu, 0, 0, 0);
+  exchange_send(S, nu, 0, 0, 0);
+  if (m15 <= BATCH_FINE && nu > 0) {
+    // Stage-1.6 scores of this CTA's union members only, from the rows P7
+    // left in the staging area (row i at i * STRIDE_FINE), while the union
+    // counts travel; members listed in union order in clist (free until P10)
+    for (int i = tid; i < m15; i += FT)
+      if (S.b.p.flag[i]) S.b.p.clist[S.b.p.urank[i]] = (uint16_t)i;
+    __syncthreads();
+    BFrag F;
+    load_frag(S, R_QS, lane, F);
+    const Pow2 s16A = pow2s(S.shift[R_QS][hA] + 4), s16B = pow2s(S.shift[R_QS][hB] + 4);
+    const int tiles = (nu + 15) >> 4;
+    for (int tile = warp; tile < tiles; tile += FW) {
+      const int rg = tile * 16 + gq, r8 = rg + 8;
+      long long dh[2];
+      tile_dots<1>(S.big + S.b.p.clist[min(rg, nu - 1)] * STRIDE_FINE,
+                   S.big + S.b.p.clist[min(r8, nu - 1)] * STRIDE_FINE, t, F, dh);
+      const int row = (t & 1) ? r8 : rg;
+      if (row < nu) {
+        const int i = S.b.p.clist[row];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int h = k ? hB : hA;
+          // operand 16*qs, weights 2*c4 - 15: the same digits, scale 2^4 higher
+          S.b.p.sc16[h][i] = (uint16_t)ord16(
+              bf16_score(exact_to_float(2 * dh[k] - 15 * S.sxsum[R_QS][h], k ? s16B : s16A)));
+        }
+      }
+    }
+  }
+  exchange_wait(S);
   const int u_base = before(S, 0, rank), nu_all = min(total(S, 0), U15_MAX);
   for (int i = tid; i < m15; i += FT) {
     if (!S.b.p.flag[i]) continue;
