@@ -186,8 +186,8 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // The two halves of cluster_sync(), for overlapping independent work.
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -825,6 +825,29 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (tid < (nrows >> 5)) s4 = c.coarse_scale4[(r0 >> 5) + tid];
 #pragma unroll
     for (int k = 0; k < 2; ++k) fs[k] = tid + k * FT < (nc >> 5) ? c.fine_scale[tid + k * FT] : 0.0f;
+    if (tid == 0) {
+      // the coarse slice goes out right behind the small loads (the stores
+      // below wait for those), with every mbarrier of the step initialised
+      for (int k = 0; k < NCHUNK; ++k) mbar_init(&S.mbar[k], 1);
+      mbar_init(&S.mb_in, 1);
+      mbar_init(&S.mb_res, 1);
+      mbar_init(&S.mb_x[0], 1);
+      mbar_init(&S.mb_x[1], 1);
+      mbar_init(&S.mb_sh, 1);
+      mbar_init(&S.mb_pool, 1);
+      mbar_init(&S.mb_s2, 1);
+      mbar_init(&S.mb_win, 1);
+      mbar_init(&S.mb_attn, 1);
+      S.ph_in = S.ph_res = S.ph_x = 0;
+      S.status = 0;
+      mbar_fence_init();
+      for (int k = 0; k * SLICE_CHUNK < nrows; ++k) {
+        const int rows = min(SLICE_CHUNK, nrows - k * SLICE_CHUNK);
+        mbar_expect_tx(&S.mbar[k], (uint32_t)rows * 64u);
+        bulk_g2s(S.big + k * SLICE_CHUNK * 64, c.upper + (size_t)(r0 + k * SLICE_CHUNK) * 64, (uint32_t)rows * 64u,
+                 &S.mbar[k]);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < 2; ++k) S.sx[tid + k * FT] = bf16f(qv[k]);
     if (tid < D) S.kscale[tid] = ks;
@@ -840,27 +863,6 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (tid < (nrows >> 5)) w.selbits[(size_t)cell * (nc >> 5) + (r0 >> 5) + tid] = 0u;
   }
   for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0u;  // (P1 adds the coarse first round)
-  if (tid == 0) {
-    for (int k = 0; k < NCHUNK; ++k) mbar_init(&S.mbar[k], 1);
-    mbar_init(&S.mb_in, 1);
-    mbar_init(&S.mb_res, 1);
-    mbar_init(&S.mb_x[0], 1);
-    mbar_init(&S.mb_x[1], 1);
-    mbar_init(&S.mb_sh, 1);
-    mbar_init(&S.mb_pool, 1);
-    mbar_init(&S.mb_s2, 1);
-    mbar_init(&S.mb_win, 1);
-    mbar_init(&S.mb_attn, 1);
-    S.ph_in = S.ph_res = S.ph_x = 0;
-    mbar_fence_init();
-    for (int k = 0; k * SLICE_CHUNK < nrows; ++k) {
-      const int rows = min(SLICE_CHUNK, nrows - k * SLICE_CHUNK);
-      mbar_expect_tx(&S.mbar[k], (uint32_t)rows * 64u);
-      bulk_g2s(S.big + k * SLICE_CHUNK * 64, c.upper + (size_t)(r0 + k * SLICE_CHUNK) * 64, (uint32_t)rows * 64u,
-               &S.mbar[k]);
-    }
-    S.status = 0;
-  }
   __syncthreads();
   mark(M_ISSUE);
   static_assert(FW == 16, "12 operand-row warps + 4 norm warps");
@@ -941,9 +943,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   __syncthreads();
   mark(M_QEXP);
   mark(M_QPREP);
-  // this CTA has started and its owner bins are zero; the matching wait
-  // precedes the first distributed-shared-memory access (P2)
-  cluster_arrive();
+  // this CTA has started and its mbarriers are initialised (made visible by
+  // fence.mbarrier_init above, so the arrive can be relaxed); the matching
+  // wait precedes the first push into another CTA (P2)
+  cluster_arrive_relaxed();
   __syncthreads();
   mark(M_STARTED);
 
