@@ -118,6 +118,15 @@ int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *str
  * be device-resident (SKV_E_STATE otherwise). */
 int skv_run(void *handle, void *stream);
 
+/* skv_bind_query + skv_run in one call (one host crossing per step). */
+int skv_step(void *handle, const uint16_t *q, int32_t on_device, void *stream);
+
+/* Wait for the last step, fill *status (if not NULL) and copy the output
+ * [n_slots][16][256] BF16 into host memory `out` (if not NULL); returns
+ * SKV_E_CAPACITY, after filling both, when a cell reported a live count out
+ * of range.  skv_sync + skv_status + skv_output in one call. */
+int skv_finish(void *handle, uint16_t *out, SkvStatus *status);
+
 /* Wait for all work of this engine, then check the device status words:
  * returns SKV_E_CAPACITY if any cell reported a live count out of range. */
 int skv_sync(void *handle);

@@ -26,7 +26,7 @@ EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
     "skv_upload_kv", "skv_bind_query", "skv_run", "skv_sync", "skv_status", "skv_output",
     "skv_debug_ids", "skv_read_stage", "skv_traffic", "skv_profile_step", "skv_kernel_name",
-    "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name", "skv_profile_ctas",
+    "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name", "skv_profile_ctas", "skv_step", "skv_finish",
     "skv_shard_outputs", "skv_shard_merge", "skv_shard_attention", "skv_shard_combine",
     "skv_shard_setup", "skv_shard_connect", "skv_shard_ipc_handle_bytes", "skv_shard_gids",
 )
@@ -115,6 +115,8 @@ def load() -> ctypes.CDLL:
         lib.skv_profile_phases.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
         lib.skv_phase_name.restype = ctypes.c_char_p
+        lib.skv_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        lib.skv_finish.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.skv_profile_ctas.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
                                          ctypes.POINTER(ctypes.c_float), ctypes.c_void_p, ctypes.c_int32]
@@ -204,6 +206,16 @@ class Engine:
 
     def run(self, stream: int = 0) -> None:
         check(self.lib.skv_run(self.handle, ctypes.c_void_p(stream or None)), "skv_run")
+
+    def step(self, q_ptr: int, on_device: bool, stream: int = 0) -> None:
+        """bind_query + run in one call."""
+        check(self.lib.skv_step(self.handle, ctypes.c_void_p(q_ptr), int(on_device),
+                                ctypes.c_void_p(stream or None)), "skv_step")
+
+    def finish(self, out: np.ndarray | None) -> None:
+        """Wait for the last step; copy its output into `out` (uint16 [n_slots, 16, 256]) if given.
+        Raises NativeError (SKV_E_CAPACITY) when a live count left its range."""
+        check(self.lib.skv_finish(self.handle, None if out is None else _ptr(out), None), "skv_finish")
 
     def sync(self) -> None:
         check(self.lib.skv_sync(self.handle), "skv_sync")

@@ -115,8 +115,12 @@ class SeoulKV4:
         if first:
             self._engine = self._initialize()
             self._host_kv = None
-        self._bind_query(q)
-        self._engine.run(self._stream())
+        eng = self._engine
+        if q.device.type == "cuda":
+            qd = _bits(q.to(f"cuda:{self._device_index}"))
+            eng.step(qd.data_ptr(), True, self._stream())
+        else:
+            eng.step(_bits(q).data_ptr(), False, self._stream())
         self._generation += 1
         if first:
             # the reference's first run checks the live pool against capacity

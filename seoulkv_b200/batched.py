@@ -19,6 +19,7 @@ from __future__ import annotations
 
 from typing import Sequence
 
+import numpy as np
 import torch
 
 from seoulkv_b200 import _native
@@ -44,9 +45,12 @@ class BatchResult:
     def to_torch(self) -> torch.Tensor:
         """Synchronise and copy the outputs into a CPU BF16 tensor [n, 1, 16, 256]."""
         o = self._live()
-        o.synchronize()
-        out = o._engine.output_host()  # uint16 [n, 16, 256]
-        return torch.from_numpy(out.view("int16")).view(torch.bfloat16).reshape(o.n, 1, N_HEADS, 256).clone()
+        out = np.empty((o.n, N_HEADS, 256), dtype=np.uint16)
+        try:
+            o._engine.finish(out)  # wait, status check and output copy in one native call
+        except _native.NativeError as exc:
+            raise RuntimeError(str(exc)) from exc
+        return torch.from_numpy(out.view(np.int16)).view(torch.bfloat16).reshape(o.n, 1, N_HEADS, 256)
 
     @property
     def device_tensor(self) -> torch.Tensor:
@@ -150,10 +154,9 @@ class SeoulKV4Batch:
             self._caches = [(None, None, c[2]) for c in self._caches]  # K/V now live on the device
         if q.device.type == "cuda":
             qd = _bits(q.to(f"cuda:{self._device_index}"))
-            self._engine.bind_query(qd.data_ptr(), True, self._stream())
+            self._engine.step(qd.data_ptr(), True, self._stream())
         else:
-            self._engine.bind_query(_bits(q).data_ptr(), False, self._stream())
-        self._engine.run(self._stream())
+            self._engine.step(_bits(q).data_ptr(), False, self._stream())
         self._generation += 1
         if first:
             st = self._engine.status()

@@ -535,6 +535,38 @@ int skv_run(void *handle, void *stream) {
   return SKV_OK;
 }
 
+int skv_step(void *handle, const uint16_t *q, int32_t on_device, void *stream) {
+  int rc = skv_bind_query(handle, q, on_device, stream);
+  return rc ? rc : skv_run(handle, stream);
+}
+
+int skv_finish(void *handle, uint16_t *out, SkvStatus *status) {
+  Engine *e = as_engine(handle);
+  if (!e) return fail(SKV_E_INVALID, "null engine");
+  SkvStatus s{};
+  int rc = skv_status(handle, &s);
+  if (rc) return rc;
+  if (status) *status = s;
+  if (out) {
+    if (e->host_io) {
+      std::memcpy(out, e->out_pinned, (size_t)e->desc.n_slots * 16 * D * 2);
+    } else {
+      CK(cudaMemcpy(out, e->work.out, (size_t)e->desc.n_slots * 16 * D * 2, cudaMemcpyDeviceToHost));
+    }
+  }
+  if (s.flags) {
+    char msg[256];
+    std::snprintf(msg, sizeof msg,
+                  "live count out of range at cell %d (status 0x%x: %s%s%s); pool range [%d, %d], capacity %d",
+                  s.first_bad_cell, s.flags, (s.flags & SKV_STATUS_POOL_OVER) ? "pool above capacity " : "",
+                  (s.flags & SKV_STATUS_POOL_UNDER) ? "pool below 2048 " : "",
+                  (s.flags & SKV_STATUS_FINE_SHORT) ? "fewer than nprobe survivors" : "", s.pool_min,
+                  s.pool_max, e->desc.stage15_capacity);
+    return fail(SKV_E_CAPACITY, msg);
+  }
+  return SKV_OK;
+}
+
 int skv_status(void *handle, SkvStatus *out) {
   Engine *e = as_engine(handle);
   if (!e || !out) return fail(SKV_E_INVALID, "null engine or output");

@@ -4,7 +4,10 @@ from __future__ import annotations
 
 import weakref
 
+import numpy as np
 import torch
+
+from seoulkv_b200 import _native
 
 
 class _DeviceBuffer:
@@ -40,8 +43,13 @@ class DecodeResult:
         return tuple(base[4 * g:4 * g + 4].unsqueeze(0) for g in range(4))
 
     def to_torch(self) -> torch.Tensor:
-        """Synchronise and copy the output into a CPU BF16 tensor [1, 1, 16, 256]."""
+        """Synchronise and copy the output into a CPU BF16 tensor [1, 1, 16, 256]
+        (RuntimeError if a live count left its range, as ``synchronize``)."""
         owner = self._owner()
-        owner.synchronize()
-        out = owner._require_initialized().output_host()
-        return torch.from_numpy(out[0].view("int16")).view(torch.bfloat16).reshape(1, 1, 16, 256).clone()
+        eng = owner._require_initialized()
+        out = np.empty((eng.n_slots, 16, 256), dtype=np.uint16)
+        try:
+            eng.finish(out)  # wait, status check and output copy in one native call
+        except _native.NativeError as exc:
+            raise RuntimeError(str(exc)) from exc
+        return torch.from_numpy(out[0].view(np.int16)).view(torch.bfloat16).reshape(1, 1, 16, 256)
