@@ -20,6 +20,7 @@ Tenstorrent board) on this host's cores, on a bounded sample of steps.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -405,12 +406,15 @@ def _timed_steps(args, device, flush, step_fn):
         step_fn(i)
     torch.cuda.synchronize(device)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    gc.disable()
+    torch.cuda._sleep(int(2e7))  # the host enqueues ahead of the device
     for i in range(args.steps):
         flush.zero_()
         ev[i][0].record(stream)
         step_fn(args.warmup + i)
         ev[i][1].record(stream)
     torch.cuda.synchronize(device)
+    gc.enable()
     return np.array([a.elapsed_time(b) * 1e3 for a, b in ev])
 
 
@@ -605,8 +609,7 @@ def main():
     qbits = q_dev.view(torch.int16)
 
     def step(i):
-        eng.bind_query(qbits[i].data_ptr(), True, stream.cuda_stream)
-        eng.run(stream.cuda_stream)
+        eng.step(qbits[i].data_ptr(), True, stream.cuda_stream)
 
     for i in range(args.warmup):
         flush.zero_()
@@ -620,12 +623,18 @@ def main():
     torch.cuda.synchronize(device)
     clocks.start()
     time.sleep(0.3)
+    # the host enqueues ahead of the device (a short device-side sleep before
+    # the first timed step; no garbage collection meanwhile), so that no host
+    # pause falls between a step's start event and its launch
+    gc.disable()
+    torch.cuda._sleep(int(2e7))
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
         step(args.warmup + i)
         ends[i].record(stream)
     torch.cuda.synchronize(device)
+    gc.enable()
     if world > 1:
         torch.distributed.barrier()
     clk = clocks.stop()
