@@ -67,6 +67,7 @@ struct ShardLinkDev {
   int32_t rank, n_shards, token_begin;
   int32_t total, sink, local;     // the whole layer's context and dense zones
   uint32_t *epoch;                // steps completed (device counter)
+  uint32_t *exits;                // clusters of the current fused step that have finished
 };
 
 // Cross-GPU flags: release/acquire at system scope; bounded polls.

@@ -102,6 +102,7 @@ ShardLinkDev link_view(const Engine *e) {
   L.n_shards = e->link.n;
   L.token_begin = e->link.begin[e->link.rank];
   L.epoch = e->link.epoch;
+  L.exits = e->link.epoch + 1;
   return L;
 }
 
@@ -112,7 +113,8 @@ cudaError_t launch_step(const Engine *e, const Work &w, cudaStream_t st) {
   if (r != cudaSuccess || !e->link.active) return r;
   // the fused kernel exchanges inside itself (Work::link); the staged path
   // runs the exchange kernels after its funnel
-  if (!e->fused) r = launch_shard_p2p_step(w, link_view(e), e->link.gids, e->link.part, w.counts + C_STATUS, st);
+  if (e->fused) return r;  // the fused kernel advances the step counter itself
+  r = launch_shard_p2p_step(w, link_view(e), e->link.gids, e->link.part, w.counts + C_STATUS, st);
   return r == cudaSuccess ? launch_shard_epoch(e->link.dev, st) : r;
 }
 
@@ -787,7 +789,7 @@ int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t 
   e->link.n = n_shards;
   CK(cudaMalloc(&e->link.region, shard_region_bytes()));
   CK(cudaMemset(e->link.region, 0, shard_region_bytes()));
-  int rc = dalloc(e, &e->link.epoch, 1);
+  int rc = dalloc(e, &e->link.epoch, 2);  // [0] steps completed, [1] the fused step's finished clusters
   if (!rc) rc = dalloc(e, &e->link.gids, (size_t)SHARD_CELLS * G * TOPK);
   if (!rc) rc = dalloc(e, &e->link.part, (size_t)SHARD_CELLS * G * PART);
   if (rc) return rc;
@@ -932,8 +934,7 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
     w.shard_gids = e->link.gids;
   }
   e->host_io = false;
-  CK(launch_fused(w, st));
-  if (e->link.active) CK(launch_shard_epoch(e->link.dev, st));
+  CK(launch_fused(w, st));  // (with a connected group, the kernel advances the step counter)
   CK(cudaMemcpyAsync(ts.data(), e->phase_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   CK(cudaEventRecord(e->done, st));

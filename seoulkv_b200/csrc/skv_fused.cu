@@ -1413,7 +1413,21 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     for (int j = 0; j < 2; ++j)
       if (f[j]) S.b.p.clist[r++] = (uint16_t)(i0 + j);
   }
-  exchange(S, ncl, 0, 0, 0);
+  exchange_send(S, ncl, 0, 0, 0);
+  // the first batch of the candidates' Stage-II rows goes out while the
+  // candidate counts travel
+  auto s2_gather = [&](int b0, int nb) {
+    for (int q = tid; q < nb * 16; q += FT) {
+      const int rr = q >> 4, part = q & 15;
+      const int tok = S.b.p.tok[S.b.p.clist[b0 + rr]];
+      const uint8_t *src = part < 4   ? c.prefix2 + (size_t)tok * 64 + part * 16
+                           : part < 8 ? c.residual2 + (size_t)tok * 64 + (part - 4) * 16
+                                      : c.residual4 + (size_t)tok * 128 + (part - 8) * 16;
+      cp16(S.big + rr * STRIDE_S2 + part * 16, src);
+    }
+  };
+  s2_gather(0, min(BATCH_S2, ncl));
+  exchange_wait(S);
   const int c_base = before(S, 0, rank), ncand = min(total(S, 0), CAND_MAX);
   if (rank == 0 && tid == 0) counts[C_CAND] = ncand;
   // candidates: their union position; their Stage-II keys (8-bit scores of
@@ -1436,14 +1450,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     const Pow2 s2A = pow2s(S.shift[R_QS][hA]), s2B = pow2s(S.shift[R_QS][hB]);
     for (int b0 = 0; b0 < ncl; b0 += BATCH_S2) {
       const int nb = min(BATCH_S2, ncl - b0);
-      __syncthreads();
-      for (int q = tid; q < nb * 16; q += FT) {
-        const int rr = q >> 4, part = q & 15;
-        const int tok = S.b.p.tok[S.b.p.clist[b0 + rr]];
-        const uint8_t *src = part < 4   ? c.prefix2 + (size_t)tok * 64 + part * 16
-                             : part < 8 ? c.residual2 + (size_t)tok * 64 + (part - 4) * 16
-                                        : c.residual4 + (size_t)tok * 128 + (part - 8) * 16;
-        cp16(S.big + rr * STRIDE_S2 + part * 16, src);
+      if (b0 > 0) {
+        __syncthreads();
+        s2_gather(b0, nb);
       }
       cp_wait_all();
       __syncthreads();
@@ -1604,55 +1613,62 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         }
       }
     }
-    auto record = [&](int j, uint2 &kb, uint2 &vb) {
+    auto record = [&](int j) -> const uint8_t * {
       const int tok = __shfl_sync(0xffffffffu, my_tok, j);
-      const uint8_t *rec;
       if (Lk) {
         int s = 0;
         while (s + 1 < Lk->n_shards && Lk->begin[s + 1] <= tok) ++s;
-        rec = Lk->kv8[s][cell] + (size_t)(tok - Lk->begin[s]) * REC;
-      } else {
-        rec = c.kv8 + (size_t)tok * REC;
+        return Lk->kv8[s][cell] + (size_t)(tok - Lk->begin[s]) * REC;
       }
-      kb = *reinterpret_cast<const uint2 *>(rec + 8 * lane);
-      vb = *reinterpret_cast<const uint2 *>(rec + 256 + 8 * lane);
+      return c.kv8 + (size_t)tok * REC;
     };
-    uint2 kb, vb;
-    if (nmine > 0) record(0, kb, vb);
+    // the records of up to SB of this warp's items are copied into its
+    // staging slots together (cp.async, one memory latency per batch rather
+    // than one per item), then folded in order
+    constexpr int SB = 4;
+    static_assert(88 * 1024 + FW * SB * REC <= BIG, "attention staging fits the staging area");
+    uint8_t *stg = S.big + 88 * 1024 + warp * SB * REC;  // clear of ao/am/al, part and pin
 #pragma unroll 1
-    for (int j = 0; j < nmine; ++j) {
-      const int head = __shfl_sync(0xffffffffu, my_head, j);
-      if (head == -2) {  // (warp-uniform)
-        if (j + 1 < nmine) record(j + 1, kb, vb);
-        continue;
+    for (int j0 = 0; j0 < nmine; j0 += SB) {
+      const int nb = min(SB, nmine - j0);
+#pragma unroll 1
+      for (int u = 0; u < nb; ++u) cp16(stg + u * REC + 16 * lane, record(j0 + u) + 16 * lane);
+      cp_wait_all();
+      __syncwarp();
+#pragma unroll 1
+      for (int u = 0; u < nb; ++u) {
+        const int head = __shfl_sync(0xffffffffu, my_head, j0 + u);
+        if (head == -2) continue;  // (warp-uniform)
+        const uint2 kb = *reinterpret_cast<const uint2 *>(stg + u * REC + 8 * lane);
+        const uint2 vb = *reinterpret_cast<const uint2 *>(stg + u * REC + 256 + 8 * lane);
+        float kf[8], vf[8];
+        fp8x8(kb, kf);
+        fp8x8(vb, vf);
+        float dot[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float a = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a = fmaf(qv[h][e], kf[e], a);
+          dot[h] = a;
+        }
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+          for (int h = 0; h < G; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o2);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          if (head >= 0 && head != h) continue;
+          const float mn = fmaxf(m[h], dot[h]);
+          const float scale = exp2f(m[h] - mn);
+          const float p = exp2f(dot[h] - mn);
+          l[h] = l[h] * scale + p;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[h][e] = fmaf(o[h][e], scale, p * vf[e]);
+          m[h] = mn;
+        }
       }
-      float kf[8], vf[8];
-      fp8x8(kb, kf);
-      fp8x8(vb, vf);
-      if (j + 1 < nmine) record(j + 1, kb, vb);
-      float dot[G];
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float a = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a = fmaf(qv[h][e], kf[e], a);
-        dot[h] = a;
-      }
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1)
-#pragma unroll
-        for (int h = 0; h < G; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o2);
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        if (head >= 0 && head != h) continue;
-        const float mn = fmaxf(m[h], dot[h]);
-        const float scale = exp2f(m[h] - mn);
-        const float p = exp2f(dot[h] - mn);
-        l[h] = l[h] * scale + p;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[h][e] = fmaf(o[h][e], scale, p * vf[e]);
-        m[h] = mn;
-      }
+      __syncwarp();  // the slots are read before the next batch lands
     }
     mark(M_ATTN_ITEMS);
     // warps -> CTA partial per head
@@ -1727,6 +1743,15 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   mark(M_ATTN);
   if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
   cluster_sync();  // no CTA leaves while its shared memory may still be read
+  if (w.link && rank == 0 && tid == 0) {
+    // the last cluster of the step to finish advances the group's step
+    // counter (every cluster read it in P12, before this barrier)
+    const ShardLinkDev *Lk = w.link;
+    if (atomicAdd(Lk->exits, 1u) == (uint32_t)w.n_cells - 1u) {
+      *Lk->exits = 0u;
+      *Lk->epoch += 1u;
+    }
+  }
   if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank) + 1] = (long long)global_ns();
 }
 
