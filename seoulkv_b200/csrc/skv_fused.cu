@@ -390,12 +390,26 @@ __device__ __forceinline__ uint32_t select_key(const FusedSmem &S, int kind, int
 template <int KIND>
 __device__ __forceinline__ void hist_pass(uint32_t *hist, const FusedSmem &S, int nloc, int q0,
                                           const uint32_t (&pf)[4], const uint32_t (&mk)[4], int sh) {
+  if constexpr (KIND == KEY_COARSE) {
+    // two 16-bit keys per 32-bit load (nloc is even: a slice is whole 16-row tiles)
 #pragma unroll 1
-  for (int i = threadIdx.x; i < nloc; i += FT) {
+    for (int i = 2 * threadIdx.x; i < nloc; i += 2 * FT) {
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const uint32_t v = select_key(S, KIND, h, i, q0);
-      if ((v & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v >> sh) & 255u)], 1u);
+      for (int h = 0; h < 4; ++h) {
+        const uint32_t two = *reinterpret_cast<const uint32_t *>(&S.b.c.lo[h][i]);
+        const uint32_t v0 = two << 16, v1 = two & 0xffff0000u;
+        if ((v0 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v0 >> sh) & 255u)], 1u);
+        if ((v1 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v1 >> sh) & 255u)], 1u);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int i = threadIdx.x; i < nloc; i += FT) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint32_t v = select_key(S, KIND, h, i, q0);
+        if ((v & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v >> sh) & 255u)], 1u);
+      }
     }
   }
 }

@@ -84,3 +84,30 @@ def test_device_query_and_replay(case, cuda, path):
         attn.run(case.query(202))
         attn.run(q)
         assert torch.equal(attn.debug_snapshot()["selected_ids"], ids1)
+
+
+@pytest.mark.parametrize("context,nprobe,capacity,staged", [
+    (6400, 256, 13056, False),                    # the smallest context the profile accepts
+    (16384, (128, 192, 256, 512), 13056, False),  # a different nprobe per KV head
+    (32768, 512, 15360, False),                   # the largest nprobe, a larger Stage-1.5 capacity
+    (32768, 512, 15360, True),
+], ids=["6400-256", "16384-perhead", "32768-512-fused", "32768-512-staged"])
+def test_parity_sweep(cuda, monkeypatch, context, nprobe, capacity, staged):
+    """Every stage bit-exact and the output within tolerance across contexts,
+    per-head nprobe and capacities."""
+    monkeypatch.setattr(_native, "FORCE_STAGED", staged)
+    case = Case(context=context, nprobe=64, seed=61)
+    cfg = SeoulKV4Config(debug=True, nprobe=nprobe, stage15_capacity=capacity)
+    per_head = [nprobe] * 4 if isinstance(nprobe, int) else list(nprobe)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
+        for qseed in (1, 2):
+            q = case.query(qseed)
+            y = attn.run(q).to_torch()
+            assert attn._engine.fused == (not staged)
+            res, ref_out = case.oracle(q, capacity=capacity, nprobe=per_head)
+            _compare(attn._engine, res, case.index.cells()[0]["centroids"].shape[0], capacity)
+            ids = attn.debug_snapshot()["selected_ids"].numpy()
+            assert np.array_equal(ids, np.stack([r["final_ids"] for r in res])), "selected token ids"
+            got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
+            err = np.abs(got - O.bf16_to_f32(ref_out).astype(np.float64))
+            assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
