@@ -76,6 +76,10 @@ constexpr int STRIDE_FINE = 144;   // upper | lower
 constexpr int STRIDE_S2 = 272;     // prefix2 | residual2 | residual4
 constexpr int BATCH_FINE = (BIG / STRIDE_FINE) & ~15;
 constexpr int BATCH_S2 = (BIG / STRIDE_S2) & ~15;
+// kept pool tokens a CTA stages (P6): only pool positions below the capacity
+// (<= CL * POS_MAX) are used, so a CTA keeps at most that many
+constexpr int KMAX = CL * POS_MAX;
+static_assert(KMAX * 4 <= BIG, "kept tokens fit the staging area");
 
 struct SelCtl {
   uint32_t prefix[4], mask[4], krem[4], th[4];
@@ -1039,7 +1043,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         ++r;
       }
   }
-  // posting lists a survivor would bring into the pool (into L2)
+  exchange_send(S, nsurv, 0, 0, 0);
+  // posting lists a survivor would bring into the pool (into L2), while the
+  // survivor counts travel
   for (int k = tid; k < nsurv; k += FT) {
     const int lr = S.sidx[k], b = S.offs[lr], e = S.offs[lr + 1];
     if (e > b) {
@@ -1051,7 +1057,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       }
     }
   }
-  exchange(S, nsurv, 0, 0, 0);
+  exchange_wait(S);
   const int surv_base = before(S, 0, rank), nsurv_all = total(S, 0);
   // The Fine work is balanced over the cluster: CTA r scores the survivors at
   // global positions [r L, r L + L), L = ceil(survivors / 16) (positions stay
@@ -1172,7 +1178,31 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (tid == 0) S.b.s.ppre[nsel] = npost;
   }
   mark(M_SELLIST);
-  exchange(S, nsel, npost, 0, 0);  // (also orders the selected bits before the mate rule reads them)
+  exchange_send(S, nsel, npost, 0, 0);  // (also orders the selected bits before the mate rule reads them)
+  // this CTA's postings (their clusters, mates and tokens) load while the
+  // counts travel; the mate rule, which reads every CTA's selected bits, runs
+  // after the wait (one pass covers up to 4 * FT postings)
+  auto posting = [&](int p, int &jj, int &cid) {
+    jj = -1;
+    cid = 0;
+    if (p < npost) {
+      int lo = 0, hi = nsel - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (S.b.s.ppre[mid] <= p) lo = mid; else hi = mid - 1;
+      }
+      cid = S.b.s.slist[lo];
+      jj = S.b.s.soff[lo] + (p - S.b.s.ppre[lo]);
+    }
+  };
+  int pj[4], pc_[4], pm[4], pt[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    posting(tid * 4 + j, pj[j], pc_[j]);
+    pm[j] = pj[j] >= 0 ? c.mates[pj[j]] : -1;
+    pt[j] = pj[j] >= 0 ? c.values[pj[j]] : 0;
+  }
+  exchange_wait(S);
   const int sel_base = before(S, 0, rank), nsel_all = total(S, 0), npost_all = total(S, 1);
   for (int k = tid; k < nsel; k += FT)
     if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = S.b.s.slist[k];
@@ -1182,29 +1212,19 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   int nkept = 0;
   {
     int *klist = reinterpret_cast<int *>(S.big);
-    const int KMAX = BIG / 4;
     const uint32_t *selbits = w.selbits + (size_t)cell * (nc >> 5);
     for (int p0 = 0; p0 < npost; p0 += FT * 4) {
       int jj[4], cid[4], mate[4], tok[4], keep[4];
+      if (p0 == 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int p = p0 + tid * 4 + j;
-        jj[j] = -1;
-        cid[j] = 0;
-        if (p < npost) {
-          int lo = 0, hi = nsel - 1;
-          while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (S.b.s.ppre[mid] <= p) lo = mid; else hi = mid - 1;
-          }
-          cid[j] = S.b.s.slist[lo];
-          jj[j] = S.b.s.soff[lo] + (p - S.b.s.ppre[lo]);
+        for (int j = 0; j < 4; ++j) { jj[j] = pj[j]; cid[j] = pc_[j]; mate[j] = pm[j]; tok[j] = pt[j]; }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          posting(p0 + tid * 4 + j, jj[j], cid[j]);
+          mate[j] = jj[j] >= 0 ? c.mates[jj[j]] : -1;
+          tok[j] = jj[j] >= 0 ? c.values[jj[j]] : 0;
         }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        mate[j] = jj[j] >= 0 ? c.mates[jj[j]] : -1;
-        tok[j] = jj[j] >= 0 ? c.values[jj[j]] : 0;
       }
       int cnt = 0;
 #pragma unroll
@@ -1235,7 +1255,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   {
     const int *klist = reinterpret_cast<const int *>(S.big);
     int32_t *pool = w.pool + (size_t)cell * cap;
-    for (int k = tid; k < nkept && k < BIG / 4; k += FT) {
+    for (int k = tid; k < nkept && k < KMAX; k += FT) {
       const int p = kept_base + k;
       if (p < cap) pool[p] = klist[k];
       if (p < n15) {
