@@ -1592,81 +1592,51 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       }
     }
   }
-  if (w.link) {
-    cluster_sync();  // the group's global winners are complete in global memory
-  } else {
-    if (tid == 0) mbar_expect_tx(&S.mb_win, G * TOPK * 4);
-    mbar_wait_cluster(&S.mb_win, 0u, &S.status);
-  }
-  mark(M_S2SEL);
-
   // --------------------------------------------------------------- P13
-  {
-    // sharded (Work::link): the whole layer's zones and global token ids; the
-    // records come from the owning shard's memory (plain loads over NVLink)
-    const ShardLinkDev *Lk = w.link;
-    const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local, T = Lk ? Lk->total : w.T;
-    const int dense = sink + local;
-    const int nitems = dense + G * TOPK;
-    const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
-    float qv[G][8];
+  // (the block closes after the combine below)
+  const ShardLinkDev *Lk = w.link;
+  const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local, T = Lk ? Lk->total : w.T;
+  const int dense = sink + local;
+  const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
+  float qv[G][8];
 #pragma unroll
-    for (int h = 0; h < G; ++h)
+  for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) qv[h][e] = S.sx[h * D + 8 * lane + e] * qscale;
-    float m[G], l[G], o[G][8];
+    for (int e = 0; e < 8; ++e) qv[h][e] = S.sx[h * D + 8 * lane + e] * qscale;
+  float m[G], l[G], o[G][8];
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      m[h] = -INFINITY;
-      l[h] = 0.0f;
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
-    }
-    const int nw = CL * FW, gw = rank * FW + warp;
-    // this warp's items are gw, gw + nw, ...: lane j holds item j's token and
-    // head (-1: dense key shared by the four heads); records are loaded one
-    // item ahead of the one being folded in
-    const int nmine = gw < nitems ? (nitems - gw + nw - 1) / nw : 0;
-    int my_tok = 0, my_head = -1;
-    if (lane < nmine) {
-      const int it = gw + lane * nw;
-      if (it < sink) {
-        my_tok = it;
-      } else if (it < dense) {
-        my_tok = T - local + (it - sink);
-      } else {
-        const int r = it - dense;
-        my_head = r / TOPK;
-        if (Lk) {
-          // sharded: the group's global winners (-2: fewer than 100 in the group)
-          const int gid = __ldcg(w.shard_gids + (size_t)cell * G * TOPK + r);
-          if (gid >= 0) my_tok = gid;
-          else my_head = -2;
-        } else {
-          my_tok = S.win[r / TOPK][r - (r / TOPK) * TOPK];
-        }
-      }
-    }
-    auto record = [&](int j) -> const uint8_t * {
-      const int tok = __shfl_sync(0xffffffffu, my_tok, j);
-      if (Lk) {
-        int s = 0;
-        while (s + 1 < Lk->n_shards && Lk->begin[s + 1] <= tok) ++s;
-        return Lk->kv8[s][cell] + (size_t)(tok - Lk->begin[s]) * REC;
-      }
-      return c.kv8 + (size_t)tok * REC;
-    };
-    // the records of up to SB of this warp's items are copied into its
-    // staging slots together (cp.async, one memory latency per batch rather
-    // than one per item), then folded in order
-    constexpr int SB = 4;
-    static_assert(88 * 1024 + FW * SB * REC <= BIG, "attention staging fits the staging area");
-    uint8_t *stg = S.big + 88 * 1024 + warp * SB * REC;  // clear of ao/am/al, part and pin
+    for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
+  }
+  // the records of up to SB of a warp's items are copied into its staging
+  // slots together (cp.async, one memory latency per batch rather than one per
+  // item) and folded in order; lane j names item j (token, head: -1 for a
+  // dense key shared by the four heads, -2 for none)
+  constexpr int SB = 4;
+  static_assert(88 * 1024 + FW * SB * REC <= BIG, "attention staging fits the staging area");
+  uint8_t *stg = S.big + 88 * 1024 + warp * SB * REC;  // clear of ao/am/al, part and pin
+  auto fold = [&](int nmine, int my_tok, int my_head) {
 #pragma unroll 1
     for (int j0 = 0; j0 < nmine; j0 += SB) {
       const int nb = min(SB, nmine - j0);
 #pragma unroll 1
-      for (int u = 0; u < nb; ++u) cp16(stg + u * REC + 16 * lane, record(j0 + u) + 16 * lane);
+      for (int u = 0; u < nb; ++u) {
+        const int tok = __shfl_sync(0xffffffffu, my_tok, j0 + u);
+        const uint8_t *rec;
+        if (Lk) {
+          // sharded: the record lives in the owning shard's memory (plain
+          // loads over NVLink)
+          int s = 0;
+          while (s + 1 < Lk->n_shards && Lk->begin[s + 1] <= tok) ++s;
+          rec = Lk->kv8[s][cell] + (size_t)(tok - Lk->begin[s]) * REC;
+        } else {
+          rec = c.kv8 + (size_t)tok * REC;
+        }
+        cp16(stg + u * REC + 16 * lane, rec + 16 * lane);
+      }
       cp_wait_all();
       __syncwarp();
 #pragma unroll 1
@@ -1703,6 +1673,57 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         }
       }
       __syncwarp();  // the slots are read before the next batch lands
+    }
+  };
+  auto dense_tok = [&](int it) { return it < sink ? it : T - local + (it - sink); };
+  // the dense zones (sink and local window) need no winners: CTAs G.. fold
+  // them while CTAs 0..G-1 select the top-100 (when the zones are small
+  // enough for that split to be balanced); a warp's items go 32 at a time
+  const int nwa = (CL - G) * FW;
+  const bool early = dense <= nwa * 32;
+  if (early && rank >= G) {
+    const int gwa = (rank - G) * FW + warp;
+    const int na = gwa < dense ? (dense - gwa + nwa - 1) / nwa : 0;
+    for (int c0 = 0; c0 < na; c0 += 32) {
+      const int nb = min(32, na - c0);
+      fold(nb, lane < nb ? dense_tok(gwa + (c0 + lane) * nwa) : 0, -1);
+    }
+  }
+  if (Lk) {
+    cluster_sync();  // the group's global winners are complete in global memory
+  } else {
+    if (tid == 0) mbar_expect_tx(&S.mb_win, G * TOPK * 4);
+    mbar_wait_cluster(&S.mb_win, 0u, &S.status);
+  }
+  mark(M_S2SEL);
+  {
+    // the winners over all warps (and the dense zones too when they were
+    // not folded early): items gw, gw + nw, ...
+    const int nw = CL * FW, gw = rank * FW + warp;
+    const int first = early ? dense : 0;
+    const int nitems = dense + G * TOPK - first;
+    const int nmine = gw < nitems ? (nitems - gw + nw - 1) / nw : 0;
+    for (int c0 = 0; c0 < nmine; c0 += 32) {
+      const int nb = min(32, nmine - c0);
+      int my_tok = 0, my_head = -1;
+      if (lane < nb) {
+        const int it = first + gw + (c0 + lane) * nw;
+        if (it < dense) {
+          my_tok = dense_tok(it);
+        } else {
+          const int r = it - dense;
+          my_head = r / TOPK;
+          if (Lk) {
+            // sharded: the group's global winners (-2: fewer than 100 in the group)
+            const int gid = __ldcg(w.shard_gids + (size_t)cell * G * TOPK + r);
+            if (gid >= 0) my_tok = gid;
+            else my_head = -2;
+          } else {
+            my_tok = S.win[r / TOPK][r - (r / TOPK) * TOPK];
+          }
+        }
+      }
+      fold(nb, my_tok, my_head);
     }
     mark(M_ATTN_ITEMS);
     // warps -> CTA partial per head

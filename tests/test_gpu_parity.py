@@ -111,3 +111,20 @@ def test_parity_sweep(cuda, monkeypatch, context, nprobe, capacity, staged):
             got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
             err = np.abs(got - O.bf16_to_f32(ref_out).astype(np.float64))
             assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
+
+
+@pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
+def test_large_attention_zones(cuda, monkeypatch, staged):
+    """A sink of 512 and a local window of 8192 keys: more dense keys than a
+    warp folds in one pass (8,704 keys over 256 warps)."""
+    monkeypatch.setattr(_native, "FORCE_STAGED", staged)
+    case = Case(context=32768, nprobe=384, seed=71, sink=512, local=8192)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
+        q = case.query(3)
+        y = attn.run(q).to_torch()
+        res, ref_out = case.oracle(q)
+        ids = attn.debug_snapshot()["selected_ids"].numpy()
+        assert np.array_equal(ids, np.stack([r["final_ids"] for r in res])), "selected token ids"
+        got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
+        err = np.abs(got - O.bf16_to_f32(ref_out).astype(np.float64))
+        assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
