@@ -371,7 +371,7 @@ def run_sharded(args, world, rank, local, device):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": value / 1e3, "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64-exact dots, f32 softmax, bf16 scores, fp8 K/V",
+            "vs_baseline": None, "dtype": "int8 (exact digit dots, int32/int64 accumulation), f32 softmax, bf16 scores, fp8 K/V",
             "data": "synthetic (BASELINE generator, seeded, block-seeded per token range), fresh Q per step",
             "config": {"workload": f"1 layer sequence-sharded over {world} GPUs, T={total} "
                                    f"({args.context} per GPU), 4 KV / 16 Q heads, d=256, nprobe={args.nprobe} "
@@ -742,7 +742,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": value / 1e3, "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64-exact dots, f32 softmax, bf16 scores, fp8 K/V",
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 (exact digit dots, int32/int64 accumulation), f32 softmax, bf16 scores, fp8 K/V",
             "data": "synthetic (BASELINE generator, seeded), fresh Q per step",
             "config": {"workload": "1 layer, 1 query token, T=131072, 4 KV / 16 Q heads, d=256, nprobe=384, "
                                    "sink=128, local=256, top-100",
