@@ -115,7 +115,7 @@ struct FusedSmem {
   long long sxsum[3][4];           // sum over d of X_d per operand row and head
   int round, status, n_win, pad_;
   CellDev cell;                    // this cell's descriptor (read once from global)
-  union {
+  alignas(16) union {
     struct { uint16_t lo[4][PER_MAX]; uint16_t hi[4][PER_MAX]; } c;   // P1-P3
     uint32_t fkey[4][PER_MAX];                                        // P4-P5
     struct { uint16_t slist[PER_MAX]; int soff[PER_MAX]; int ppre[PER_MAX + 1]; } s;  // P5-P6
@@ -407,12 +407,29 @@ __device__ __forceinline__ void hist_pass(uint32_t *hist, const FusedSmem &S, in
       }
     }
   } else {
+    // two keys per load (i even; the second one counts only below nloc)
 #pragma unroll 1
-    for (int i = threadIdx.x; i < nloc; i += FT) {
+    for (int i = 2 * threadIdx.x; i < nloc; i += 2 * FT) {
+      const bool two = i + 1 < nloc;
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        const uint32_t v = select_key(S, KIND, h, i, q0);
-        if ((v & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v >> sh) & 255u)], 1u);
+        uint32_t v0, v1;
+        if constexpr (KIND == KEY_FINE) {
+          const uint2 k = *reinterpret_cast<const uint2 *>(&S.b.fkey[h][i]);
+          v0 = k.x;
+          v1 = k.y;
+        } else if constexpr (KIND == KEY_S15) {
+          const uint32_t sc = *reinterpret_cast<const uint32_t *>(&S.b.p.sc15[h][i]);
+          v0 = (sc << 16) | (0xffffu - (uint32_t)(q0 + i));
+          v1 = (sc & 0xffff0000u) | (0xffffu - (uint32_t)(q0 + i + 1));
+        } else {
+          const uint32_t sc = *reinterpret_cast<const uint32_t *>(&S.b.p.sc16[h][i]);
+          const uint32_t fl = *reinterpret_cast<const uint16_t *>(&S.b.p.flag[i]);
+          v0 = (fl & 0xffu) ? (sc << 16) | (0xffffu - (uint32_t)(q0 + i)) : 0u;
+          v1 = (fl >> 8) ? (sc & 0xffff0000u) | (0xffffu - (uint32_t)(q0 + i + 1)) : 0u;
+        }
+        if ((v0 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v0 >> sh) & 255u)], 1u);
+        if (two && (v1 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v1 >> sh) & 255u)], 1u);
       }
     }
   }
