@@ -556,11 +556,14 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
       if (tid == 0) mbar_expect_tx(&S.mb_in, CL * 512);
       mbar_wait_cluster(&S.mb_in, (uint32_t)ph_in & 1u, &S.status);
       ++ph_in;
-      if (tid < 256) {
+      if (tid < 128) {
+        // word w holds bins 2w, 2w+1 as 16-bit counts; a bin's total over the
+        // cluster is at most 16 * 2048 < 2^16, so the pairs add as one word
         uint32_t c = 0;
 #pragma unroll
-        for (int q = 0; q < CL; ++q) c += (S.tab[q][tid >> 1] >> (16 * (tid & 1))) & 0xffffu;
-        S.sum[tid] = c;
+        for (int q = 0; q < CL; ++q) c += S.tab[q][tid];
+        S.sum[2 * tid] = c & 0xffffu;
+        S.sum[2 * tid + 1] = c >> 16;
       }
       __syncthreads();
       if (warp == 0) {
