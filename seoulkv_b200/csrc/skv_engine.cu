@@ -63,8 +63,10 @@ struct Engine {
   // host-I/O steps: a query bound from host memory is copied in by the step
   // graph itself, which also copies the output and the counters back into
   // pinned host memory, so that a step costs one launch and one wait
-  uint16_t *out_pinned = nullptr;
+  uint8_t *io_pinned = nullptr;    // output then counters (one copy back per host-I/O step)
+  uint16_t *out_pinned = nullptr;  // views into io_pinned
   int32_t *counts_pinned = nullptr;
+  size_t io_bytes = 0;
   cudaGraph_t graph_host = nullptr;
   cudaGraphExec_t exec_host = nullptr;
   bool q_host = false;   // the bound query is in q_pinned
@@ -233,10 +235,15 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming) ? fail(SKV_E_CUDA, "event") : 0);
   TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->q_pinned), (size_t)d->n_slots * 16 * D * 2,
                     cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned query buffer") : 0);
-  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->out_pinned), (size_t)d->n_slots * 16 * D * 2,
-                    cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned output buffer") : 0);
-  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->counts_pinned), (size_t)d->n_slots * G * NCOUNT * 4,
-                    cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned counter buffer") : 0);
+  // the output and the counters live in one device block (and one pinned
+  // mirror), so that a host-I/O step copies them back in one transfer
+  const size_t out_bytes = (size_t)d->n_slots * 16 * D * 2;
+  e->io_bytes = out_bytes + (size_t)d->n_slots * G * NCOUNT * 4;
+  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->io_pinned), e->io_bytes, cudaHostAllocDefault)
+          ? fail(SKV_E_CUDA, "pinned output buffer")
+          : 0);
+  e->out_pinned = reinterpret_cast<uint16_t *>(e->io_pinned);
+  e->counts_pinned = reinterpret_cast<int32_t *>(e->io_pinned + out_bytes);
   TRY(prepare_funnel_attributes() ? fail(SKV_E_CUDA, "kernel attributes") : 0);
   e->bufs.resize(e->n_cells);
   e->hcells.assign(e->n_cells, CellDev{});
@@ -288,11 +295,15 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(dalloc(e, &w.final_pos, C * G * TOPK));
   TRY(dalloc(e, &w.final_ids, C * G * TOPK));
   TRY(dalloc(e, &w.final_keys, C * G * TOPK));
-  TRY(dalloc(e, &w.counts, C * NCOUNT));
+  {
+    uint8_t *io = nullptr;
+    TRY(dalloc(e, &io, e->io_bytes));
+    w.out = reinterpret_cast<uint16_t *>(io);
+    w.counts = reinterpret_cast<int32_t *>(io + out_bytes);
+  }
   TRY(dalloc(e, &w.attn_part, C * G * ATTN_SPLIT * PART));
   TRY(dalloc(e, &w.arrive, C));
   TRY(dalloc(e, &w.hist, C * 4 * G * 4096));
-  TRY(dalloc(e, &w.out, (size_t)d->n_slots * 16 * D));
   TRY(dalloc(e, &e->phase_ts, 2 * FUSED_MARKS));
   w.phase_ts = nullptr;
   w.cta_ts = nullptr;
@@ -319,8 +330,7 @@ void skv_destroy(void *handle) {
   for (auto &b : e->bufs) free_cell(b, true, true);
   for (void *p : e->allocs) cudaFree(p);
   if (e->q_pinned) cudaFreeHost(e->q_pinned);
-  if (e->out_pinned) cudaFreeHost(e->out_pinned);
-  if (e->counts_pinned) cudaFreeHost(e->counts_pinned);
+  if (e->io_pinned) cudaFreeHost(e->io_pinned);
   if (e->q_copied) cudaEventDestroy(e->q_copied);
   if (e->done) cudaEventDestroy(e->done);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -511,11 +521,8 @@ int skv_run(void *handle, void *stream) {
     cudaError_t le = cudaSuccess;
     if (host) le = cudaMemcpyAsync(const_cast<uint16_t *>(w.q), e->q_pinned, qbytes, cudaMemcpyHostToDevice, e->stream);
     if (le == cudaSuccess) le = launch_step(e, w, e->stream);
-    if (host && le == cudaSuccess)
-      le = cudaMemcpyAsync(e->out_pinned, w.out, qbytes, cudaMemcpyDeviceToHost, e->stream);
-    if (host && le == cudaSuccess)
-      le = cudaMemcpyAsync(e->counts_pinned, w.counts, (size_t)e->n_cells * NCOUNT * sizeof(int32_t),
-                           cudaMemcpyDeviceToHost, e->stream);
+    if (host && le == cudaSuccess)  // output and counters: one contiguous block
+      le = cudaMemcpyAsync(e->io_pinned, w.out, e->io_bytes, cudaMemcpyDeviceToHost, e->stream);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (le != cudaSuccess) {
