@@ -514,6 +514,7 @@ def run_requests(args, world, rank, device):
     sweep = []
     for p in (int(x) for x in args.sweep.split(",")):
         batch = SeoulKV4Batch(device=device, caches=caches, config=SeoulKV4Config(nprobe=p, debug=True))
+        err = "another GPU's first run failed"
         try:
             batch.run(q_all[0].unsqueeze(1))
             batch.synchronize()
@@ -528,7 +529,7 @@ def run_requests(args, world, rank, device):
             dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         if ok.item() == 0:
             batch.close()
-            sweep.append({"nprobe": p, "not_applicable": err if "err" in locals() else "another GPU's first run failed"})
+            sweep.append({"nprobe": p, "not_applicable": err})
             continue
         t = _timed_steps(args, device, flush, lambda i: batch.run(q_all[i].unsqueeze(1)))
         # recall of the last step's ids against the exact dense top-100 (retrieval zone)
