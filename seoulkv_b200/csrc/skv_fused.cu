@@ -25,8 +25,9 @@
 //   P11 Stage-II scores of this CTA's candidates (small gather), pushed to
 //       CTA h for head h
 //   P12 exact top-100 per head (CTA h), rank order, pushed to every CTA
-//   P13 attention: sink + local + top-100 partials per CTA, each CTA's
-//       share of the output dimensions pushed to the CTA finishing them
+//   P13 attention: CTAs 4-15 fold the sink and local zones during P12, then
+//       every warp folds its share of the top-100; each CTA's partials for
+//       a share of the output dimensions go to the CTA finishing them
 //
 // Communication inside the cluster is by asynchronous stores into the
 // receiver's shared memory (st.async ... mbarrier::complete_tx), each
