@@ -46,6 +46,7 @@ extern "C" {
 #define SKV_STATUS_POOL_UNDER 2u  /* Stage-1.5 pool smaller than 2048     */
 #define SKV_STATUS_FINE_SHORT 4u  /* a head had fewer than nprobe survivors */
 #define SKV_STATUS_TIMEOUT 8u     /* a bounded device wait gave up (results invalid) */
+#define SKV_STATUS_APPEND_FULL 16u /* an append replayed from a graph did not fit max_context (skipped) */
 
 /* SkvDesc.flags */
 #define SKV_FLAG_STAGED 1         /* run the 14-kernel staged path even where the
@@ -60,6 +61,7 @@ typedef struct SkvDesc {
     int32_t stage15_capacity; /* pool slots per KV head                    */
     int32_t device;           /* CUDA device ordinal                       */
     int32_t flags;            /* SKV_FLAG_* (0: fused path where it applies) */
+    int32_t max_context;      /* capacity for skv_append (0: context, no appends) */
 } SkvDesc;
 
 /* One KV head's index in the engine layout (host memory). */
@@ -140,6 +142,29 @@ int skv_output(void *handle, void *out, int32_t to_host);
  * query head, rank).  Synchronises. */
 int skv_debug_ids(void *handle, int32_t *out);
 
+/* Cache append (no counterpart in the reference, whose cache is static:
+ * README.md "out of scope"; see the build path it would extend,
+ * _index_build.py:22-59 and _codecs/keys.py:16-44).  Appends n_tokens
+ * tokens to every slot: k and v are BF16 [n_slots][4][n_tokens][256]
+ * (host memory, or device memory with on_device != 0).  Each new token gets
+ * its key planes (with the build's per-dimension scales, codes clamped to
+ * 0..255) and FP8 record at positions T..T+n-1, and its two spill-2 lists:
+ * the top-2 stored centroids by
+ *     S(k, c) = fl64(fl64sum_{d ascending}(k_d * (2 code_cd - 15)) * fine_scale_c)
+ * (FP64, dimension order, ties to the lower centroid).  The tokens leaving
+ * the local window (T-local .. T-local+n-1) join their two lists after the
+ * lists' current postings.  The context then advances by n on the device,
+ * so decode steps replayed from graphs, and appends captured in one, see
+ * it.  Needs SkvDesc.max_context above the context; n_tokens in [1, 512];
+ * stream-ordered (no host wait for device input); uploads are closed
+ * afterwards.  SKV_E_CAPACITY when the append would pass max_context (a
+ * replayed append that does not fit is skipped and raises
+ * SKV_STATUS_APPEND_FULL instead).  A sharded engine takes no appends. */
+int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tokens, int32_t on_device,
+               void *stream);
+/* The slots' current context, after every enqueued append (waits). */
+int skv_context(void *handle, int32_t *context);
+
 /* Intermediate buffers of the last run, for diagnostics and parity tests.
  * `which` selects one of SKV_STAGE_*; copies at most `bytes` bytes of the
  * given slot's four cells (cell-major) and returns the byte count in *written. */
@@ -158,6 +183,9 @@ int skv_debug_ids(void *handle, int32_t *out);
 #define SKV_STAGE_KV8 12        /* uint8 [4][T][512] FP8-e4m3 [K | V] records  */
 #define SKV_STAGE_KEY_SCALE 13  /* float [4][256] per-dimension max |k|        */
 #define SKV_STAGE_FINAL_KEYS 14 /* uint32 [4][4][100] Stage-II keys of the ranks (0: none) */
+#define SKV_STAGE_OFFSETS 15    /* int32 [4][nc+1] live CSR offsets              */
+#define SKV_STAGE_VALUES 16     /* int32 per cell offsets[nc] token ids, cell after cell */
+#define SKV_STAGE_MATES 17      /* int32 per cell offsets[nc] mates, cell after cell     */
 int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
                    size_t *written);
 

@@ -16,7 +16,11 @@ are plain array work:
 * ``attention`` restates the sink + local + top-100 softmax of
   ``src/seoulkv4/_kernels/codegen/attention.py:83-146`` with the score scale
   ``D**-0.5`` of ``src/seoulkv4/_kernels/stage16/seoulkv4_stage16_fused.py:1607``,
-  in float64.
+  in float64;
+* ``encode_planes``, ``assign_spill2`` and ``append_postings`` define the cache
+  append (which the reference, a static cache, does not have): new tokens'
+  planes under the build's scales, their two lists, and the CSR after the
+  tokens leaving the local window join their lists.
 
 Parity of the funnel is pinned against the reference's own helper oracles by
 the fixtures under ``tests/golden`` (see ``tests/golden/make_golden.py``).
@@ -148,6 +152,99 @@ def key_codec(k_bf16_bits: np.ndarray):
         pack((code8 >> 4) & 3, 2),
         pack(code8 & 15, 4),
     )
+
+
+def encode_planes(k_bf16_bits: np.ndarray, scales: np.ndarray):
+    """Key planes of keys [..., T, 256] under given per-dimension scales [256].
+
+    The arithmetic of ``key_codec`` with the scales held fixed: the planes of
+    tokens appended after the build use the build's scales, codes clamped to
+    0..255 (``src/seoulkv4/_codecs/keys.py:29-44``).  Returns
+    ``(prefix2 [..., T, 64], residual2 [..., T, 64], residual4 [..., T, 128])``.
+    """
+    import torch
+
+    kf = torch.from_numpy(np.ascontiguousarray(k_bf16_bits).view(np.int16)).view(torch.bfloat16).float()
+    sc = torch.from_numpy(np.ascontiguousarray(scales, dtype=np.float32))
+    step8 = (2 * sc) / 256
+    code8 = torch.clamp(torch.floor((kf + sc) / step8), 0, 255).to(torch.int32).numpy()
+    return (_pack_low(code8 >> 6, 2), _pack_low((code8 >> 4) & 3, 2), _pack_low(code8 & 15, 4))
+
+
+# ----------------------------------------------------------- cache append
+#
+# The reference's cache is static (its README puts appends out of scope), so
+# these functions define the append this package adds, in terms of the
+# reference's own build outputs: a token's spill-2 posting goes to two
+# distinct stored centroids, and every list holds its tokens in ascending
+# order, as the build's CSR does (``src/seoulkv4/_index_build.py:22-59``).
+
+
+def centroid_weights(upper: np.ndarray, lower: np.ndarray) -> np.ndarray:
+    """(2 code - 15) per centroid and dimension, float64 [nc, 256]; code = upper << 2 | lower."""
+    def unpack(p):
+        p = np.asarray(p, dtype=np.uint8)
+        return np.stack([(p >> (2 * i)) & 3 for i in range(4)], axis=-1).reshape(p.shape[0], -1)
+
+    code = (unpack(upper).astype(np.int32) << 2) | unpack(lower).astype(np.int32)
+    return (2 * code - 15).astype(np.float64)
+
+
+def assign_spill2(k_bf16_bits: np.ndarray, upper: np.ndarray, lower: np.ndarray,
+                  fine_scale: np.ndarray) -> np.ndarray:
+    """The two lists of each key [m, 256] (BF16 patterns): the top-2 centroids by
+
+        S(k, c) = fl64( fl64sum_{d = 0..255}( k_d * (2 code_cd - 15) ) * fine_scale[c // 32] )
+
+    with the sum taken in dimension order in float64 (each product is exact)
+    and ties going to the lower centroid id.  Returns int64 [m, 2] (best, second).
+    """
+    w = centroid_weights(upper, lower)                      # [nc, 256]
+    nc = w.shape[0]
+    k = bf16_to_f32(np.asarray(k_bf16_bits, dtype=np.uint16).reshape(-1, 256)).astype(np.float64)
+    acc = np.zeros((k.shape[0], nc), dtype=np.float64)
+    for d in range(256):
+        acc = acc + k[:, d:d + 1] * w[None, :, d]           # one rounding per step, no fused multiply-add
+    fs = np.repeat(np.asarray(fine_scale, dtype=np.float32).astype(np.float64), 32)[:nc]
+    s = acc * fs[None, :]
+    best = np.argmax(s, axis=1)                             # first maximum: the lower id on ties
+    s2 = s.copy()
+    s2[np.arange(len(best)), best] = -np.inf
+    second = np.argmax(s2, axis=1)
+    return np.stack([best, second], axis=1).astype(np.int64)
+
+
+def append_postings(offsets: np.ndarray, values: np.ndarray, mates: np.ndarray, tokens: np.ndarray,
+                    labels: np.ndarray):
+    """CSR after posting ``tokens`` (ascending) into their two lists ``labels`` [n, 2].
+
+    Every list keeps its postings and gains its new tokens after them, in
+    token order; each new posting's mate is the token's other list.
+    Returns (offsets [nc+1], values, mates) as int32.
+    """
+    off = np.asarray(offsets, dtype=np.int64)
+    nc = len(off) - 1
+    tokens = np.asarray(tokens, dtype=np.int64)
+    labels = np.asarray(labels, dtype=np.int64).reshape(-1, 2)
+    lists = labels.reshape(-1)
+    toks = np.repeat(tokens, 2)
+    other = labels[:, ::-1].reshape(-1)
+    order = np.lexsort((toks, lists))
+    lists, toks, other = lists[order], toks[order], other[order]
+    add = np.bincount(lists, minlength=nc)
+    new_off = off + np.concatenate([[0], np.cumsum(add)])
+    n_old = int(off[-1])
+    new_vals = np.empty(n_old + len(toks), dtype=np.int32)
+    new_mates = np.empty_like(new_vals)
+    owner = np.repeat(np.arange(nc), np.diff(off))
+    shift = np.concatenate([[0], np.cumsum(add)])[:-1]
+    pos_old = np.arange(n_old) + shift[owner]
+    new_vals[pos_old] = np.asarray(values)[:n_old]
+    new_mates[pos_old] = np.asarray(mates)[:n_old]
+    pos_new = off[lists + 1] + np.arange(len(toks))
+    new_vals[pos_new] = toks
+    new_mates[pos_new] = other
+    return new_off.astype(np.int32), new_vals, new_mates
 
 
 def fp8_e4m3(x_f32: np.ndarray) -> np.ndarray:

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libseoulkv_b200.so"
-SOURCES = ("skv_kernels.cu", "skv_fused.cu", "skv_shard.cu", "skv_engine.cu", "skv_noalloc.cu")
+SOURCES = ("skv_kernels.cu", "skv_fused.cu", "skv_shard.cu", "skv_append.cu", "skv_engine.cu", "skv_noalloc.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

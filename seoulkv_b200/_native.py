@@ -17,10 +17,13 @@ from seoulkv_b200 import _build
 SKV_STATUS_POOL_OVER = 1
 SKV_STATUS_POOL_UNDER = 2
 SKV_STATUS_FINE_SHORT = 4
+SKV_STATUS_APPEND_FULL = 16
+APPEND_MAX = 512  # tokens per skv_append call
 SKV_E_CAPACITY = -3
 
 STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8,
-             prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13, final_keys=14)
+             prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13, final_keys=14, offsets=15,
+             values=16, mates=17)
 
 EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
@@ -29,6 +32,7 @@ EXPORTS = (
     "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name", "skv_profile_ctas", "skv_step", "skv_finish",
     "skv_shard_outputs", "skv_shard_merge", "skv_shard_attention", "skv_shard_combine",
     "skv_shard_setup", "skv_shard_connect", "skv_shard_ipc_handle_bytes", "skv_shard_gids",
+    "skv_append", "skv_context",
 )
 
 SKV_FLAG_STAGED = 1
@@ -39,7 +43,8 @@ FORCE_STAGED = False
 
 class SkvDesc(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in
-                ("n_slots", "context", "sink", "local", "nc", "stage15_capacity", "device", "flags")]
+                ("n_slots", "context", "sink", "local", "nc", "stage15_capacity", "device", "flags",
+                 "max_context")]
 
 
 class SkvCellView(ctypes.Structure):
@@ -134,6 +139,9 @@ def load() -> ctypes.CDLL:
         lib.skv_shard_connect.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.skv_shard_ipc_handle_bytes.restype = ctypes.c_int32
         lib.skv_shard_gids.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.skv_append.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                   ctypes.c_int32, ctypes.c_void_p]
+        lib.skv_context.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
         _lib = lib
         return lib
 
@@ -159,13 +167,15 @@ class Engine:
     """One engine instance: ``n_slots`` caches x 4 KV heads on one CUDA device."""
 
     def __init__(self, *, n_slots: int, context: int, sink: int, local: int, nc: int,
-                 capacity: int, device: int, staged: bool | None = None):
+                 capacity: int, device: int, staged: bool | None = None, max_context: int = 0):
         self.lib = load()
         self.n_slots, self.context, self.nc, self.capacity = n_slots, context, nc, capacity
         self.sink, self.local, self.device = sink, local, device
+        self.max_context = max_context or context
         staged = FORCE_STAGED if staged is None else staged
         desc = SkvDesc(n_slots=n_slots, context=context, sink=sink, local=local, nc=nc,
-                       stage15_capacity=capacity, device=device, flags=SKV_FLAG_STAGED if staged else 0)
+                       stage15_capacity=capacity, device=device, flags=SKV_FLAG_STAGED if staged else 0,
+                       max_context=max_context)
         h = ctypes.c_void_p()
         check(self.lib.skv_create(ctypes.byref(desc), ctypes.byref(h)), "skv_create")
         self.handle = h
@@ -219,6 +229,30 @@ class Engine:
 
     def sync(self) -> None:
         check(self.lib.skv_sync(self.handle), "skv_sync")
+
+    def append(self, k_ptr: int, v_ptr: int, n_tokens: int, on_device: bool, stream: int = 0) -> None:
+        """Append n_tokens (<= APPEND_MAX) tokens to every slot: BF16 [n_slots][4][n_tokens][256]."""
+        check(self.lib.skv_append(self.handle, ctypes.c_void_p(k_ptr), ctypes.c_void_p(v_ptr), n_tokens,
+                                  int(on_device), ctypes.c_void_p(stream or None)), "skv_append")
+
+    def current_context(self) -> int:
+        """The slots' context after every enqueued append (waits)."""
+        t = ctypes.c_int32()
+        check(self.lib.skv_context(self.handle, ctypes.byref(t)), "skv_context")
+        return t.value
+
+    def read_csr(self, slot: int) -> list[tuple[np.ndarray, np.ndarray, np.ndarray]]:
+        """Live (offsets, values, mates) of the slot's four cells."""
+        offs = self.read_stage(slot, "offsets", np.int32, (4, self.nc + 1))
+        total = int(offs[:, -1].sum())
+        vals = self.read_stage(slot, "values", np.int32, (max(total, 1),))
+        mates = self.read_stage(slot, "mates", np.int32, (max(total, 1),))
+        out, o = [], 0
+        for g in range(4):
+            n = int(offs[g, -1])
+            out.append((offs[g], vals[o:o + n], mates[o:o + n]))
+            o += n
+        return out
 
     def status(self) -> SkvStatus:
         s = SkvStatus()

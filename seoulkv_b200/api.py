@@ -31,6 +31,59 @@ def _bits(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.int16)
 
 
+def _max_context(config: SeoulKV4Config, context: int) -> int:
+    if config.max_context is None:
+        return context
+    if config.max_context < context:
+        raise ValueError(f"max_context {config.max_context} is below the index's context {context}")
+    return config.max_context
+
+
+def _check_append(k, v, lead: tuple, context: int | None, max_context: int) -> int:
+    """Validate appended K/V (BF16 [*lead, m, 256], one device type); returns m.
+
+    ``context`` None: the append is being captured into a CUDA graph, where
+    nothing may wait on the device; the finiteness of the keys is then the
+    caller's to guarantee and the engine's own device-side capacity check
+    (a skipped append and an error at the next synchronize) replaces the
+    host's.
+    """
+    shape = None
+    for name, t in (("K", k), ("V", v)):
+        if (not isinstance(t, torch.Tensor) or t.dtype != torch.bfloat16 or t.device.type not in ("cpu", "cuda")
+                or t.ndim != len(lead) + 2 or tuple(t.shape[:len(lead)]) != lead or t.shape[-1] != 256
+                or t.shape[-2] < 1):
+            dims = ",".join(str(x) for x in lead)
+            raise ValueError(f"expected BF16 appended {name} [{dims},m,256] with m >= 1")
+        shape = shape or tuple(t.shape)
+        if tuple(t.shape) != shape:
+            raise ValueError("appended K and V must have the same shape")
+    if k.device != v.device:
+        raise ValueError("appended K and V must be on one device")
+    m = int(k.shape[-2])
+    if context is None:
+        return m
+    if not bool(torch.isfinite(k).all()):
+        raise ValueError("appended keys must be finite")
+    if context + m > max_context:
+        hint = " (SeoulKV4Config(max_context=...) lets the cache grow)" if max_context == context else ""
+        raise ValueError(f"append of {m} tokens to context {context} passes max_context {max_context}{hint}")
+    return m
+
+
+def _enqueue_append(eng, k, v, device_index: int, stream: int) -> None:
+    """Append [..., m, 256] K/V in chunks the engine takes in one call."""
+    m = k.shape[-2]
+    on_dev = k.device.type == "cuda"
+    for j0 in range(0, m, _native.APPEND_MAX):
+        n = min(_native.APPEND_MAX, m - j0)
+        kc, vc = k[..., j0:j0 + n, :], v[..., j0:j0 + n, :]
+        if on_dev:
+            kc, vc = kc.to(f"cuda:{device_index}"), vc.to(f"cuda:{device_index}")
+        kb, vb = _bits(kc), _bits(vc)
+        eng.append(kb.data_ptr(), vb.data_ptr(), n, on_dev, stream)
+
+
 class SeoulKV4:
     """Static-cache sparse decode: one request, one query token per run."""
 
@@ -54,6 +107,9 @@ class SeoulKV4:
                         else index.nprobe)
         self._index = index
         self._host_kv = (k, v)
+        self._context = context
+        self._max_context = _max_context(self._config, context)
+        self._captured_appends = False
         self._engine: _native.Engine | None = None
         self._generation = 0
         self._closed = False
@@ -90,7 +146,8 @@ class SeoulKV4:
         if any(int(c["centroids"].shape[0]) != nc for c in cells):
             raise ValueError("all four index cells must have the same centroid count")
         eng = _native.Engine(n_slots=1, context=zones.context, sink=zones.sink, local=zones.local,
-                             nc=nc, capacity=self._config.stage15_capacity, device=self._device_index)
+                             nc=nc, capacity=self._config.stage15_capacity, device=self._device_index,
+                             max_context=self._max_context if self._max_context > zones.context else 0)
         try:
             eng.upload_index(0, [device_view(c, p) for c, p in zip(cells, self._nprobe)])
             k, v = self._host_kv
@@ -132,6 +189,43 @@ class SeoulKV4:
                     "change capacity, never truncate")
         return DecodeResult(self, self._generation)
 
+    @property
+    def context(self) -> int:
+        """Tokens in the cache: the index's context plus every appended token
+        (read from the device, after pending work, once appends were captured
+        into a graph: its replays append too)."""
+        if self._captured_appends and self._engine is not None:
+            return self._engine.current_context()
+        return self._context
+
+    def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Grow the cache by m tokens: BF16 K and V [4, m, 256], host or CUDA.
+
+        Stream-ordered on the current PyTorch stream, like ``run``; the first
+        call initialises the instance as ``run`` does.  The new tokens enter
+        the local window and the window's m oldest tokens join the retrieval
+        zone, each posted to its two nearest stored centroids (the index's
+        centroids and key-code scales stay those of the build).  Needs
+        ``SeoulKV4Config(max_context=...)`` with room for the m tokens.  May
+        be captured into a CUDA graph (CUDA K/V, instance already
+        initialised); every replay then appends m more tokens.
+        """
+        self._require_open()
+        capturing = torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+        if capturing and self._engine is None:
+            raise RuntimeError("initialise SeoulKV4 (run or append once) before capturing an append")
+        if not capturing and self._captured_appends and self._engine is not None:
+            self._context = self._engine.current_context()
+        m = _check_append(k, v, (N_KV_HEADS,), None if capturing else self._context, self._max_context)
+        if self._engine is None:
+            self._engine = self._initialize()
+            self._host_kv = None
+        _enqueue_append(self._engine, k, v, self._device_index, self._stream())
+        if capturing:
+            self._captured_appends = True
+        else:
+            self._context += m
+
     def _bind_query(self, q: torch.Tensor) -> None:
         self._validate_query(q)
         eng = self._require_initialized()
@@ -160,6 +254,8 @@ class SeoulKV4:
             "cache_layout": "flat",
             "index": self._index.metadata(),
             "nprobe": list(self._nprobe),
+            "context": self._context,
+            "max_context": self._max_context,
         }
         if self.initialized:
             meta.update(

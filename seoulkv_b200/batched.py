@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from seoulkv_b200 import _native
-from seoulkv_b200.api import _bits, _cuda_index
+from seoulkv_b200.api import _bits, _check_append, _cuda_index, _enqueue_append, _max_context
 from seoulkv_b200.config import MAX_CONTEXT, MIN_CONTEXT, N_HEADS, N_KV_HEADS, SeoulKV4Config, validate_nprobe
 from seoulkv_b200.index import SeoulKV4Index, device_view
 from seoulkv_b200.result import _DeviceBuffer
@@ -103,6 +103,8 @@ class SeoulKV4Batch:
                                 else index.nprobe)
         self._caches = list(caches)
         self._zones, self._nc = zones, nc
+        self._context = zones[0]
+        self._max_context = _max_context(self._config, zones[0])
         self.n = len(caches)
         self._engine: _native.Engine | None = None
         self._generation = 0
@@ -120,7 +122,8 @@ class SeoulKV4Batch:
     def _initialize(self) -> _native.Engine:
         context, sink, local = self._zones
         eng = _native.Engine(n_slots=self.n, context=context, sink=sink, local=local, nc=self._nc,
-                             capacity=self._config.stage15_capacity, device=self._device_index)
+                             capacity=self._config.stage15_capacity, device=self._device_index,
+                             max_context=self._max_context if self._max_context > context else 0)
         try:
             for s, (k, v, index) in enumerate(self._caches):
                 eng.upload_index(s, [device_view(c, p) for c, p in zip(index.cells(), self._nprobe[s])])
@@ -166,6 +169,25 @@ class SeoulKV4Batch:
                     f"(status {st.flags:#x}); change capacity, never truncate")
         return BatchResult(self, self._generation)
 
+    @property
+    def context(self) -> int:
+        """Tokens in every cache: the shared context plus every appended token."""
+        return self._context
+
+    def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Grow every cache by m tokens: BF16 K and V [n, 4, m, 256], host or CUDA.
+
+        The same contract as ``SeoulKV4.append`` per cache; all caches keep one
+        shared context.
+        """
+        self._require_open()
+        m = _check_append(k, v, (self.n, N_KV_HEADS), self._context, self._max_context)
+        if self._engine is None:
+            self._engine = self._initialize()
+            self._caches = [(None, None, c[2]) for c in self._caches]
+        _enqueue_append(self._engine, k, v, self._device_index, self._stream())
+        self._context += m
+
     def synchronize(self) -> None:
         """Wait for the last run; raises RuntimeError if a live count left its range."""
         self._require_open()
@@ -188,7 +210,8 @@ class SeoulKV4Batch:
     def metadata(self) -> dict:
         self._require_open()
         context, sink, local = self._zones
-        meta = {"initialized": self.initialized, "caches": self.n, "context": context, "sink": sink,
+        meta = {"initialized": self.initialized, "caches": self.n, "context": self._context,
+                "max_context": self._max_context, "sink": sink,
                 "local": local, "centroids_per_head": self._nc, "nprobe": [list(p) for p in self._nprobe]}
         if self._engine is not None:
             meta.update(kernels_per_step=self._engine.kernels_per_step(),

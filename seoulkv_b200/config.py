@@ -18,6 +18,7 @@ STAGE16_M = 256
 MIN_CONTEXT = 6400
 MAX_CONTEXT = 524288      # reference limit (index.py:114); the engine itself takes up to 2^20
 MAX_CENTROIDS = 65536     # Fine's 16-bit survivor positions (index.py:126)
+ENGINE_MAX_CONTEXT = 1 << 20  # largest context the engine holds (appends included)
 
 
 def validate_nprobe(nprobe, nc: int) -> tuple[int, ...]:
@@ -41,12 +42,15 @@ class SeoulKV4Config:
     ``stage15_capacity`` must be a multiple of 768 in [12288, 24576]; a live
     pool above it is reported as an error, never truncated.  ``nprobe``
     (None = keep the index's value) overrides the index's probe budget for this
-    instance without rebuilding the index.
+    instance without rebuilding the index.  ``max_context`` (None = the
+    index's context: a static cache, as in the reference) is the context the
+    cache may grow to by ``append``; device buffers are sized for it.
     """
 
     stage15_capacity: int = 13056
     debug: bool = False
     nprobe: int | tuple[int, ...] | None = None
+    max_context: int | None = None
 
     def __post_init__(self):
         n = self.stage15_capacity
@@ -58,3 +62,6 @@ class SeoulKV4Config:
             validate_nprobe(self.nprobe if type(self.nprobe) is int else tuple(self.nprobe), 512)
             if not isinstance(self.nprobe, int):
                 object.__setattr__(self, "nprobe", tuple(self.nprobe))
+        if self.max_context is not None and (type(self.max_context) is not int
+                                             or not MIN_CONTEXT <= self.max_context <= ENGINE_MAX_CONTEXT):
+            raise ValueError(f"max_context must be None or an integer in [{MIN_CONTEXT}, {ENGINE_MAX_CONTEXT}]")

@@ -159,7 +159,12 @@ struct Work {
                             // (tag, ns) phase marks of cell 0's CTAs (fused), or null
   const ShardLinkDev *link; // sequence-sharded group (device copy), or null
   int32_t *shard_gids;      // [4][4][TOPK] the group's global winners (with link)
+  const int32_t *tlen;      // the slots' current context (grows with cache appends), or null: T
 };
+
+// Current context of the engine's slots: cache appends advance it on the
+// device, so a step replayed from a graph sees the appended tokens.
+__device__ __forceinline__ int context_of(const Work &w) { return w.tlen ? *w.tlen : w.T; }
 
 __device__ __forceinline__ uint16_t bf16_rne(float f) {
   uint32_t u = __float_as_uint(f);

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/seoulkv_b200.h"
+#include "skv_append.cuh"
 #include "skv_device.cuh"
 #include "skv_fused.cuh"
 #include "skv_kernels.cuh"
@@ -43,6 +44,8 @@ struct CellBufs {
   uint8_t *prefix2 = nullptr, *residual2 = nullptr, *residual4 = nullptr, *kv8 = nullptr;
   float *key_scale = nullptr;
   int32_t n_postings = 0;
+  // cache append: the second CSR set and every token's two lists
+  int32_t *offsets2 = nullptr, *values2 = nullptr, *mates2 = nullptr, *labels = nullptr;
 };
 
 struct Engine {
@@ -88,6 +91,22 @@ struct Engine {
     float *part = nullptr;               // [4][4][PART] this shard's partials
     ShardLinkDev *dev = nullptr;         // device copy of the group (Work::link)
   } link;
+  // cache append (SkvDesc.max_context above the context)
+  int32_t tmax = 0;                    // largest context of the slots
+  int32_t t_host = 0;                  // context after the appends enqueued outside a capture
+  bool appended = false;               // an append was enqueued (uploads are closed)
+  bool append_captured = false;        // an append went into a caller's graph (t_host unknown)
+  int32_t *tlen = nullptr;             // device context (Work::tlen)
+  uint32_t *append_status = nullptr;   // APPEND_FULL when a replayed append did not fit
+  AppendCellDev *dacells = nullptr;
+  std::vector<AppendCellDev> hacells;
+  std::vector<uint16_t *> wkeys;       // per slot: BF16 keys of the first local window [4][local][256]
+  std::vector<int> labeled;            // per slot: the first window's lists are computed
+  double *part_s = nullptr;
+  int32_t *part_i = nullptr;
+  int32_t *newlist = nullptr, *newtok = nullptr, *newmate = nullptr;
+  uint16_t *kv_stage = nullptr;        // host-input staging [2][n_cells][APPEND_MAX][256]
+  bool appends() const { return tmax > desc.context; }
 };
 
 ShardLinkDev link_view(const Engine *e) {
@@ -131,19 +150,22 @@ int dalloc(Engine *e, T **p, size_t count) {
 void free_cell(CellBufs &b, bool index, bool kv) {
   if (index) {
     for (void *p : {(void *)b.upper, (void *)b.lower, (void *)b.coarse_scale4, (void *)b.fine_scale,
-                    (void *)b.resid, (void *)b.offsets, (void *)b.values, (void *)b.mates})
+                    (void *)b.resid, (void *)b.offsets, (void *)b.values, (void *)b.mates, (void *)b.offsets2,
+                    (void *)b.values2, (void *)b.mates2})
       if (p) cudaFree(p);
     b.upper = b.lower = nullptr;
     b.coarse_scale4 = b.fine_scale = nullptr;
     b.resid = nullptr;
     b.offsets = b.values = b.mates = nullptr;
+    b.offsets2 = b.values2 = b.mates2 = nullptr;
   }
   if (kv) {
     for (void *p : {(void *)b.prefix2, (void *)b.residual2, (void *)b.residual4, (void *)b.kv8,
-                    (void *)b.key_scale})
+                    (void *)b.key_scale, (void *)b.labels})
       if (p) cudaFree(p);
     b.prefix2 = b.residual2 = b.residual4 = b.kv8 = nullptr;
     b.key_scale = nullptr;
+    b.labels = nullptr;
   }
 }
 
@@ -151,6 +173,14 @@ template <class T>
 int upload(T **dst, const T *src, size_t count) {
   CK(cudaMalloc(reinterpret_cast<void **>(dst), count * sizeof(T) + 16));
   CK(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+  return SKV_OK;
+}
+
+// Upload `count` elements into a buffer of `cap` >= count elements.
+template <class T>
+int upload_cap(T **dst, const T *src, size_t count, size_t cap) {
+  CK(cudaMalloc(reinterpret_cast<void **>(dst), cap * sizeof(T) + 16));
+  if (count) CK(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
   return SKV_OK;
 }
 
@@ -177,6 +207,29 @@ int read_counts(Engine *e, std::vector<int32_t> &c) {
     return SKV_OK;
   }
   CK(cudaMemcpy(c.data(), e->work.counts, c.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+  return SKV_OK;
+}
+
+// The error a status with flags set turns into (skv_sync, skv_finish).
+int status_error(const Engine *e, const SkvStatus &s) {
+  char msg[320];
+  if (s.flags & SKV_STATUS_APPEND_FULL) {
+    std::snprintf(msg, sizeof msg, "a device-side append would have passed max_context %d (status 0x%x)",
+                  e->tmax, s.flags);
+    return fail(SKV_E_CAPACITY, msg);
+  }
+  std::snprintf(msg, sizeof msg,
+                "live count out of range at cell %d (status 0x%x: %s%s%s); pool range [%d, %d], capacity %d",
+                s.first_bad_cell, s.flags, (s.flags & SKV_STATUS_POOL_OVER) ? "pool above capacity " : "",
+                (s.flags & SKV_STATUS_POOL_UNDER) ? "pool below 2048 " : "",
+                (s.flags & SKV_STATUS_FINE_SHORT) ? "fewer than nprobe survivors" : "", s.pool_min, s.pool_max,
+                e->desc.stage15_capacity);
+  return fail(SKV_E_CAPACITY, msg);
+}
+
+// The device context (after every enqueued append has run).
+int device_context(Engine *e, int32_t *t) {
+  CK(cudaMemcpy(t, e->tlen, sizeof(int32_t), cudaMemcpyDeviceToHost));
   return SKV_OK;
 }
 
@@ -211,6 +264,8 @@ int skv_create(const SkvDesc *d, void **handle) {
     return fail(SKV_E_INVALID, "nc must be a multiple of 32 in [32, 65536]");
   if (d->stage15_capacity < M15_MIN || d->stage15_capacity > 65536 || d->stage15_capacity % 32)
     return fail(SKV_E_INVALID, "stage15_capacity must be a multiple of 32 in [2048, 65536]");
+  if (d->max_context != 0 && (d->max_context < d->context || d->max_context > (1 << 20)))
+    return fail(SKV_E_INVALID, "max_context must be 0 or in [context, 2^20]");
   auto *e = new Engine();
   e->desc = *d;
   e->n_cells = d->n_slots * G;
@@ -305,6 +360,27 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(dalloc(e, &w.arrive, C));
   TRY(dalloc(e, &w.hist, C * 4 * G * 4096));
   TRY(dalloc(e, &e->phase_ts, 2 * FUSED_MARKS));
+  e->tmax = d->max_context ? d->max_context : d->context;
+  e->t_host = d->context;
+  {
+    int32_t *tl = nullptr;
+    TRY(dalloc(e, &tl, 1));
+    TRY(cudaMemcpy(tl, &d->context, sizeof(int32_t), cudaMemcpyHostToDevice) ? fail(SKV_E_CUDA, "context word") : 0);
+    e->tlen = tl;
+    w.tlen = tl;
+  }
+  e->wkeys.assign(d->n_slots, nullptr);
+  e->labeled.assign(d->n_slots, 0);
+  if (e->appends()) {
+    e->hacells.assign(C, AppendCellDev{});
+    TRY(dalloc(e, &e->dacells, C));
+    TRY(dalloc(e, &e->append_status, 1));
+    TRY(dalloc(e, &e->part_s, C * APPEND_MAX * ASSIGN_SPLIT * 2));
+    TRY(dalloc(e, &e->part_i, C * APPEND_MAX * ASSIGN_SPLIT * 2));
+    TRY(dalloc(e, &e->newlist, C * 2 * APPEND_MAX));
+    TRY(dalloc(e, &e->newtok, C * 2 * APPEND_MAX));
+    TRY(dalloc(e, &e->newmate, C * 2 * APPEND_MAX));
+  }
   w.phase_ts = nullptr;
   w.cta_ts = nullptr;
   e->fused = !(d->flags & SKV_FLAG_STAGED) && fused_supported(w);
@@ -328,6 +404,9 @@ void skv_destroy(void *handle) {
   if (e->link.region) cudaFree(e->link.region);
   drop_graphs(e);
   for (auto &b : e->bufs) free_cell(b, true, true);
+  for (void *p : e->wkeys)
+    if (p) cudaFree(p);
+  if (e->kv_stage) cudaFree(e->kv_stage);
   for (void *p : e->allocs) cudaFree(p);
   if (e->q_pinned) cudaFreeHost(e->q_pinned);
   if (e->io_pinned) cudaFreeHost(e->io_pinned);
@@ -339,6 +418,42 @@ void skv_destroy(void *handle) {
 
 static int refresh_cells(Engine *e) {
   CK(cudaMemcpy(e->dcells, e->hcells.data(), e->hcells.size() * sizeof(CellDev), cudaMemcpyHostToDevice));
+  if (e->appends())
+    CK(cudaMemcpy(e->dacells, e->hacells.data(), e->hacells.size() * sizeof(AppendCellDev),
+                  cudaMemcpyHostToDevice));
+  return SKV_OK;
+}
+
+static int assign_split(int nc) { return std::min(ASSIGN_SPLIT, (nc + 255) / 256); }
+
+// The two lists of every token in a slot's first local window, from the
+// window's BF16 keys, once both the slot's index and its K/V are uploaded.
+static int label_window(Engine *e, int slot) {
+  e->labeled[slot] = 0;
+  if (!e->appends()) return SKV_OK;
+  for (int g = 0; g < G; ++g)
+    if (!e->index_ok[slot * G + g] || !e->kv_ok[slot * G + g]) return SKV_OK;
+  const int T0 = e->desc.context, local = e->desc.local;
+  for (int j0 = 0; j0 < local; j0 += APPEND_MAX) {
+    AssignArgs a{};
+    a.cells = e->dcells;
+    a.acells = e->dacells;
+    a.tlen = e->tlen;
+    a.k = e->wkeys[slot] + (size_t)j0 * D;
+    a.k_cell_stride = (long long)local * D;
+    a.cell0 = slot * G;
+    a.n_cells = G;
+    a.m = std::min(APPEND_MAX, local - j0);
+    a.nc = e->desc.nc;
+    a.split = assign_split(e->desc.nc);
+    a.lab_base = T0 - local + j0;
+    a.tmax = e->tmax;
+    a.part_s = e->part_s;
+    a.part_i = e->part_i;
+    CK(launch_assign(a, e->stream));
+  }
+  CK(cudaStreamSynchronize(e->stream));
+  e->labeled[slot] = 1;
   return SKV_OK;
 }
 
@@ -346,6 +461,7 @@ int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells) {
   Engine *e = as_engine(handle);
   if (!e || !cells) return fail(SKV_E_INVALID, "null engine or cells");
   if (slot < 0 || slot >= e->desc.n_slots) return fail(SKV_E_INVALID, "slot out of range");
+  if (e->appended) return fail(SKV_E_STATE, "the cache has grown by appends; uploads are closed");
   CK(cudaSetDevice(e->desc.device));
   CK(cudaStreamSynchronize(e->stream));
   const int nc = e->desc.nc, T = e->desc.context;
@@ -378,10 +494,26 @@ int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells) {
     if ((rc = upload(&b.coarse_scale4, v.coarse_scale4, (size_t)nc / 32))) return rc;
     if ((rc = upload(&b.fine_scale, v.fine_scale, (size_t)nc / 32))) return rc;
     if ((rc = upload(&b.resid, v.resid_bf16, (size_t)nc))) return rc;
+    // with appends, both CSR sets hold the postings of a full-grown cache
+    const size_t post_cap = (size_t)std::max(v.n_postings, 1) + 2 * (size_t)(e->tmax - T);
     if ((rc = upload(&b.offsets, v.offsets, (size_t)nc + 1))) return rc;
-    if ((rc = upload(&b.values, v.values, (size_t)(v.n_postings > 0 ? v.n_postings : 1)))) return rc;
-    if ((rc = upload(&b.mates, v.mates, (size_t)(v.n_postings > 0 ? v.n_postings : 1)))) return rc;
+    if ((rc = upload_cap(&b.values, v.values, (size_t)v.n_postings, post_cap))) return rc;
+    if ((rc = upload_cap(&b.mates, v.mates, (size_t)v.n_postings, post_cap))) return rc;
     b.n_postings = v.n_postings;
+    if (e->appends()) {
+      CK(cudaMalloc(reinterpret_cast<void **>(&b.offsets2), ((size_t)nc + 1) * sizeof(int32_t)));
+      CK(cudaMalloc(reinterpret_cast<void **>(&b.values2), post_cap * sizeof(int32_t)));
+      CK(cudaMalloc(reinterpret_cast<void **>(&b.mates2), post_cap * sizeof(int32_t)));
+      AppendCellDev &a = e->hacells[cell];
+      a.offsets[0] = b.offsets;
+      a.values[0] = b.values;
+      a.mates[0] = b.mates;
+      a.offsets[1] = b.offsets2;
+      a.values[1] = b.values2;
+      a.mates[1] = b.mates2;
+      a.cur = 0;
+      a.n_postings = v.n_postings;
+    }
     CellDev &c = e->hcells[cell];
     c.upper = b.upper;
     c.lower = b.lower;
@@ -396,16 +528,19 @@ int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells) {
     c.lam = v.lam;
     e->index_ok[cell] = 1;
   }
-  return refresh_cells(e);
+  int rc = refresh_cells(e);
+  return rc ? rc : label_window(e, slot);
 }
 
 int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t *v, int32_t on_device) {
   Engine *e = as_engine(handle);
   if (!e || !k || !v) return fail(SKV_E_INVALID, "null engine or K/V");
   if (slot < 0 || slot >= e->desc.n_slots) return fail(SKV_E_INVALID, "slot out of range");
+  if (e->appended) return fail(SKV_E_STATE, "the cache has grown by appends; uploads are closed");
   CK(cudaSetDevice(e->desc.device));
   CK(cudaStreamSynchronize(e->stream));
   const size_t T = e->desc.context, elems = (size_t)G * T * D;
+  const size_t rows = e->tmax;  // planes and records of a full-grown cache
   const uint16_t *dk = k, *dv = v;
   uint16_t *stage = nullptr;
   if (!on_device) {
@@ -426,11 +561,12 @@ int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t 
   for (int g = 0; g < G && rc == SKV_OK; ++g) {
     CellBufs &b = e->bufs[slot * G + g];
     free_cell(b, false, true);
-    if (cudaMalloc(reinterpret_cast<void **>(&b.prefix2), T * 64) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void **>(&b.residual2), T * 64) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void **>(&b.residual4), T * 128) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void **>(&b.kv8), T * REC) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void **>(&b.key_scale), D * sizeof(float)) != cudaSuccess)
+    if (cudaMalloc(reinterpret_cast<void **>(&b.prefix2), rows * 64) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.residual2), rows * 64) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.residual4), rows * 128) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.kv8), rows * REC) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&b.key_scale), D * sizeof(float)) != cudaSuccess ||
+        (e->appends() && cudaMalloc(reinterpret_cast<void **>(&b.labels), rows * 2 * sizeof(int32_t)) != cudaSuccess))
       rc = fail(SKV_E_CUDA, "out of device memory for key planes / FP8 records");
     scale[g] = b.key_scale;
     p2[g] = b.prefix2;
@@ -442,6 +578,14 @@ int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t 
     rc = fail(SKV_E_CUDA, "out of device memory");
   if (rc == SKV_OK) {
     cudaError_t ce = launch_key_codec(dk, dv, (int)T, smax, scale, p2, r2, r4, kv8, e->stream);
+    // with appends, the first local window's keys stay for its spill-2 lists
+    const size_t local = e->desc.local;
+    if (ce == cudaSuccess && e->appends() && local > 0) {
+      if (!e->wkeys[slot]) ce = cudaMalloc(reinterpret_cast<void **>(&e->wkeys[slot]), G * local * D * 2);
+      for (int g = 0; g < G && ce == cudaSuccess; ++g)
+        ce = cudaMemcpyAsync(e->wkeys[slot] + (size_t)g * local * D, dk + ((size_t)g * T + T - local) * D,
+                             local * D * 2, cudaMemcpyDeviceToDevice, e->stream);
+    }
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
     if (ce != cudaSuccess) rc = fail(SKV_E_CUDA, std::string("key codec: ") + cudaGetErrorString(ce));
   }
@@ -456,9 +600,19 @@ int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t 
     c.residual4 = r4[g];
     c.kv8 = kv8[g];
     c.key_scale = scale[g];
+    if (e->appends()) {
+      AppendCellDev &a = e->hacells[cell];
+      a.prefix2 = p2[g];
+      a.residual2 = r2[g];
+      a.residual4 = r4[g];
+      a.kv8 = kv8[g];
+      a.key_scale = scale[g];
+      a.labels = e->bufs[cell].labels;
+    }
     e->kv_ok[cell] = 1;
   }
-  return refresh_cells(e);
+  rc = refresh_cells(e);
+  return rc ? rc : label_window(e, slot);
 }
 
 int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *stream) {
@@ -549,6 +703,94 @@ int skv_step(void *handle, const uint16_t *q, int32_t on_device, void *stream) {
   return rc ? rc : skv_run(handle, stream);
 }
 
+int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tokens, int32_t on_device,
+               void *stream) {
+  Engine *e = as_engine(handle);
+  if (!e || !k || !v) return fail(SKV_E_INVALID, "null engine or K/V");
+  if (!e->appends()) return fail(SKV_E_STATE, "appends need an engine created with max_context above the context");
+  if (e->link.active) return fail(SKV_E_STATE, "a sequence-sharded engine does not take appends");
+  if (n_tokens < 1 || n_tokens > APPEND_MAX)
+    return fail(SKV_E_INVALID, "n_tokens must be in [1, " + std::to_string(APPEND_MAX) + "]");
+  int rc = ready(e);
+  if (rc) return rc;
+  for (int s = 0; s < e->desc.n_slots; ++s)
+    if (!e->labeled[s]) return fail(SKV_E_STATE, "slot " + std::to_string(s) + " has no window lists");
+  CK(cudaSetDevice(e->desc.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(st, &cap));
+  const bool captured = cap != cudaStreamCaptureStatusNone;
+  if (captured && !on_device) return fail(SKV_E_STATE, "a captured append needs device-resident K/V");
+  if (!captured) {
+    int32_t t = e->t_host;
+    if (e->append_captured) {  // graph replays may have appended: ask the device
+      CK(cudaStreamSynchronize(st));
+      if ((rc = sync_done(e)) || (rc = device_context(e, &t))) return rc;
+    }
+    if (t + n_tokens > e->tmax)
+      return fail(SKV_E_CAPACITY, "append of " + std::to_string(n_tokens) + " tokens to context " +
+                                      std::to_string(t) + " passes max_context " + std::to_string(e->tmax));
+  }
+  const size_t rows = (size_t)e->n_cells * n_tokens * D;
+  const uint16_t *dk = k, *dv = v;
+  if (!on_device) {
+    if (!e->kv_stage)
+      CK(cudaMalloc(reinterpret_cast<void **>(&e->kv_stage), 2 * (size_t)e->n_cells * APPEND_MAX * D * 2));
+    uint16_t *sk = e->kv_stage, *sv = e->kv_stage + (size_t)e->n_cells * APPEND_MAX * D;
+    CK(cudaMemcpyAsync(sk, k, rows * 2, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(sv, v, rows * 2, cudaMemcpyHostToDevice, st));
+    dk = sk;
+    dv = sv;
+  }
+  AppendArgs a{};
+  a.cells = e->dcells;
+  a.acells = e->dacells;
+  a.tlen = e->tlen;
+  a.status = e->append_status;
+  a.k = dk;
+  a.v = dv;
+  a.n_cells = e->n_cells;
+  a.m = n_tokens;
+  a.nc = e->desc.nc;
+  a.local = e->desc.local;
+  a.tmax = e->tmax;
+  a.newlist = e->newlist;
+  a.newtok = e->newtok;
+  a.newmate = e->newmate;
+  AssignArgs s{};
+  s.cells = e->dcells;
+  s.acells = e->dacells;
+  s.tlen = e->tlen;
+  s.k = dk;
+  s.k_cell_stride = (long long)n_tokens * D;
+  s.cell0 = 0;
+  s.n_cells = e->n_cells;
+  s.m = n_tokens;
+  s.nc = e->desc.nc;
+  s.split = assign_split(e->desc.nc);
+  s.use_tlen = 1;
+  s.guard = n_tokens;
+  s.tmax = e->tmax;
+  s.part_s = e->part_s;
+  s.part_i = e->part_i;
+  CK(launch_append(a, s, st));
+  e->appended = true;
+  if (captured) e->append_captured = true;
+  else e->t_host += n_tokens;
+  if (!captured) {
+    CK(cudaEventRecord(e->done, st));
+    e->ran = true;
+  }
+  return SKV_OK;
+}
+
+int skv_context(void *handle, int32_t *context) {
+  Engine *e = as_engine(handle);
+  if (!e || !context) return fail(SKV_E_INVALID, "null engine or output");
+  int rc = sync_done(e);
+  return rc ? rc : device_context(e, context);
+}
+
 int skv_finish(void *handle, uint16_t *out, SkvStatus *status) {
   Engine *e = as_engine(handle);
   if (!e) return fail(SKV_E_INVALID, "null engine");
@@ -563,16 +805,7 @@ int skv_finish(void *handle, uint16_t *out, SkvStatus *status) {
       CK(cudaMemcpy(out, e->work.out, (size_t)e->desc.n_slots * 16 * D * 2, cudaMemcpyDeviceToHost));
     }
   }
-  if (s.flags) {
-    char msg[256];
-    std::snprintf(msg, sizeof msg,
-                  "live count out of range at cell %d (status 0x%x: %s%s%s); pool range [%d, %d], capacity %d",
-                  s.first_bad_cell, s.flags, (s.flags & SKV_STATUS_POOL_OVER) ? "pool above capacity " : "",
-                  (s.flags & SKV_STATUS_POOL_UNDER) ? "pool below 2048 " : "",
-                  (s.flags & SKV_STATUS_FINE_SHORT) ? "fewer than nprobe survivors" : "", s.pool_min,
-                  s.pool_max, e->desc.stage15_capacity);
-    return fail(SKV_E_CAPACITY, msg);
-  }
+  if (s.flags) return status_error(e, s);
   return SKV_OK;
 }
 
@@ -597,6 +830,11 @@ int skv_status(void *handle, SkvStatus *out) {
     s.union15_max = std::max(s.union15_max, k[C_U15]);
     s.union16_max = std::max(s.union16_max, k[C_CAND]);
   }
+  if (e->append_status) {
+    uint32_t as = 0;
+    CK(cudaMemcpy(&as, e->append_status, sizeof as, cudaMemcpyDeviceToHost));
+    if (as & APPEND_FULL) s.flags |= SKV_STATUS_APPEND_FULL;
+  }
   *out = s;
   return SKV_OK;
 }
@@ -608,16 +846,7 @@ int skv_sync(void *handle) {
   SkvStatus s;
   int rc = skv_status(handle, &s);
   if (rc) return rc;
-  if (s.flags) {
-    char msg[256];
-    std::snprintf(msg, sizeof msg,
-                  "live count out of range at cell %d (status 0x%x: %s%s%s); pool range [%d, %d], capacity %d",
-                  s.first_bad_cell, s.flags, (s.flags & SKV_STATUS_POOL_OVER) ? "pool above capacity " : "",
-                  (s.flags & SKV_STATUS_POOL_UNDER) ? "pool below 2048 " : "",
-                  (s.flags & SKV_STATUS_FINE_SHORT) ? "fewer than nprobe survivors" : "", s.pool_min,
-                  s.pool_max, e->desc.stage15_capacity);
-    return fail(SKV_E_CAPACITY, msg);
-  }
+  if (s.flags) return status_error(e, s);
   return SKV_OK;
 }
 
@@ -698,12 +927,35 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
       if (written) *written = n;
       return SKV_OK;
     }
+    case SKV_STAGE_OFFSETS:
+    case SKV_STAGE_VALUES:
+    case SKV_STAGE_MATES: {
+      // the live CSR set of each cell (appends flip it on the device)
+      std::vector<CellDev> cd(G);
+      CK(cudaMemcpy(cd.data(), e->dcells + c0, G * sizeof(CellDev), cudaMemcpyDeviceToHost));
+      size_t done = 0;
+      for (int g = 0; g < G && done < bytes; ++g) {
+        if (!cd[g].offsets) return fail(SKV_E_STATE, "index not uploaded for this slot");
+        int32_t np = 0;
+        CK(cudaMemcpy(&np, cd[g].offsets + nc, sizeof np, cudaMemcpyDeviceToHost));
+        const void *p = which == SKV_STAGE_OFFSETS ? (const void *)cd[g].offsets
+                      : which == SKV_STAGE_VALUES ? (const void *)cd[g].values : (const void *)cd[g].mates;
+        const size_t per = (which == SKV_STAGE_OFFSETS ? nc + 1 : (size_t)np) * sizeof(int32_t);
+        const size_t m = std::min(per, bytes - done);
+        if (m) CK(cudaMemcpy(static_cast<char *>(dst) + done, p, m, cudaMemcpyDeviceToHost));
+        done += m;
+      }
+      if (written) *written = done;
+      return SKV_OK;
+    }
     case SKV_STAGE_PREFIX2:
     case SKV_STAGE_RESIDUAL2:
     case SKV_STAGE_RESIDUAL4:
     case SKV_STAGE_KV8:
     case SKV_STAGE_KEY_SCALE: {
-      const size_t T = e->desc.context;
+      int32_t tcur = 0;
+      if ((rc = device_context(e, &tcur))) return rc;
+      const size_t T = tcur;
       const size_t row = which == SKV_STAGE_RESIDUAL4 ? 128 : which == SKV_STAGE_KV8 ? REC
                        : which == SKV_STAGE_KEY_SCALE ? 0 : 64;
       const size_t per = which == SKV_STAGE_KEY_SCALE ? D * sizeof(float) : T * row;

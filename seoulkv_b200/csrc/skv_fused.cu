@@ -1616,7 +1616,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   // --------------------------------------------------------------- P13
   // (the block closes after the combine below)
   const ShardLinkDev *Lk = w.link;
-  const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local, T = Lk ? Lk->total : w.T;
+  const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local, T = Lk ? Lk->total : context_of(w);
   const int dense = sink + local;
   const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
   float qv[G][8];

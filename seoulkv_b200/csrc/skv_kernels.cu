@@ -20,6 +20,7 @@
 //   k_attn           FP8 sink + local + top-100 online softmax, LSE combine
 #include <cuda_fp8.h>
 
+#include "skv_codec.cuh"
 #include "skv_device.cuh"
 #include "skv_kernels.cuh"
 #include "skv_select.cuh"
@@ -812,7 +813,7 @@ __global__ void __launch_bounds__(256) k_attn(Work w) {
   const int split = blockIdx.x, cell = blockIdx.y, slot = cell >> 2, g = cell & 3;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const CellDev &c = w.cells[cell];
-  const int sink = w.sink, local = w.local, T = w.T, dense = sink + local;
+  const int sink = w.sink, local = w.local, T = context_of(w), dense = sink + local;
   const int nitems = dense + G * TOPK;
   const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
   __shared__ float s_m[G][8], s_l[G][8];
@@ -965,40 +966,19 @@ __global__ void __launch_bounds__(256) k_absmax(const uint16_t *k, int T, uint32
   atomicMax(&smax[g * D + d], __float_as_uint(mx));
 }
 
-// Key code planes (reference _codecs/keys.py:16-44): code8 =
-// clamp(floor((k + s) / (2s/256)), 0, 255), prefix2 = code8 >> 6,
-// residual2 = (code8 >> 4) & 3, residual4 = code8 & 15.
+// Key code planes of every token (encode_key_quad), the scales being the
+// per-dimension maxima k_absmax gathered.
 __global__ void __launch_bounds__(256) k_planes(const uint16_t *k, int T, const uint32_t *smax,
                                                 float *scale_out, uint8_t *p2, uint8_t *r2,
                                                 uint8_t *r4, int g) {
   const int tid = threadIdx.x, tok = blockIdx.x * 4 + (tid >> 6), q = tid & 63;
-  if (blockIdx.x == 0 && tid < 64)
-    for (int j = 0; j < 4; ++j) scale_out[4 * tid + j] = fmaxf(__uint_as_float(smax[g * D + 4 * tid + j]), 1e-9f);
+  __shared__ float s_scale[D];
+  s_scale[tid] = fmaxf(__uint_as_float(smax[g * D + tid]), 1e-9f);
+  __syncthreads();
+  if (blockIdx.x == 0) scale_out[tid] = s_scale[tid];
   if (tok >= T) return;
-  uint32_t pb = 0, rb = 0, l0 = 0, l1 = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int d = 4 * q + j;
-    const float s = fmaxf(__uint_as_float(smax[g * D + d]), 1e-9f);
-    const float step = __fdiv_rn(__fmul_rn(2.0f, s), 256.0f);
-    const float x = bf16f(k[((size_t)g * T + tok) * D + d]);
-    const float f = floorf(__fdiv_rn(__fadd_rn(x, s), step));
-    const uint32_t code = (uint32_t)fminf(fmaxf(f, 0.0f), 255.0f);
-    pb |= (code >> 6) << (2 * j);
-    rb |= ((code >> 4) & 3u) << (2 * j);
-    if (j < 2) l0 |= (code & 15u) << (4 * j); else l1 |= (code & 15u) << (4 * (j - 2));
-  }
-  p2[(size_t)tok * 64 + q] = (uint8_t)pb;
-  r2[(size_t)tok * 64 + q] = (uint8_t)rb;
-  r4[(size_t)tok * 128 + 2 * q] = (uint8_t)l0;
-  r4[(size_t)tok * 128 + 2 * q + 1] = (uint8_t)l1;
-}
-
-// FP32 -> FP8 e4m3 with torch's float8_e4m3fn semantics: nearest even,
-// |x| > 464 or NaN -> NaN.
-__device__ __forceinline__ uint8_t to_e4m3(float x) {
-  if (!(fabsf(x) <= 464.0f)) return (uint8_t)(0x7fu | ((__float_as_uint(x) >> 24) & 0x80u));
-  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  encode_key_quad(k + ((size_t)g * T + tok) * D, s_scale, q, p2 + (size_t)tok * 64, r2 + (size_t)tok * 64,
+                  r4 + (size_t)tok * 128);
 }
 
 __global__ void __launch_bounds__(256) k_fp8(const uint16_t *k, const uint16_t *v, int T, uint8_t *kv8, int g) {

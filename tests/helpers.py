@@ -121,3 +121,69 @@ class Golden:
                              resid_bf16=v["resid_bf16"], offsets=v["offsets"], values=v["values"],
                              context=self.context, prefix2=p2[g], residual2=r2[g], residual4=r4[g],
                              key_scale=scales[g]) for g, v in enumerate(self.views())]
+
+
+# ------------------------------------------------------------ cache append
+
+
+class AppendCase:
+    """A cache built on its first ``context`` tokens and grown by appends up to
+    ``total`` tokens, with the oracle's view of every intermediate context."""
+
+    def __init__(self, context=8192, total=8192 + 700, nprobe=128, seed=23, components=256, sink=128, local=256):
+        self.context, self.total, self.sink, self.local = context, total, sink, local
+        self.k_full, self.v_full, self.mixes = synthetic.make_kv(total, seed=seed, components=components)
+        self.k = self.k_full[:, :context].contiguous()
+        self.v = self.v_full[:, :context].contiguous()
+        self.index = SeoulKV4Index.build(self.k, self.v, sink=sink, local=local, nprobe=nprobe)
+        self.kb = bits(self.k_full)
+        self.scales = O.key_codec(bits(self.k))[0]
+        self.planes = [O.encode_planes(self.kb[g], self.scales[g]) for g in range(4)]
+        self.views = [device_view(c) for c in self.index.cells()]
+        first = context - local
+        self.labels = [O.assign_spill2(self.kb[g, first:total], v["upper"], v["lower"], v["fine_scale"])
+                       for g, v in enumerate(self.views)]
+        self._k8 = self._v8 = None
+
+    def appended(self, a, b):
+        """K and V of tokens [a, b) as BF16 [4, b-a, 256]."""
+        return self.k_full[:, a:b].contiguous(), self.v_full[:, a:b].contiguous()
+
+    def csr(self, g, t):
+        """Oracle (offsets, values, mates) of KV head g at context t."""
+        v = self.views[g]
+        first = self.context - self.local
+        entering = np.arange(first, t - self.local)
+        return O.append_postings(v["offsets"], v["values"], v["mates"], entering, self.labels[g][:len(entering)])
+
+    def cells(self, t, nprobe=None):
+        out = []
+        for g, v in enumerate(self.views):
+            off, vals, _ = self.csr(g, t)
+            p2, r2, r4 = self.planes[g]
+            out.append(O.CellInputs(
+                nc=v["nc"], nprobe=v["nprobe"] if nprobe is None else nprobe[g], lam=v["lam"], upper=v["upper"],
+                lower=v["lower"], coarse_scale4=v["coarse_scale4"], fine_scale=v["fine_scale"],
+                resid_bf16=v["resid_bf16"], offsets=off, values=vals, context=t, prefix2=p2[:t],
+                residual2=r2[:t], residual4=r4[:t], key_scale=self.scales[g]))
+        return out
+
+    def query(self, t, seed):
+        return synthetic.make_query(t, self.mixes, seed=seed)
+
+    def kv8(self):
+        if self._k8 is None:
+            self._k8 = O.fp8_e4m3(self.k_full.float().numpy())
+            self._v8 = O.fp8_e4m3(self.v_full.float().numpy())
+        return self._k8, self._v8
+
+    def oracle(self, q, t, capacity=13056):
+        qb = bits(q).reshape(16, 256)
+        res = [O.run_cell(c, qb[4 * g:4 * g + 4], capacity=capacity) for g, c in enumerate(self.cells(t))]
+        k8, v8 = self.kv8()
+        out = np.zeros((16, 256), np.uint16)
+        for j in range(16):
+            g, h = divmod(j, 4)
+            keys = O.attention_keys(t, self.sink, self.local, res[g]["final_ids"][h])
+            out[j] = O.attention(qb[j], k8[g], v8[g], keys)
+        return res, out
