@@ -60,6 +60,9 @@ def parse():
                    help="batched mode: R independent requests of --context tokens, split over the GPUs "
                         "(BASELINE configs[4]); sweeps --sweep nprobe values")
     p.add_argument("--sweep", default="16,64,128,256,384,512", help="nprobe values of the batched mode")
+    p.add_argument("--append", type=int, default=0,
+                   help="decode-loop mode: every step appends this many tokens to the --context cache, then "
+                        "decodes one query over the grown cache")
     p.add_argument("--transport", default="p2p", choices=("p2p", "nccl"),
                    help="sharded exchange: peer memory inside the step graph, or NCCL all-gathers")
     return p.parse_args()
@@ -489,6 +492,106 @@ def run_stack(args, device):
     print(json.dumps(line))
 
 
+def run_append(args, device):
+    """A growing cache at the headline context: every step appends M new
+    tokens (K/V already on the device, as a model's projection leaves them)
+    and decodes one fresh query over the grown cache.  Reports the append,
+    the decode after it and the whole step, plus a parity check of the
+    appended tokens' lists and the live CSR against the CPU restatement."""
+    from oracle import oracle as O
+    from seoulkv_b200 import SeoulKV4, SeoulKV4Config, SeoulKV4Index, synthetic
+    from seoulkv_b200.index import device_view
+
+    M, T0 = args.append, args.context
+    n = args.warmup + args.steps
+    total = T0 + n * M
+    seed = CONFIG_INDEX * 1000 + 600
+    k, v, mixes = synthetic.make_kv(total, seed=seed, components=args.components)
+    k0, v0 = k[:, :T0].contiguous(), v[:, :T0].contiguous()
+    index = SeoulKV4Index.build(k0, v0, sink=128, local=256, nprobe=args.nprobe, build_device=str(device))
+    kn = [k[:, T0 + i * M:T0 + (i + 1) * M].contiguous().to(device) for i in range(n)]
+    vn = [v[:, T0 + i * M:T0 + (i + 1) * M].contiguous().to(device) for i in range(n)]
+    qs = torch.stack([synthetic.make_query(T0 + (i + 1) * M, mixes, seed=seed * 7919 + i)
+                      for i in range(n)]).to(device)
+    attn = SeoulKV4(device=device, k=k0, v=v0, index=index, config=SeoulKV4Config(debug=True, max_context=total))
+    attn.run(synthetic.make_query(T0, mixes, seed=seed).to(device)).to_torch()
+    eng = attn._engine
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    qbits = qs.view(torch.int16)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+    for i in range(args.warmup):
+        flush.zero_()
+        attn.append(kn[i], vn[i])
+        eng.step(qbits[i].data_ptr(), True, stream.cuda_stream)
+    torch.cuda.synchronize(device)
+    clocks = Clocks(device.index)
+    clocks.start()
+    time.sleep(0.3)
+    gc.disable()
+    torch.cuda._sleep(int(2e7))  # the host enqueues ahead of the device
+    for i in range(args.warmup, n):
+        flush.zero_()
+        ev[i][0].record(stream)
+        attn.append(kn[i], vn[i])
+        ev[i][1].record(stream)
+        eng.step(qbits[i].data_ptr(), True, stream.cuda_stream)
+        ev[i][2].record(stream)
+    torch.cuda.synchronize(device)
+    gc.enable()
+    clk = clocks.stop()
+    eng.sync()
+    t_app = np.array([ev[i][0].elapsed_time(ev[i][1]) * 1e3 for i in range(args.warmup, n)])
+    t_dec = np.array([ev[i][1].elapsed_time(ev[i][2]) * 1e3 for i in range(args.warmup, n)])
+    assert attn.context == total and eng.current_context() == total
+
+    # parity: the appended tokens' lists (a sample, against the restatement),
+    # and the whole live CSR rebuilt on the CPU from the device's lists
+    first = T0 - 256
+    labels = eng.read_stage(0, "labels", np.int32, (4, total, 2))
+    rng = np.random.default_rng(seed)
+    sample = np.sort(rng.choice(np.arange(T0, total), size=min(8, total - T0), replace=False))
+    kb = k.contiguous().view(torch.int16).numpy().view(np.uint16)
+    views = [device_view(c) for c in index.cells()]
+    lab_ok = all(np.array_equal(labels[g, sample], O.assign_spill2(kb[g, sample], views[g]["upper"],
+                                                                   views[g]["lower"], views[g]["fine_scale"]))
+                 for g in range(4))
+    csr = eng.read_csr(0)
+    csr_ok = True
+    for g in range(4):
+        want = O.append_postings(views[g]["offsets"], views[g]["values"], views[g]["mates"],
+                                 np.arange(first, total - 256), labels[g, first:total - 256])
+        csr_ok &= all(np.array_equal(a, b) for a, b in zip(csr[g], want))
+    # algorithmic bytes of one append: the centroid codes read by the
+    # assignment, the CSR read and rewritten, the new tokens' K/V read and
+    # their planes and records written
+    nc = views[0]["nc"]
+    post = int(sum(int(c[0][-1]) for c in csr)) / 4
+    app_bytes = 4 * (nc * 128 + 2 * (nc + 1) * 4 + 2 * 2 * post * 4 + M * (2 * 512 + 64 + 64 + 128 + 512))
+    # FP64 work of the assignment: a multiply-add per (token, centroid,
+    # dimension) and a code weight per (token group of 4 or single token,
+    # centroid, dimension)
+    fp64 = 4 * nc * 256 * (2 * M + M // 4 + M % 4)
+    a_mean = float(np.mean(t_app))
+    line = {
+        "metric": f"us per decode-loop step at {T0 // 1024}K ctx: append {M} token(s), then one sparse decode",
+        "value": float(np.mean(t_app + t_dec)), "unit": "us/step", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": False,
+        "data": "synthetic (BASELINE generator), new K/V tokens of the same mixture, fresh Q at the grown context",
+        "config": {"workload": f"T={T0} grown by {M} token(s) per step to {total}, 4 KV / 16 Q heads, d=256, "
+                               f"nprobe={args.nprobe}", "l2": "flushed before every step"},
+        "append_us": a_mean, "append_p50_us": float(np.median(t_app)), "append_p99_us": float(np.percentile(t_app, 99)),
+        "decode_us": float(np.mean(t_dec)), "decode_p50_us": float(np.median(t_dec)),
+        "append_algorithmic_bytes": app_bytes, "append_gbs": app_bytes / (a_mean * 1e-6) / 1e9,
+        "append_fp64_flops": fp64, "append_fp64_tflops": fp64 / (a_mean * 1e-6) / 1e12,
+        "parity": {"sampled_token_lists_equal_restatement": bool(lab_ok), "live_csr_equals_restatement": bool(csr_ok),
+                   "sample_tokens": sample.tolist()},
+        "clocks": clk,
+    }
+    attn.close()
+    print(json.dumps(line))
+
+
 def run_requests(args, world, rank, device):
     """independent requests (one query token each) split
     contiguously over the GPUs (no collective on the data path), decoded as one
@@ -590,6 +693,9 @@ def main():
         return
     if args.layers:
         run_stack(args, device)
+        return
+    if args.append:
+        run_append(args, device)
         return
     if world > 1:
         run_sharded(args, world, rank, local, device)

@@ -47,6 +47,7 @@ extern "C" {
 #define SKV_STATUS_FINE_SHORT 4u  /* a head had fewer than nprobe survivors */
 #define SKV_STATUS_TIMEOUT 8u     /* a bounded device wait gave up (results invalid) */
 #define SKV_STATUS_APPEND_FULL 16u /* an append replayed from a graph did not fit max_context (skipped) */
+#define SKV_STATUS_APPEND_NONFINITE 32u /* an appended key had a non-finite element (assigned as 0) */
 
 /* SkvDesc.flags */
 #define SKV_FLAG_STAGED 1         /* run the 14-kernel staged path even where the
@@ -159,7 +160,10 @@ int skv_debug_ids(void *handle, int32_t *out);
  * stream-ordered (no host wait for device input); uploads are closed
  * afterwards.  SKV_E_CAPACITY when the append would pass max_context (a
  * replayed append that does not fit is skipped and raises
- * SKV_STATUS_APPEND_FULL instead).  A sharded engine takes no appends. */
+ * SKV_STATUS_APPEND_FULL instead).  Keys are checked on the device: a
+ * non-finite element counts as 0 in the assignment and raises
+ * SKV_STATUS_APPEND_NONFINITE.  Both bits stay set for the engine's life
+ * (skv_sync and skv_finish then fail).  A sharded engine takes no appends. */
 int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tokens, int32_t on_device,
                void *stream);
 /* The slots' current context, after every enqueued append (waits). */
@@ -186,6 +190,8 @@ int skv_context(void *handle, int32_t *context);
 #define SKV_STAGE_OFFSETS 15    /* int32 [4][nc+1] live CSR offsets              */
 #define SKV_STAGE_VALUES 16     /* int32 per cell offsets[nc] token ids, cell after cell */
 #define SKV_STAGE_MATES 17      /* int32 per cell offsets[nc] mates, cell after cell     */
+#define SKV_STAGE_LABELS 18     /* int32 [4][T][2] spill-2 lists of tokens from the first local window on
+                                   (engines with appends; -1 below the window)     */
 int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
                    size_t *written);
 

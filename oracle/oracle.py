@@ -197,11 +197,13 @@ def assign_spill2(k_bf16_bits: np.ndarray, upper: np.ndarray, lower: np.ndarray,
         S(k, c) = fl64( fl64sum_{d = 0..255}( k_d * (2 code_cd - 15) ) * fine_scale[c // 32] )
 
     with the sum taken in dimension order in float64 (each product is exact)
-    and ties going to the lower centroid id.  Returns int64 [m, 2] (best, second).
+    and ties going to the lower centroid id; a non-finite key element counts
+    as 0.  Returns int64 [m, 2] (best, second).
     """
     w = centroid_weights(upper, lower)                      # [nc, 256]
     nc = w.shape[0]
     k = bf16_to_f32(np.asarray(k_bf16_bits, dtype=np.uint16).reshape(-1, 256)).astype(np.float64)
+    k = np.where(np.isfinite(k), k, 0.0)
     acc = np.zeros((k.shape[0], nc), dtype=np.float64)
     for d in range(256):
         acc = acc + k[:, d:d + 1] * w[None, :, d]           # one rounding per step, no fused multiply-add

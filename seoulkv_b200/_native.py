@@ -23,7 +23,7 @@ SKV_E_CAPACITY = -3
 
 STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8,
              prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13, final_keys=14, offsets=15,
-             values=16, mates=17)
+             values=16, mates=17, labels=18)
 
 EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",

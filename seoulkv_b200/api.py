@@ -43,8 +43,7 @@ def _check_append(k, v, lead: tuple, context: int | None, max_context: int) -> i
     """Validate appended K/V (BF16 [*lead, m, 256], one device type); returns m.
 
     ``context`` None: the append is being captured into a CUDA graph, where
-    nothing may wait on the device; the finiteness of the keys is then the
-    caller's to guarantee and the engine's own device-side capacity check
+    nothing may wait on the device; the engine's device-side capacity check
     (a skipped append and an error at the next synchronize) replaces the
     host's.
     """
@@ -63,7 +62,9 @@ def _check_append(k, v, lead: tuple, context: int | None, max_context: int) -> i
     m = int(k.shape[-2])
     if context is None:
         return m
-    if not bool(torch.isfinite(k).all()):
+    # host keys are checked here; CUDA keys on the device (no wait), where a
+    # non-finite element counts as 0 and the next synchronize raises
+    if k.device.type == "cpu" and not bool(torch.isfinite(k).all()):
         raise ValueError("appended keys must be finite")
     if context + m > max_context:
         hint = " (SeoulKV4Config(max_context=...) lets the cache grow)" if max_context == context else ""

@@ -12,7 +12,8 @@
 //                    with the sum taken in dimension order in FP64 (every
 //                    product is exact: an 8-bit significand times a 5-bit
 //                    integer) and fs_c the FP16 group fine scale of c's
-//                    32-centroid group; each block keeps a top-2 over a
+//                    32-centroid group (a non-finite key element counts as
+//                    0 and is reported); each block keeps a top-2 over a
 //                    share of the centroids
 //   k_assign_reduce  top-2 over the shares (ties to the lower centroid id):
 //                    the token's two lists
@@ -119,7 +120,14 @@ __global__ void __launch_bounds__(256) k_assign(AssignArgs a, int j_begin) {
   __shared__ double s_k[TG][D];
   __shared__ Top2 s_t[8][TG];
 #pragma unroll
-  for (int t = 0; t < TG; ++t) s_k[t][tid] = (double)bf16f(a.k[y * a.k_cell_stride + (long long)(j0 + t) * D + tid]);
+  for (int t = 0; t < TG; ++t) {
+    float x = bf16f(a.k[y * a.k_cell_stride + (long long)(j0 + t) * D + tid]);
+    if (!isfinite(x)) {
+      x = 0.0f;
+      if (a.status && split == 0) atomicOr(a.status, APPEND_NONFINITE);
+    }
+    s_k[t][tid] = (double)x;
+  }
   __syncthreads();
   const CellDev &c = a.cells[cell];
   Top2 best[TG];

@@ -16,7 +16,8 @@ namespace skv {
 
 constexpr int APPEND_MAX = 512;    // tokens per append launch sequence
 constexpr int ASSIGN_SPLIT = 32;   // centroid partitions per cell in the assignment
-constexpr uint32_t APPEND_FULL = 1u;  // append status: a device-side append would have passed the capacity
+constexpr uint32_t APPEND_FULL = 1u;       // append status: a device-side append would have passed the capacity
+constexpr uint32_t APPEND_NONFINITE = 2u;  // append status: an appended key had a non-finite element
 
 // Append state of one cell (device memory).
 struct AppendCellDev {
@@ -31,7 +32,9 @@ struct AppendCellDev {
 // Spill-2 assignment of `m` key rows per cell (rows j of cell cell0 + y at
 // k + y * k_cell_stride + j * 256); results go to labels[base + j] with base
 // = (use_tlen ? *tlen : 0) + lab_base.  With guard > 0 nothing runs when
-// *tlen + guard > tmax (an append that does not fit).
+// *tlen + guard > tmax (an append that does not fit).  A non-finite key
+// element counts as 0 (and raises APPEND_NONFINITE in *status, if given), so
+// every token gets two valid lists.
 struct AssignArgs {
   const CellDev *cells;
   AppendCellDev *acells;
@@ -39,6 +42,7 @@ struct AssignArgs {
   const uint16_t *k;
   long long k_cell_stride;
   int cell0, n_cells, m, nc, split, lab_base, use_tlen, guard, tmax;
+  uint32_t *status;  // append status word, or null
   double *part_s;   // [cell][APPEND_MAX][ASSIGN_SPLIT][2] partial top-2 scores
   int32_t *part_i;  // same layout, centroid ids
 };

@@ -218,6 +218,12 @@ int status_error(const Engine *e, const SkvStatus &s) {
                   e->tmax, s.flags);
     return fail(SKV_E_CAPACITY, msg);
   }
+  if (s.flags & SKV_STATUS_APPEND_NONFINITE) {
+    std::snprintf(msg, sizeof msg,
+                  "an appended key had a non-finite element (assigned as 0; its FP8 record keeps it) (status 0x%x)",
+                  s.flags);
+    return fail(SKV_E_INVALID, msg);
+  }
   std::snprintf(msg, sizeof msg,
                 "live count out of range at cell %d (status 0x%x: %s%s%s); pool range [%d, %d], capacity %d",
                 s.first_bad_cell, s.flags, (s.flags & SKV_STATUS_POOL_OVER) ? "pool above capacity " : "",
@@ -586,6 +592,8 @@ int skv_upload_kv(void *handle, int32_t slot, const uint16_t *k, const uint16_t 
         ce = cudaMemcpyAsync(e->wkeys[slot] + (size_t)g * local * D, dk + ((size_t)g * T + T - local) * D,
                              local * D * 2, cudaMemcpyDeviceToDevice, e->stream);
     }
+    for (int g = 0; g < G && ce == cudaSuccess && e->appends(); ++g)
+      ce = cudaMemsetAsync(e->bufs[slot * G + g].labels, 0xff, rows * 2 * sizeof(int32_t), e->stream);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
     if (ce != cudaSuccess) rc = fail(SKV_E_CUDA, std::string("key codec: ") + cudaGetErrorString(ce));
   }
@@ -771,6 +779,7 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   s.use_tlen = 1;
   s.guard = n_tokens;
   s.tmax = e->tmax;
+  s.status = e->append_status;
   s.part_s = e->part_s;
   s.part_i = e->part_i;
   CK(launch_append(a, s, st));
@@ -834,6 +843,7 @@ int skv_status(void *handle, SkvStatus *out) {
     uint32_t as = 0;
     CK(cudaMemcpy(&as, e->append_status, sizeof as, cudaMemcpyDeviceToHost));
     if (as & APPEND_FULL) s.flags |= SKV_STATUS_APPEND_FULL;
+    if (as & APPEND_NONFINITE) s.flags |= SKV_STATUS_APPEND_NONFINITE;
   }
   *out = s;
   return SKV_OK;
@@ -952,11 +962,14 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
     case SKV_STAGE_RESIDUAL2:
     case SKV_STAGE_RESIDUAL4:
     case SKV_STAGE_KV8:
-    case SKV_STAGE_KEY_SCALE: {
+    case SKV_STAGE_KEY_SCALE:
+    case SKV_STAGE_LABELS: {
+      if (which == SKV_STAGE_LABELS && !e->appends()) return fail(SKV_E_STATE, "the engine takes no appends");
       int32_t tcur = 0;
       if ((rc = device_context(e, &tcur))) return rc;
       const size_t T = tcur;
       const size_t row = which == SKV_STAGE_RESIDUAL4 ? 128 : which == SKV_STAGE_KV8 ? REC
+                       : which == SKV_STAGE_LABELS ? 2 * sizeof(int32_t)
                        : which == SKV_STAGE_KEY_SCALE ? 0 : 64;
       const size_t per = which == SKV_STAGE_KEY_SCALE ? D * sizeof(float) : T * row;
       size_t done = 0;
@@ -965,7 +978,8 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
         const void *p = which == SKV_STAGE_PREFIX2 ? (const void *)b.prefix2
                       : which == SKV_STAGE_RESIDUAL2 ? (const void *)b.residual2
                       : which == SKV_STAGE_RESIDUAL4 ? (const void *)b.residual4
-                      : which == SKV_STAGE_KV8 ? (const void *)b.kv8 : (const void *)b.key_scale;
+                      : which == SKV_STAGE_KV8 ? (const void *)b.kv8
+                      : which == SKV_STAGE_LABELS ? (const void *)b.labels : (const void *)b.key_scale;
         if (!p) return fail(SKV_E_STATE, "K/V not uploaded for this slot");
         const size_t m = std::min(per, bytes - done);
         CK(cudaMemcpy(static_cast<char *>(dst) + done, p, m, cudaMemcpyDeviceToHost));

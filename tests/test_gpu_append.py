@@ -58,6 +58,16 @@ def _check_planes(ac, eng, t0, t, slot=0):
         np.testing.assert_array_equal(rec[:, 256:], v8[g, t0:t])
 
 
+def _check_labels(ac, eng, t, slot=0):
+    """Every token's two lists, from the first local window (assigned at
+    upload) through the appended tokens, equal the oracle's assignment."""
+    lab = eng.read_stage(slot, "labels", np.int32, (4, t, 2))
+    first = ac.context - ac.local
+    for g in range(4):
+        assert (lab[g, :first] == -1).all()
+        assert np.array_equal(lab[g, first:t], ac.labels[g][:t - first]), g
+
+
 @pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
 @pytest.mark.parametrize("device_input", [False, True], ids=["host", "device"])
 def test_append_matches_oracle(ac, cuda, staged, device_input, monkeypatch):
@@ -78,6 +88,7 @@ def test_append_matches_oracle(ac, cuda, staged, device_input, monkeypatch):
             _check_csr(ac, attn._engine, t)
             _check_decode(ac, attn, t, seed=t)
         _check_planes(ac, attn._engine, ac.context, t)
+        _check_labels(ac, attn._engine, t)
         with pytest.raises(ValueError, match="passes max_context"):
             attn.append(*ac.appended(t - 1, t))
 
@@ -156,3 +167,22 @@ def test_batch_append(ac, cuda):
             for g in range(4):
                 assert np.array_equal(ids[i, g], res[g]["final_ids"])
             _check_out(bits(out[i]).reshape(16, 256), want)
+
+
+def test_append_nonfinite_key_counts_as_zero(ac, cuda):
+    """A CUDA key with a NaN element is appended without a host wait: the
+    element counts as 0 in the assignment and the next synchronize raises."""
+    cfg = SeoulKV4Config(max_context=ac.context + 1)
+    with SeoulKV4(device=cuda, k=ac.k, v=ac.v, index=ac.index, config=cfg) as attn:
+        attn.run(ac.query(ac.context, seed=9)).to_torch()
+        k, v = ac.appended(ac.context, ac.context + 1)
+        k = k.clone()
+        k[2, 0, 17] = float("nan")
+        attn.append(k.cuda(), v.cuda())
+        with pytest.raises(RuntimeError, match="non-finite"):
+            attn.synchronize()
+        lab = attn._engine.read_stage(0, "labels", np.int32, (4, ac.context + 1, 2))
+        for g in range(4):
+            view = ac.views[g]
+            want = O.assign_spill2(bits(k[g]), view["upper"], view["lower"], view["fine_scale"])[0]
+            assert list(lab[g, ac.context]) == list(want), g
