@@ -568,10 +568,9 @@ def run_append(args, device):
     nc = views[0]["nc"]
     post = int(sum(int(c[0][-1]) for c in csr)) / 4
     app_bytes = 4 * (nc * 128 + 2 * (nc + 1) * 4 + 2 * 2 * post * 4 + M * (2 * 512 + 64 + 64 + 128 + 512))
-    # FP64 work of the assignment: a multiply-add per (token, centroid,
-    # dimension) and a code weight per (token group of 4 or single token,
-    # centroid, dimension)
-    fp64 = 4 * nc * 256 * (2 * M + M // 4 + M % 4)
+    # tensor work of the assignment: per group of 4 new keys and cell, 16
+    # int8 m16n8k32 MMAs (4096 multiply-adds each) per 16-centroid tile
+    int8_ops = 4 * (nc // 16) * 16 * 4096 * 2 * ((M + 3) // 4)
     a_mean = float(np.mean(t_app))
     line = {
         "metric": f"us per decode-loop step at {T0 // 1024}K ctx: append {M} token(s), then one sparse decode",
@@ -583,7 +582,7 @@ def run_append(args, device):
         "append_us": a_mean, "append_p50_us": float(np.median(t_app)), "append_p99_us": float(np.percentile(t_app, 99)),
         "decode_us": float(np.mean(t_dec)), "decode_p50_us": float(np.median(t_dec)),
         "append_algorithmic_bytes": app_bytes, "append_gbs": app_bytes / (a_mean * 1e-6) / 1e9,
-        "append_fp64_flops": fp64, "append_fp64_tflops": fp64 / (a_mean * 1e-6) / 1e12,
+        "append_int8_ops": int8_ops, "append_int8_tops": int8_ops / (a_mean * 1e-6) / 1e12,
         "parity": {"sampled_token_lists_equal_restatement": bool(lab_ok), "live_csr_equals_restatement": bool(csr_ok),
                    "sample_tokens": sample.tolist()},
         "clocks": clk,

@@ -151,8 +151,11 @@ int skv_debug_ids(void *handle, int32_t *out);
  * its key planes (with the build's per-dimension scales, codes clamped to
  * 0..255) and FP8 record at positions T..T+n-1, and its two spill-2 lists:
  * the top-2 stored centroids by
- *     S(k, c) = fl64(fl64sum_{d ascending}(k_d * (2 code_cd - 15)) * fine_scale_c)
- * (FP64, dimension order, ties to the lower centroid).  The tokens leaving
+ *     S(k, c) = fl64(X(k, c) * fine_scale_c),  X(k, c) = sum_d x_d (2 code_cd - 15)
+ * with x the key on the decode's operand grid (elements below 2^(E-22) of
+ * its top exponent E flushed, the rest integers on the 2^(E-29) grid), X
+ * exact, ties to the lower centroid: the Fine score with the key as the
+ * query.  The tokens leaving
  * the local window (T-local .. T-local+n-1) join their two lists after the
  * lists' current postings.  The context then advances by n on the device,
  * so decode steps replayed from graphs, and appends captured in one, see

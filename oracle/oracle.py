@@ -190,25 +190,36 @@ def centroid_weights(upper: np.ndarray, lower: np.ndarray) -> np.ndarray:
     return (2 * code - 15).astype(np.float64)
 
 
+def operand_grid(x: np.ndarray) -> np.ndarray:
+    """Rows of float64 values on the decode's operand grid: with E the row's
+    top exponent, elements below 2^(E-22) become 0 and the rest the integers
+    x / 2^(E-29) (exact, |X| < 2^30); the grid of ``skv_oracle_prepare_query``."""
+    x = np.asarray(x, dtype=np.float64)
+    _, ex = np.frexp(np.abs(x))                             # |x| = mant * 2^ex, mant in [0.5, 1)
+    e = np.where(x != 0, ex - 1, np.iinfo(np.int32).min)
+    E = e.max(axis=-1, keepdims=True)
+    keep = (x != 0) & (e >= E - 22)
+    return np.where(keep, np.ldexp(x, (29 - np.where(keep, E, 0)).astype(np.int32)), 0.0)
+
+
 def assign_spill2(k_bf16_bits: np.ndarray, upper: np.ndarray, lower: np.ndarray,
                   fine_scale: np.ndarray) -> np.ndarray:
     """The two lists of each key [m, 256] (BF16 patterns): the top-2 centroids by
 
-        S(k, c) = fl64( fl64sum_{d = 0..255}( k_d * (2 code_cd - 15) ) * fine_scale[c // 32] )
+        S(k, c) = fl64( X(k, c) * fine_scale[c // 32] ),   X(k, c) = sum_d x_d * (2 code_cd - 15)
 
-    with the sum taken in dimension order in float64 (each product is exact)
-    and ties going to the lower centroid id; a non-finite key element counts
-    as 0.  Returns int64 [m, 2] (best, second).
+    with x the key on the decode's operand grid (``operand_grid``; a
+    non-finite element counts as 0), X exact (an integer below 2^42, so the
+    float64 matrix product is exact in any order) and ties going to the lower
+    centroid id.  Returns int64 [m, 2] (best, second).
     """
     w = centroid_weights(upper, lower)                      # [nc, 256]
     nc = w.shape[0]
     k = bf16_to_f32(np.asarray(k_bf16_bits, dtype=np.uint16).reshape(-1, 256)).astype(np.float64)
     k = np.where(np.isfinite(k), k, 0.0)
-    acc = np.zeros((k.shape[0], nc), dtype=np.float64)
-    for d in range(256):
-        acc = acc + k[:, d:d + 1] * w[None, :, d]           # one rounding per step, no fused multiply-add
+    X = operand_grid(k) @ w.T                               # exact integers
     fs = np.repeat(np.asarray(fine_scale, dtype=np.float32).astype(np.float64), 32)[:nc]
-    s = acc * fs[None, :]
+    s = X * fs[None, :]
     best = np.argmax(s, axis=1)                             # first maximum: the lower id on ties
     s2 = s.copy()
     s2[np.arange(len(best)), best] = -np.inf

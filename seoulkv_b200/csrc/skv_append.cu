@@ -1,33 +1,36 @@
 // skv_append.cu -- cache-append kernels.
 //
-// An append of m tokens to every cell of the engine is six stream-ordered
+// An append of m tokens to every cell of the engine is four stream-ordered
 // launches that read the current context from device memory, so the same
 // launches replayed from a graph append at successive positions:
 //
-//   k_append_codec   key planes (the build's scales) and FP8 records of the
-//                    new tokens at positions T .. T+m-1
-//   k_assign<TG>     spill-2 assignment of the new keys: score of key k
-//                    against stored centroid c is
-//                        S(k, c) = fl64( fl64sum_{d=0..255}( k_d * (2 code_cd - 15) ) * fs_c )
-//                    with the sum taken in dimension order in FP64 (every
-//                    product is exact: an 8-bit significand times a 5-bit
-//                    integer) and fs_c the FP16 group fine scale of c's
-//                    32-centroid group (a non-finite key element counts as
-//                    0 and is reported); each block keeps a top-2 over a
-//                    share of the centroids
-//   k_assign_reduce  top-2 over the shares (ties to the lower centroid id):
-//                    the token's two lists
-//   k_post_prepare   the tokens leaving the local window, T-local ..
-//                    T-local+m-1, as 2m (list, token) postings sorted by
-//                    list then token, each with its mate (the other list)
+//   k_assign         spill-2 assignment of the new keys, and (partition 0)
+//                    their key planes (the build's scales) and FP8 records
+//                    at positions T .. T+m-1.  The score of key k against
+//                    stored centroid c is
+//                        S(k, c) = fl64( X(k, c) * fs_c ),
+//                        X(k, c) = sum_d x_d * (2 code_cd - 15)   (exact)
+//                    where x is the key on the decode's operand grid (with E
+//                    its top exponent, elements below 2^(E-22) flushed, the
+//                    rest integers on the 2^(E-29) grid; a non-finite element
+//                    counts as 0 and is reported) and fs_c the FP16 group
+//                    fine scale of c's 32-centroid group.  This is the Fine
+//                    stage's centroid score with the key as the query,
+//                    computed the way the decode computes it (int8 digit
+//                    fragments on the tensor cores, int64 recombination) and
+//                    rounded once.  Each CTA keeps a top-2 per key over a
+//                    partition of the centroids.
+//   k_append_lists   top-2 over the partitions (ties to the lower centroid
+//                    id): the new tokens' two lists; then the tokens leaving
+//                    the local window, T-local .. T-local+m-1, as 2m (list,
+//                    token) postings sorted by list then token, each with its
+//                    mate (the other list) and its insertion point
 //   k_post_rebuild   the next CSR set: every old list followed by its new
 //                    postings, so each list stays in ascending token order
 //                    exactly as a CSR built over all tokens would be
 //   k_append_commit  the live CSR set flips and the context advances
 //
-// The score is the Fine stage's centroid score of the key used as a query
-// (the decode path scores centroids with the same 4-bit codes and scales),
-// so a token is posted where the funnel looks for its nearest neighbours.
+// The score puts a token where the funnel looks for its nearest neighbours.
 #include <cuda_runtime.h>
 
 #include <cfloat>
@@ -79,16 +82,18 @@ __device__ __forceinline__ Top2 top2_merge(const Top2 &a, const Top2 &b) {
 
 __device__ __forceinline__ Top2 top2_empty() { return Top2{-DBL_MAX, -DBL_MAX, INT_MAX, INT_MAX}; }
 
+__device__ __forceinline__ Top2 shfl_top2(const Top2 &t, int o) {
+  Top2 u;
+  u.s1 = __shfl_xor_sync(0xffffffffu, t.s1, o);
+  u.s2 = __shfl_xor_sync(0xffffffffu, t.s2, o);
+  u.i1 = __shfl_xor_sync(0xffffffffu, t.i1, o);
+  u.i2 = __shfl_xor_sync(0xffffffffu, t.i2, o);
+  return u;
+}
+
 __device__ __forceinline__ Top2 warp_top2(Top2 t) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Top2 u;
-    u.s1 = __shfl_xor_sync(0xffffffffu, t.s1, o);
-    u.s2 = __shfl_xor_sync(0xffffffffu, t.s2, o);
-    u.i1 = __shfl_xor_sync(0xffffffffu, t.i1, o);
-    u.i2 = __shfl_xor_sync(0xffffffffu, t.i2, o);
-    t = top2_merge(t, u);
-  }
+  for (int o = 16; o > 0; o >>= 1) t = top2_merge(t, shfl_top2(t, o));
   return t;
 }
 
@@ -103,97 +108,166 @@ __device__ __forceinline__ int lower_bound_i32(const int32_t *a, int n, int x) {
   return lo;
 }
 
-// 2 code - 15 as an FP64 value without a conversion instruction:
-// 2^52 + 2 code is built from its bits and 2^52 + 15 subtracted (exact).
-__device__ __forceinline__ double code_weight(uint32_t code) {
-  return __hiloint2double(0x43300000, (int)(code << 1)) - 4503599627370511.0;
+__device__ __forceinline__ void load_plane_row(const uint8_t *base, int row, uint4 (&r)[4]) {
+  const uint4 *p = reinterpret_cast<const uint4 *>(base + (size_t)row * 64);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) r[k] = p[k];
 }
 
 // ------------------------------------------------------------------ assign
 
-template <int TG>
-__global__ void __launch_bounds__(256) k_assign(AssignArgs a, int j_begin) {
-  const int split = blockIdx.x, y = blockIdx.y, cell = a.cell0 + y, tid = threadIdx.x;
-  const int lane = tid & 31, warp = tid >> 5;
+// One CTA per (centroid partition, cell, group of 4 keys).  The keys are the
+// B operand of the decode's exact int8 dot (in the four query heads' place);
+// every warp scores 16-centroid tiles with the 4-bit codes as the A operand
+// and keeps a top-2 per key.  With `codec`, partition 0 also writes the
+// group's key planes and FP8 records (an append).
+__global__ void __launch_bounds__(256) k_assign(AssignArgs a, AppendArgs app, int codec) {
+  const int split = blockIdx.x, y = blockIdx.y, cell = a.cell0 + y, j0 = blockIdx.z * 4;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
   if (a.guard > 0 && !append_fits(a.tlen, a.guard, a.tmax)) return;
-  const int j0 = j_begin + blockIdx.z * TG;
-  __shared__ double s_k[TG][D];
-  __shared__ Top2 s_t[8][TG];
+  __shared__ uint32_t s_frag[FRAG_ROW];
+  __shared__ int s_e[4][8];
+  __shared__ Top2 s_t[8][4];
+  __shared__ float s_scale[D];
+  float x[4];
 #pragma unroll
-  for (int t = 0; t < TG; ++t) {
-    float x = bf16f(a.k[y * a.k_cell_stride + (long long)(j0 + t) * D + tid]);
-    if (!isfinite(x)) {
-      x = 0.0f;
-      if (a.status && split == 0) atomicOr(a.status, APPEND_NONFINITE);
+  for (int r = 0; r < 4; ++r) {
+    float v = 0.0f;
+    if (j0 + r < a.m) {
+      v = bf16f(a.k[y * a.k_cell_stride + (long long)(j0 + r) * D + tid]);
+      if (!isfinite(v)) {
+        v = 0.0f;
+        if (a.status && split == 0) atomicOr(a.status, APPEND_NONFINITE);
+      }
     }
-    s_k[t][tid] = (double)x;
+    x[r] = v;
+    const int e = __reduce_max_sync(0xffffffffu, v != 0.0f ? ilogbf(v) : INT_MIN);
+    if (lane == 0) s_e[r][warp] = e;
+  }
+  if (codec && split == 0) s_scale[tid] = app.acells[cell].key_scale[tid];
+  __syncthreads();
+  // digit fragments: the decode's operand encoding (elements below 2^(E-22)
+  // flushed, the rest integers X on the 2^(E-29) grid, |X| < 2^30, as four
+  // signed base-256 digits); key r of the group in query head r's columns
+  uint8_t *fb = reinterpret_cast<uint8_t *>(s_frag);
+  const int ks = tid >> 5, reg = (tid >> 4) & 1, byte = (tid >> 2) & 3, tq = tid & 3;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    int E = INT_MIN;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) E = max(E, s_e[r][k]);
+    int X = 0;
+    if (E != INT_MIN) {
+      const double v = (double)x[r];
+      if (!(fabs(v) < ldexp(1.0, E - 22))) X = __double2int_rn(ldexp(v, 29 - E));
+    }
+    int dg[4];
+    dg[0] = (int)(int8_t)(X & 0xff);
+    int rest = (X - dg[0]) >> 8;
+    dg[1] = (int)(int8_t)(rest & 0xff);
+    rest = (rest - dg[1]) >> 8;
+    dg[2] = (int)(int8_t)(rest & 0xff);
+    dg[3] = (rest - dg[2]) >> 8;
+    const int nt = r >> 1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int lane_b = 4 * (4 * (r & 1) + j) + tq;
+      fb[(((ks * 2 + nt) * 32 + lane_b) * 2 + reg) * 4 + byte] = (uint8_t)(int8_t)dg[j];
+    }
+  }
+  if (codec && split == 0) {  // the group's planes and records
+    const AppendCellDev &A = app.acells[cell];
+    const int T = *app.tlen;
+    for (int r = 0; r < 4 && j0 + r < a.m; ++r) {
+      const size_t tok = (size_t)T + j0 + r;
+      const uint16_t *krow = app.k + ((size_t)cell * app.m + j0 + r) * D;
+      const uint16_t *vrow = app.v + ((size_t)cell * app.m + j0 + r) * D;
+      A.kv8[tok * REC + tid] = to_e4m3(bf16f(krow[tid]));
+      A.kv8[tok * REC + 256 + tid] = to_e4m3(bf16f(vrow[tid]));
+      if (tid < 64)
+        encode_key_quad(krow, s_scale, tid, A.prefix2 + tok * 64, A.residual2 + tok * 64, A.residual4 + tok * 128);
+    }
   }
   __syncthreads();
-  const CellDev &c = a.cells[cell];
-  Top2 best[TG];
+  BFrag F;
 #pragma unroll
-  for (int t = 0; t < TG; ++t) best[t] = top2_empty();
-  for (int chunk = split; chunk * 256 < a.nc; chunk += a.split) {
-    const int ci = chunk * 256 + tid;
-    if (ci >= a.nc) continue;
-    const uint4 *up = reinterpret_cast<const uint4 *>(c.upper + (size_t)ci * 64);
-    const uint4 *lo = reinterpret_cast<const uint4 *>(c.lower + (size_t)ci * 64);
-    double acc[TG];
+  for (int k = 0; k < 8; ++k)
 #pragma unroll
-    for (int t = 0; t < TG; ++t) acc[t] = 0.0;
-#pragma unroll 1
-    for (int qd = 0; qd < 4; ++qd) {  // 64 dimensions per 16-byte quarter of each plane
-      const uint4 U = up[qd], L = lo[qd];
-      const uint32_t uw[4] = {U.x, U.y, U.z, U.w}, lw[4] = {L.x, L.y, L.z, L.w};
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int d = qd * 64 + r * 16 + i;
-          const uint32_t code = (((uw[r] >> (2 * i)) & 3u) << 2) | ((lw[r] >> (2 * i)) & 3u);
-          const double wv = code_weight(code);
-#pragma unroll
-          for (int t = 0; t < TG; ++t) acc[t] = fma(s_k[t][d], wv, acc[t]);
-        }
+    for (int nt = 0; nt < 2; ++nt) {
+      F.b[k][nt][0] = s_frag[((k * 2 + nt) * 32 + lane) * 2];
+      F.b[k][nt][1] = s_frag[((k * 2 + nt) * 32 + lane) * 2 + 1];
     }
-    const double fs = (double)c.fine_scale[ci >> 5];
+  const CellDev &c = a.cells[cell];
+  Top2 best[2] = {top2_empty(), top2_empty()};  // keys t/2 and 2 + t/2
+  const int tiles = a.nc >> 4;
+  for (int tile = split * 8 + warp; tile < tiles; tile += a.split * 8) {
+    const int rg = tile * 16 + g;
+    uint4 ug[4], lg[4], u8[4], l8[4];
+    load_plane_row(c.upper, rg, ug);
+    load_plane_row(c.lower, rg, lg);
+    load_plane_row(c.upper, rg + 8, u8);
+    load_plane_row(c.lower, rg + 8, l8);
+    int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 #pragma unroll
-    for (int t = 0; t < TG; ++t) top2_insert(best[t], acc[t] * fs, ci);
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t a0 = w_odd4(w2(word_of(ug, 2 * k), t), w2(word_of(lg, 2 * k), t));
+      const uint32_t a1 = w_odd4(w2(word_of(u8, 2 * k), t), w2(word_of(l8, 2 * k), t));
+      const uint32_t a2 = w_odd4(w2(word_of(ug, 2 * k + 1), t), w2(word_of(lg, 2 * k + 1), t));
+      const uint32_t a3 = w_odd4(w2(word_of(u8, 2 * k + 1), t), w2(word_of(l8, 2 * k + 1), t));
+      mma_s8(acc[0], a0, a1, a2, a3, F.b[k][0][0], F.b[k][0][1]);
+      mma_s8(acc[1], a0, a1, a2, a3, F.b[k][1][0], F.b[k][1][1]);
+    }
+    long long dsum[2];
+    combine_digits(acc, t, dsum);
+    const int row = rg + ((t & 1) << 3);
+    const double fs = (double)c.fine_scale[row >> 5];
+    top2_insert(best[0], (double)dsum[0] * fs, row);  // |dsum| < 2^42: exact as a double
+    top2_insert(best[1], (double)dsum[1] * fs, row);
   }
+  // lanes with equal t >> 1 hold the same two keys
 #pragma unroll
-  for (int t = 0; t < TG; ++t) {
-    const Top2 r = warp_top2(best[t]);
-    if (lane == 0) s_t[warp][t] = r;
+  for (int k = 0; k < 2; ++k) {
+    best[k] = top2_merge(best[k], shfl_top2(best[k], 1));
+    best[k] = top2_merge(best[k], shfl_top2(best[k], 4));
+    best[k] = top2_merge(best[k], shfl_top2(best[k], 8));
+    best[k] = top2_merge(best[k], shfl_top2(best[k], 16));
+  }
+  if (lane == 0 || lane == 2) {
+    s_t[warp][lane >> 1] = best[0];
+    s_t[warp][2 + (lane >> 1)] = best[1];
   }
   __syncthreads();
   if (warp == 0) {
 #pragma unroll
-    for (int t = 0; t < TG; ++t) {
-      Top2 r = lane < 8 ? s_t[lane][t] : top2_empty();
-      r = warp_top2(r);
-      if (lane == 0) {
-        const size_t o = (((size_t)cell * APPEND_MAX + (j0 + t)) * ASSIGN_SPLIT + split) * 2;
-        a.part_s[o] = r.s1;
-        a.part_s[o + 1] = r.s2;
-        a.part_i[o] = r.i1;
-        a.part_i[o + 1] = r.i2;
+    for (int r = 0; r < 4; ++r) {
+      const Top2 v = warp_top2(lane < 8 ? s_t[lane][r] : top2_empty());
+      if (lane == 0 && j0 + r < a.m) {
+        const size_t o = (((size_t)cell * APPEND_MAX + (j0 + r)) * ASSIGN_SPLIT + split) * 2;
+        a.part_s[o] = v.s1;
+        a.part_s[o + 1] = v.s2;
+        a.part_i[o] = v.i1;
+        a.part_i[o + 1] = v.i2;
       }
     }
   }
 }
 
+// Top-2 of key j over its partitions (a warp; split <= ASSIGN_SPLIT).
+__device__ __forceinline__ Top2 reduce_parts(const AssignArgs &a, int cell, int j, int lane) {
+  Top2 t = top2_empty();
+  for (int s = lane; s < a.split; s += 32) {
+    const size_t o = (((size_t)cell * APPEND_MAX + j) * ASSIGN_SPLIT + s) * 2;
+    t = top2_merge(t, Top2{a.part_s[o], a.part_s[o + 1], a.part_i[o], a.part_i[o + 1]});
+  }
+  return warp_top2(t);
+}
+
 __global__ void __launch_bounds__(1024) k_assign_reduce(AssignArgs a) {
   const int cell = a.cell0 + blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (a.guard > 0 && !append_fits(a.tlen, a.guard, a.tmax)) return;
   const int base = (a.use_tlen ? *a.tlen : 0) + a.lab_base;
   int32_t *lab = a.acells[cell].labels;
   for (int j = warp; j < a.m; j += 32) {
-    Top2 t = top2_empty();
-    if (lane < a.split) {
-      const size_t o = (((size_t)cell * APPEND_MAX + j) * ASSIGN_SPLIT + lane) * 2;
-      t = Top2{a.part_s[o], a.part_s[o + 1], a.part_i[o], a.part_i[o + 1]};
-    }
-    t = warp_top2(t);
+    const Top2 t = reduce_parts(a, cell, j, lane);
     if (lane == 0) {
       lab[2 * (size_t)(base + j)] = t.i1;
       lab[2 * (size_t)(base + j) + 1] = t.i2;
@@ -203,33 +277,30 @@ __global__ void __launch_bounds__(1024) k_assign_reduce(AssignArgs a) {
 
 // ------------------------------------------------------------------ append
 
-__global__ void __launch_bounds__(256) k_append_codec(AppendArgs a) {
-  const int j = blockIdx.x, cell = blockIdx.y, tid = threadIdx.x;
+// One CTA per cell: the new keys' lists, then the 2m postings of the tokens
+// leaving the local window sorted by (list, token), each with its mate and
+// its insertion point (the old CSR position where its list ends).
+__global__ void __launch_bounds__(1024) k_append_lists(AppendArgs a, AssignArgs s) {
+  const int cell = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (!append_fits(a.tlen, a.m, a.tmax)) return;
-  const size_t tok = (size_t)*a.tlen + j;
-  const AppendCellDev &A = a.acells[cell];
-  const uint16_t *krow = a.k + ((size_t)cell * a.m + j) * D;
-  const uint16_t *vrow = a.v + ((size_t)cell * a.m + j) * D;
-  __shared__ float s_scale[D];
-  s_scale[tid] = A.key_scale[tid];
+  const int T = *a.tlen;
+  int32_t *lab = a.acells[cell].labels;
+  for (int j = warp; j < a.m; j += 32) {
+    const Top2 t = reduce_parts(s, cell, j, lane);
+    if (lane == 0) {
+      lab[2 * (size_t)(T + j)] = t.i1;
+      lab[2 * (size_t)(T + j) + 1] = t.i2;
+    }
+  }
   __syncthreads();
-  A.kv8[tok * REC + tid] = to_e4m3(bf16f(krow[tid]));
-  A.kv8[tok * REC + 256 + tid] = to_e4m3(bf16f(vrow[tid]));
-  if (tid < 64) encode_key_quad(krow, s_scale, tid, A.prefix2 + tok * 64, A.residual2 + tok * 64, A.residual4 + tok * 128);
-}
-
-__global__ void __launch_bounds__(1024) k_post_prepare(AppendArgs a) {
-  const int cell = blockIdx.x, tid = threadIdx.x;
-  if (!append_fits(a.tlen, a.m, a.tmax)) return;
-  const int r1 = *a.tlen - a.local;  // first token leaving the local window
+  const int r1 = T - a.local;  // first token leaving the local window
   const int n = 2 * a.m;
   int np = 1;
   while (np < n) np <<= 1;
   __shared__ unsigned long long key[2 * APPEND_MAX];
-  const int32_t *lab = a.acells[cell].labels;
   for (int i = tid; i < np; i += blockDim.x) {
-    const int t = r1 + (i >> 1);
-    key[i] = i < n ? ((unsigned long long)(uint32_t)lab[2 * (size_t)t + (i & 1)] << 32) | (uint32_t)t : ~0ull;
+    const int tk = r1 + (i >> 1);
+    key[i] = i < n ? ((unsigned long long)(uint32_t)lab[2 * (size_t)tk + (i & 1)] << 32) | (uint32_t)tk : ~0ull;
   }
   __syncthreads();
   for (int k = 2; k <= np; k <<= 1)
@@ -237,51 +308,60 @@ __global__ void __launch_bounds__(1024) k_post_prepare(AppendArgs a) {
       for (int i = tid; i < np; i += blockDim.x) {
         const int ixj = i ^ jj;
         if (ixj > i) {
-          const unsigned long long x = key[i], y = key[ixj];
-          if ((x > y) == ((i & k) == 0)) {
-            key[i] = y;
-            key[ixj] = x;
+          const unsigned long long u = key[i], v = key[ixj];
+          if ((u > v) == ((i & k) == 0)) {
+            key[i] = v;
+            key[ixj] = u;
           }
         }
       }
       __syncthreads();
     }
+  const AppendCellDev &A = a.acells[cell];
+  const int32_t *off = A.offsets[A.cur];
   const size_t o = (size_t)cell * 2 * APPEND_MAX;
   for (int i = tid; i < n; i += blockDim.x) {
-    const int c = (int)(key[i] >> 32), t = (int)(uint32_t)key[i];
-    const int l0 = lab[2 * (size_t)t], l1 = lab[2 * (size_t)t + 1];
+    const int c = (int)(key[i] >> 32), tk = (int)(uint32_t)key[i];
+    const int l0 = lab[2 * (size_t)tk], l1 = lab[2 * (size_t)tk + 1];
     a.newlist[o + i] = c;
-    a.newtok[o + i] = t;
+    a.newtok[o + i] = tk;
     a.newmate[o + i] = l0 == c ? l1 : l0;
+    a.newins[o + i] = off[c + 1];
   }
 }
 
+// The next CSR set, one thread per element: old posting p moves up by the
+// new postings inserted at or before it (#{j : ins_j <= p}); new posting j
+// lands at ins_j + j; offset c grows by the new postings of lists below c.
 __global__ void __launch_bounds__(256) k_post_rebuild(AppendArgs a) {
   const int cell = blockIdx.y, tid = threadIdx.x;
   if (!append_fits(a.tlen, a.m, a.tmax)) return;
   const int n = 2 * a.m;
-  __shared__ int32_t nl[2 * APPEND_MAX];
+  __shared__ int32_t s_nl[2 * APPEND_MAX], s_ins[2 * APPEND_MAX];
   const size_t o = (size_t)cell * 2 * APPEND_MAX;
-  for (int i = tid; i < n; i += blockDim.x) nl[i] = a.newlist[o + i];
+  for (int i = tid; i < n; i += blockDim.x) {
+    s_nl[i] = a.newlist[o + i];
+    s_ins[i] = a.newins[o + i];
+  }
   __syncthreads();
   const AppendCellDev &A = a.acells[cell];
-  const int cur = A.cur;
+  const int cur = A.cur, n_old = A.n_postings;
   const int32_t *off = A.offsets[cur], *val = A.values[cur], *mat = A.mates[cur];
   int32_t *off2 = A.offsets[cur ^ 1], *val2 = A.values[cur ^ 1], *mat2 = A.mates[cur ^ 1];
-  const int c = blockIdx.x * 256 + tid;
-  if (c > a.nc) return;
-  const int s = lower_bound_i32(nl, n, c);  // new postings in lists below c
-  off2[c] = off[c] + s;
-  if (c == a.nc) return;
-  const int b = off[c], e = off[c + 1];
-  for (int p = b; p < e; ++p) {
-    val2[p + s] = val[p];
-    mat2[p + s] = mat[p];
-  }
-  const int s1 = lower_bound_i32(nl, n, c + 1);
-  for (int j = s; j < s1; ++j) {  // list c's new postings, after its old ones
-    val2[e + j] = a.newtok[o + j];
-    mat2[e + j] = a.newmate[o + j];
+  const int total = n_old + n + a.nc + 1;
+  for (int i = blockIdx.x * blockDim.x + tid; i < total; i += gridDim.x * blockDim.x) {
+    if (i < n_old) {
+      const int sft = lower_bound_i32(s_ins, n, i + 1);  // insertion points <= i
+      val2[i + sft] = val[i];
+      mat2[i + sft] = mat[i];
+    } else if (i < n_old + n) {
+      const int j = i - n_old;
+      val2[s_ins[j] + j] = a.newtok[o + j];
+      mat2[s_ins[j] + j] = a.newmate[o + j];
+    } else {
+      const int c = i - n_old - n;
+      off2[c] = off[c] + lower_bound_i32(s_nl, n, c);
+    }
   }
 }
 
@@ -311,20 +391,16 @@ __global__ void __launch_bounds__(256) k_append_commit(AppendArgs a) {
 
 cudaError_t launch_assign(const AssignArgs &a, cudaStream_t st) {
   if (a.m < 1 || a.m > APPEND_MAX || a.split < 1 || a.split > ASSIGN_SPLIT) return cudaErrorInvalidValue;
-  const int full = a.m / 4, rest = a.m % 4;
-  if (full) k_assign<4><<<dim3(a.split, a.n_cells, full), 256, 0, st>>>(a, 0);
-  if (rest) k_assign<1><<<dim3(a.split, a.n_cells, rest), 256, 0, st>>>(a, 4 * full);
+  k_assign<<<dim3(a.split, a.n_cells, (a.m + 3) / 4), 256, 0, st>>>(a, AppendArgs{}, 0);
   k_assign_reduce<<<a.n_cells, 1024, 0, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_append(const AppendArgs &a, const AssignArgs &assign, cudaStream_t st) {
-  if (a.m < 1 || a.m > APPEND_MAX) return cudaErrorInvalidValue;
-  k_append_codec<<<dim3(a.m, a.n_cells), 256, 0, st>>>(a);
-  cudaError_t e = launch_assign(assign, st);
-  if (e != cudaSuccess) return e;
-  k_post_prepare<<<a.n_cells, 1024, 0, st>>>(a);
-  k_post_rebuild<<<dim3(a.nc / 256 + 1, a.n_cells), 256, 0, st>>>(a);
+  if (a.m < 1 || a.m > APPEND_MAX || assign.split < 1 || assign.split > ASSIGN_SPLIT) return cudaErrorInvalidValue;
+  k_assign<<<dim3(assign.split, a.n_cells, (a.m + 3) / 4), 256, 0, st>>>(assign, a, 1);
+  k_append_lists<<<a.n_cells, 1024, 0, st>>>(a, assign);
+  k_post_rebuild<<<dim3(REBUILD_CTAS, a.n_cells), 256, 0, st>>>(a);
   k_append_commit<<<1, 256, 0, st>>>(a);
   return cudaGetLastError();
 }

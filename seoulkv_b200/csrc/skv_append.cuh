@@ -15,7 +15,8 @@
 namespace skv {
 
 constexpr int APPEND_MAX = 512;    // tokens per append launch sequence
-constexpr int ASSIGN_SPLIT = 32;   // centroid partitions per cell in the assignment
+constexpr int ASSIGN_SPLIT = 64;   // centroid partitions per cell in the assignment (at most)
+constexpr int REBUILD_CTAS = 64;   // CTAs per cell of the CSR rebuild
 constexpr uint32_t APPEND_FULL = 1u;       // append status: a device-side append would have passed the capacity
 constexpr uint32_t APPEND_NONFINITE = 2u;  // append status: an appended key had a non-finite element
 
@@ -34,7 +35,8 @@ struct AppendCellDev {
 // = (use_tlen ? *tlen : 0) + lab_base.  With guard > 0 nothing runs when
 // *tlen + guard > tmax (an append that does not fit).  A non-finite key
 // element counts as 0 (and raises APPEND_NONFINITE in *status, if given), so
-// every token gets two valid lists.
+// every token gets two valid lists.  `split` partitions of the centroids'
+// 16-row tiles per cell (at most ASSIGN_SPLIT).
 struct AssignArgs {
   const CellDev *cells;
   AppendCellDev *acells;
@@ -56,6 +58,7 @@ struct AppendArgs {
   const uint16_t *k, *v;
   int n_cells, m, nc, local, tmax;
   int32_t *newlist, *newtok, *newmate;  // [cell][2 * APPEND_MAX] postings entering the lists, sorted
+  int32_t *newins;                      // [cell][2 * APPEND_MAX] old CSR position each one is inserted at
 };
 
 cudaError_t launch_assign(const AssignArgs &a, cudaStream_t st);

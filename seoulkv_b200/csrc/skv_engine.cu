@@ -104,7 +104,7 @@ struct Engine {
   std::vector<int> labeled;            // per slot: the first window's lists are computed
   double *part_s = nullptr;
   int32_t *part_i = nullptr;
-  int32_t *newlist = nullptr, *newtok = nullptr, *newmate = nullptr;
+  int32_t *newlist = nullptr, *newtok = nullptr, *newmate = nullptr, *newins = nullptr;
   uint16_t *kv_stage = nullptr;        // host-input staging [2][n_cells][APPEND_MAX][256]
   bool appends() const { return tmax > desc.context; }
 };
@@ -386,6 +386,7 @@ int skv_create(const SkvDesc *d, void **handle) {
     TRY(dalloc(e, &e->newlist, C * 2 * APPEND_MAX));
     TRY(dalloc(e, &e->newtok, C * 2 * APPEND_MAX));
     TRY(dalloc(e, &e->newmate, C * 2 * APPEND_MAX));
+    TRY(dalloc(e, &e->newins, C * 2 * APPEND_MAX));
   }
   w.phase_ts = nullptr;
   w.cta_ts = nullptr;
@@ -430,7 +431,8 @@ static int refresh_cells(Engine *e) {
   return SKV_OK;
 }
 
-static int assign_split(int nc) { return std::min(ASSIGN_SPLIT, (nc + 255) / 256); }
+// Centroid partitions of the assignment: at least one 16-row tile per warp.
+static int assign_split(int nc) { return std::max(1, std::min(ASSIGN_SPLIT, (nc / 16 + 7) / 8)); }
 
 // The two lists of every token in a slot's first local window, from the
 // window's BF16 keys, once both the slot's index and its K/V are uploaded.
@@ -765,6 +767,7 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   a.newlist = e->newlist;
   a.newtok = e->newtok;
   a.newmate = e->newmate;
+  a.newins = e->newins;
   AssignArgs s{};
   s.cells = e->dcells;
   s.acells = e->dacells;

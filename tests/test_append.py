@@ -25,25 +25,41 @@ def _random_codebook(nc, seed):
     return _pack2(code >> 2), _pack2(code & 3), fs, code
 
 
-def test_assign_spill2_is_the_sequential_fp64_top2():
+def _grid_ints(vals):
+    """The decode's operand grid in exact Python integers (flush below 2^(E-22), unit 2^(E-29))."""
+    import math
+
+    nz = [abs(v) for v in vals if v != 0]
+    if not nz:
+        return [0] * len(vals)
+    E = max(math.frexp(v)[1] - 1 for v in nz)
+    out = []
+    for v in vals:
+        if v == 0 or math.frexp(abs(v))[1] - 1 < E - 22:
+            out.append(0)
+        else:
+            q = math.ldexp(v, 29 - E)
+            assert q == int(q)
+            out.append(int(q))
+    return out
+
+
+def test_assign_spill2_is_the_exact_score_top2():
     nc = 96
     upper, lower, fs, code = _random_codebook(nc, 1)
     # two equal rows in one scale group: every key ties on them
     code[40] = code[41]
     upper, lower = _pack2(code >> 2), _pack2(code & 3)
     rng = np.random.default_rng(2)
-    keys = torch.from_numpy(rng.normal(size=(5, 256)).astype(np.float32)).bfloat16()
+    keys = torch.from_numpy(rng.normal(size=(6, 256)).astype(np.float32)).bfloat16()
     keys[3] = 0  # all scores 0: the two lowest ids
+    keys[4, 7] = 2.0 ** -40  # below 2^(E-22): flushed
     kb = bits(keys)
     got = O.assign_spill2(kb, upper, lower, fs)
     for j in range(len(keys)):
-        kk = [float(x) for x in O.bf16_to_f32(kb[j])]
-        scores = []
-        for c in range(nc):
-            acc = 0.0
-            for d in range(256):
-                acc = acc + kk[d] * float(2 * int(code[c, d]) - 15)
-            scores.append(acc * float(fs[c // 32]))
+        xs = _grid_ints([float(x) for x in O.bf16_to_f32(kb[j])])
+        scores = [float(sum(xs[d] * (2 * int(code[c, d]) - 15) for d in range(256))) * float(fs[c // 32])
+                  for c in range(nc)]
         want = sorted(range(nc), key=lambda c: (-scores[c], c))[:2]
         assert list(got[j]) == want, j
     assert list(got[3]) == [0, 1]
