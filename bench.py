@@ -520,16 +520,21 @@ def run_append(args, device):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     qbits = qs.view(torch.int16)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+    torch.cuda.synchronize(device)
+    h0 = time.perf_counter()
     for i in range(args.warmup):
         flush.zero_()
         attn.append(kn[i], vn[i])
         eng.step(qbits[i].data_ptr(), True, stream.cuda_stream)
+    host_us = (time.perf_counter() - h0) / max(args.warmup, 1) * 1e6  # enqueue cost of one step
     torch.cuda.synchronize(device)
     clocks = Clocks(device.index)
     clocks.start()
     time.sleep(0.3)
     gc.disable()
-    torch.cuda._sleep(int(2e7))  # the host enqueues ahead of the device
+    # the host enqueues the whole timed loop while the device sleeps, so the
+    # events time the device alone (the host's enqueue cost is reported apart)
+    torch.cuda._sleep(int(2e7 + 1.5 * host_us * 1e-6 * args.steps * 2.0e9))
     for i in range(args.warmup, n):
         flush.zero_()
         ev[i][0].record(stream)
@@ -581,6 +586,7 @@ def run_append(args, device):
                                f"nprobe={args.nprobe}", "l2": "flushed before every step"},
         "append_us": a_mean, "append_p50_us": float(np.median(t_app)), "append_p99_us": float(np.percentile(t_app, 99)),
         "decode_us": float(np.mean(t_dec)), "decode_p50_us": float(np.median(t_dec)),
+        "host_enqueue_us_per_step": host_us,
         "append_algorithmic_bytes": app_bytes, "append_gbs": app_bytes / (a_mean * 1e-6) / 1e9,
         "append_int8_ops": int8_ops, "append_int8_tops": int8_ops / (a_mean * 1e-6) / 1e12,
         "parity": {"sampled_token_lists_equal_restatement": bool(lab_ok), "live_csr_equals_restatement": bool(csr_ok),

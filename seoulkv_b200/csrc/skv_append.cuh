@@ -15,8 +15,8 @@
 namespace skv {
 
 constexpr int APPEND_MAX = 512;    // tokens per append launch sequence
-constexpr int ASSIGN_SPLIT = 64;   // centroid partitions per cell in the assignment (at most)
-constexpr int REBUILD_CTAS = 64;   // CTAs per cell of the CSR rebuild
+constexpr int ASSIGN_SPLIT = 128;  // centroid partitions per cell in the assignment (at most)
+constexpr int REBUILD_PER_THREAD = 4;  // CSR elements per thread of the rebuild
 constexpr uint32_t APPEND_FULL = 1u;       // append status: a device-side append would have passed the capacity
 constexpr uint32_t APPEND_NONFINITE = 2u;  // append status: an appended key had a non-finite element
 
@@ -59,6 +59,9 @@ struct AppendArgs {
   int n_cells, m, nc, local, tmax;
   int32_t *newlist, *newtok, *newmate;  // [cell][2 * APPEND_MAX] postings entering the lists, sorted
   int32_t *newins;                      // [cell][2 * APPEND_MAX] old CSR position each one is inserted at
+  uint32_t *done;                       // rebuild CTAs finished (zero between appends)
+  uint32_t *assign_done;                // [cell] assignment CTAs finished (zero between appends)
+  int rebuild_ctas;                     // rebuild CTAs per cell
 };
 
 cudaError_t launch_assign(const AssignArgs &a, cudaStream_t st);

@@ -105,6 +105,9 @@ struct Engine {
   double *part_s = nullptr;
   int32_t *part_i = nullptr;
   int32_t *newlist = nullptr, *newtok = nullptr, *newmate = nullptr, *newins = nullptr;
+  uint32_t *rebuild_done = nullptr;    // CTAs of the running CSR rebuild that finished
+  uint32_t *assign_done = nullptr;     // [cell] CTAs of the running assignment that finished
+  size_t post_cap = 0;                 // postings a CSR set holds (largest over cells)
   uint16_t *kv_stage = nullptr;        // host-input staging [2][n_cells][APPEND_MAX][256]
   bool appends() const { return tmax > desc.context; }
 };
@@ -387,6 +390,8 @@ int skv_create(const SkvDesc *d, void **handle) {
     TRY(dalloc(e, &e->newtok, C * 2 * APPEND_MAX));
     TRY(dalloc(e, &e->newmate, C * 2 * APPEND_MAX));
     TRY(dalloc(e, &e->newins, C * 2 * APPEND_MAX));
+    TRY(dalloc(e, &e->rebuild_done, 1));
+    TRY(dalloc(e, &e->assign_done, C));
   }
   w.phase_ts = nullptr;
   w.cta_ts = nullptr;
@@ -431,8 +436,12 @@ static int refresh_cells(Engine *e) {
   return SKV_OK;
 }
 
-// Centroid partitions of the assignment: at least one 16-row tile per warp.
-static int assign_split(int nc) { return std::max(1, std::min(ASSIGN_SPLIT, (nc / 16 + 7) / 8)); }
+// Centroid partitions of the assignment: enough CTAs to fill the GPU (about
+// 8 per SM over all cells and key groups), at least one 16-row tile per warp.
+static int assign_split(int nc, int m, int n_cells) {
+  const int groups = (m + 3) / 4, fill = (1184 + n_cells * groups - 1) / (n_cells * groups);
+  return std::max(1, std::min({ASSIGN_SPLIT, (nc / 16 + 7) / 8, fill}));
+}
 
 // The two lists of every token in a slot's first local window, from the
 // window's BF16 keys, once both the slot's index and its K/V are uploaded.
@@ -453,7 +462,7 @@ static int label_window(Engine *e, int slot) {
     a.n_cells = G;
     a.m = std::min(APPEND_MAX, local - j0);
     a.nc = e->desc.nc;
-    a.split = assign_split(e->desc.nc);
+    a.split = assign_split(e->desc.nc, a.m, G);
     a.lab_base = T0 - local + j0;
     a.tmax = e->tmax;
     a.part_s = e->part_s;
@@ -508,6 +517,7 @@ int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells) {
     if ((rc = upload_cap(&b.values, v.values, (size_t)v.n_postings, post_cap))) return rc;
     if ((rc = upload_cap(&b.mates, v.mates, (size_t)v.n_postings, post_cap))) return rc;
     b.n_postings = v.n_postings;
+    e->post_cap = std::max(e->post_cap, post_cap);
     if (e->appends()) {
       CK(cudaMalloc(reinterpret_cast<void **>(&b.offsets2), ((size_t)nc + 1) * sizeof(int32_t)));
       CK(cudaMalloc(reinterpret_cast<void **>(&b.values2), post_cap * sizeof(int32_t)));
@@ -768,6 +778,10 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   a.newtok = e->newtok;
   a.newmate = e->newmate;
   a.newins = e->newins;
+  a.done = e->rebuild_done;
+  a.assign_done = e->assign_done;
+  a.rebuild_ctas = (int)((e->post_cap + e->desc.nc + 1 + 2 * APPEND_MAX + 256 * REBUILD_PER_THREAD - 1) /
+                         (256 * REBUILD_PER_THREAD));
   AssignArgs s{};
   s.cells = e->dcells;
   s.acells = e->dacells;
@@ -778,7 +792,7 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   s.n_cells = e->n_cells;
   s.m = n_tokens;
   s.nc = e->desc.nc;
-  s.split = assign_split(e->desc.nc);
+  s.split = assign_split(e->desc.nc, n_tokens, e->n_cells);
   s.use_tlen = 1;
   s.guard = n_tokens;
   s.tmax = e->tmax;
