@@ -695,6 +695,9 @@ def main():
     _native.FORCE_STAGED = args.staged
     if args.requests:
         run_requests(args, world, rank, device)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
         return
     if args.layers:
         run_stack(args, device)
