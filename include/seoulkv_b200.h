@@ -166,7 +166,11 @@ int skv_debug_ids(void *handle, int32_t *out);
  * SKV_STATUS_APPEND_FULL instead).  Keys are checked on the device: a
  * non-finite element counts as 0 in the assignment and raises
  * SKV_STATUS_APPEND_NONFINITE.  Both bits stay set for the engine's life
- * (skv_sync and skv_finish then fail).  A sharded engine takes no appends. */
+ * (skv_sync and skv_finish then fail).  In a connected shard group every
+ * shard calls it with the same n_tokens (each engine created with the same
+ * room to grow): the last shard, which holds the local window, appends the
+ * tokens as above; every shard's device copy of the layer's length grows by
+ * n, so the in-kernel merge and attention see the grown layer. */
 int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tokens, int32_t on_device,
                void *stream);
 /* The slots' current context, after every enqueued append (waits). */

@@ -86,6 +86,7 @@ struct Engine {
     void *opened[SHARD_MAX] = {};        // peers' regions mapped here (IPC)
     void *kv8[SHARD_MAX][SHARD_CELLS] = {};  // peers' FP8 records mapped here (IPC)
     int32_t total = 0, sink = 0, local = 0;
+    int32_t total_max = 0;               // the layer's length with every allowed append
     uint32_t *epoch = nullptr;
     int32_t *gids = nullptr;             // [4][4][100] global winners
     float *part = nullptr;               // [4][4][PART] this shard's partials
@@ -728,7 +729,10 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   Engine *e = as_engine(handle);
   if (!e || !k || !v) return fail(SKV_E_INVALID, "null engine or K/V");
   if (!e->appends()) return fail(SKV_E_STATE, "appends need an engine created with max_context above the context");
-  if (e->link.active) return fail(SKV_E_STATE, "a sequence-sharded engine does not take appends");
+  if (e->link.region && !e->link.active) return fail(SKV_E_STATE, "connect the shard group before appending");
+  // in a connected group the tokens join the last shard (it holds the local
+  // window); every shard's kernel learns the layer's new length
+  const bool linked = e->link.active, last = !linked || e->link.rank == e->link.n - 1;
   if (n_tokens < 1 || n_tokens > APPEND_MAX)
     return fail(SKV_E_INVALID, "n_tokens must be in [1, " + std::to_string(APPEND_MAX) + "]");
   int rc = ready(e);
@@ -743,13 +747,25 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   if (captured && !on_device) return fail(SKV_E_STATE, "a captured append needs device-resident K/V");
   if (!captured) {
     int32_t t = e->t_host;
-    if (e->append_captured) {  // graph replays may have appended: ask the device
+    if (e->append_captured && last) {  // graph replays may have appended: ask the device
       CK(cudaStreamSynchronize(st));
       if ((rc = sync_done(e)) || (rc = device_context(e, &t))) return rc;
     }
     if (t + n_tokens > e->tmax)
       return fail(SKV_E_CAPACITY, "append of " + std::to_string(n_tokens) + " tokens to context " +
                                       std::to_string(t) + " passes max_context " + std::to_string(e->tmax));
+  }
+  if (!last) {  // a shard before the last: only the layer's length grows
+    CK(launch_link_grow(e->link.dev, n_tokens, e->link.total_max, st));
+    e->appended = true;
+    if (captured) {
+      e->append_captured = true;
+    } else {
+      e->t_host += n_tokens;
+      CK(cudaEventRecord(e->done, st));
+      e->ran = true;
+    }
+    return SKV_OK;
   }
   const size_t rows = (size_t)e->n_cells * n_tokens * D;
   const uint16_t *dk = k, *dv = v;
@@ -800,6 +816,7 @@ int skv_append(void *handle, const uint16_t *k, const uint16_t *v, int32_t n_tok
   s.part_s = e->part_s;
   s.part_i = e->part_i;
   CK(launch_append(a, s, st));
+  if (linked) CK(launch_link_grow(e->link.dev, n_tokens, e->link.total_max, st));
   e->appended = true;
   if (captured) e->append_captured = true;
   else e->t_host += n_tokens;
@@ -1073,6 +1090,7 @@ int skv_shard_setup(void *handle, int32_t rank, int32_t n_shards, const int32_t 
   CK(cudaSetDevice(e->desc.device));
   for (int p = 0; p < n_shards; ++p) e->link.begin[p] = begin[p];
   e->link.total = total;
+  e->link.total_max = total + (e->tmax - e->desc.context);
   e->link.sink = sink;
   e->link.local = local;
   e->link.rank = rank;

@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(256) k_shard_attn(Work w, const int32_t *gids,
   const int split = blockIdx.x, cell = blockIdx.y, slot = cell >> 2, g = cell & 3;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const CellDev &c = w.cells[cell];
-  const int sink = w.sink, local = w.local, T = w.T, dense = sink + local;
+  const int sink = w.sink, local = w.local, T = context_of(w), dense = sink + local;
   const int nitems = dense + G * TOPK;
   const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
   __shared__ float s_m[G][8], s_l[G][8];
@@ -341,6 +341,18 @@ cudaError_t launch_shard_p2p_step(const Work &w, const ShardLinkDev &L, int32_t 
   k_shard_merge_p2p<<<SHARD_CELLS * G, MERGE_THREADS, 0, st>>>(L, w.final_keys, w.final_ids, gids, status);
   k_shard_attn<<<dim3(ATTN_SPLIT, SHARD_CELLS), 256, 0, st>>>(w, gids, L.token_begin, part);
   k_shard_combine_p2p<<<SHARD_CELLS, 256, 0, st>>>(L, part, w.out, status);
+  return cudaGetLastError();
+}
+
+// The layer grows by m tokens (they joined the last shard): every shard's
+// kernel reads the layer's length from its device copy of the group.  An
+// append past the group's capacity is skipped, as the last shard skips it.
+__global__ void k_link_grow(ShardLinkDev *L, int m, int total_max) {
+  if (L->total + m <= total_max) L->total += m;
+}
+
+cudaError_t launch_link_grow(ShardLinkDev *dlink, int m, int total_max, cudaStream_t st) {
+  k_link_grow<<<1, 1, 0, st>>>(dlink, m, total_max);
   return cudaGetLastError();
 }
 

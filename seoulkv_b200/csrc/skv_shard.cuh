@@ -23,6 +23,7 @@ size_t shard_region_bytes();
 // the partials) and the epoch bump, on `st`, for a connected group.
 // Bumps the group's step counter (after a step's exchanges).
 cudaError_t launch_shard_epoch(const ShardLinkDev *dlink, cudaStream_t st);
+cudaError_t launch_link_grow(ShardLinkDev *dlink, int m, int total_max, cudaStream_t st);
 cudaError_t launch_shard_p2p_step(const Work &w, const ShardLinkDev &L, int32_t *gids, float *part,
                                   int32_t *status, cudaStream_t st);
 

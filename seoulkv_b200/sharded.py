@@ -30,12 +30,13 @@ and partials between GPUs:
 
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 
 import torch
 
 from . import _native
-from .api import SeoulKV4
+from .api import SeoulKV4, _check_append, _enqueue_append
 from .config import SeoulKV4Config
 
 PART = 260  # floats per (cell, head) partial: m, l, 0, 0, o[256]
@@ -126,11 +127,16 @@ class ShardedSeoulKV4:
     """
 
     def __init__(self, *, device, k, v, index, plan: ShardPlan, config: SeoulKV4Config | None = None,
-                 group=None, transport: str | None = None):
+                 group=None, transport: str | None = None, grow: int = 0):
         zones = index.zones
         if (zones.context, zones.sink, zones.local) != (plan.context, plan.shard_sink, plan.shard_local):
             raise ValueError("index zones do not match the shard plan")
+        if type(grow) is not int or grow < 0:
+            raise ValueError("grow must be a non-negative token count")
+        if grow:  # every shard's engine gets the same room (the last one uses it)
+            config = dataclasses.replace(config or SeoulKV4Config(), max_context=plan.context + grow)
         self.plan = plan
+        self.grow, self.appended = grow, 0
         self.exchange = Exchange(group)
         if self.exchange.size != plan.n_shards or self.exchange.rank != plan.shard:
             raise ValueError("the process group must hold one rank per shard, rank r = shard r")
@@ -188,6 +194,27 @@ class ShardedSeoulKV4:
         self.exchange.gather(self.part_all, self.part)
         _native.shard_combine(self.part_all.data_ptr(), n, 4, self.out.data_ptr(), st)
         return self.out.view(torch.bfloat16).reshape(1, 1, 16, 256)
+
+    @property
+    def total(self) -> int:
+        """Tokens in the layer: the plan's total plus every appended token."""
+        return self.plan.total + self.appended
+
+    def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Grow the layer by m tokens: BF16 K and V [4, m, 256] (host or CUDA),
+        the same on every rank, which all call this.  The tokens join the last
+        shard (it holds the local window, whose oldest tokens enter its
+        retrieval zone); with the peer-memory transport every shard's kernel
+        learns the layer's new length on the device.  Needs ``grow`` room."""
+        m = _check_append(k, v, (4,), 0, 1 << 30)
+        if self.appended + m > self.grow:
+            raise ValueError(f"append of {m} tokens passes the layer's room to grow ({self.grow - self.appended} "
+                             "tokens left; set ShardedSeoulKV4(grow=...))")
+        if self.plan.shard == self.plan.n_shards - 1:
+            self.attn.append(k, v)
+        elif self.transport == "p2p":
+            _enqueue_append(self.attn._engine, k, v, self.device.index, self._stream())
+        self.appended += m
 
     def selected_ids(self) -> torch.Tensor:
         """Global token ids of the last step: CUDA int32 [4, 4, 100] (KV head, query head, rank; -1 past the end)."""

@@ -130,9 +130,13 @@ class AppendCase:
     """A cache built on its first ``context`` tokens and grown by appends up to
     ``total`` tokens, with the oracle's view of every intermediate context."""
 
-    def __init__(self, context=8192, total=8192 + 700, nprobe=128, seed=23, components=256, sink=128, local=256):
+    def __init__(self, context=8192, total=8192 + 700, nprobe=128, seed=23, components=256, sink=128, local=256,
+                 kv=None):
         self.context, self.total, self.sink, self.local = context, total, sink, local
-        self.k_full, self.v_full, self.mixes = synthetic.make_kv(total, seed=seed, components=components)
+        if kv is None:
+            kv = synthetic.make_kv(total, seed=seed, components=components)
+        self.k_full, self.v_full, self.mixes = kv
+        assert self.k_full.shape[1] == total
         self.k = self.k_full[:, :context].contiguous()
         self.v = self.v_full[:, :context].contiguous()
         self.index = SeoulKV4Index.build(self.k, self.v, sink=sink, local=local, nprobe=nprobe)
@@ -176,6 +180,12 @@ class AppendCase:
             self._k8 = O.fp8_e4m3(self.k_full.float().numpy())
             self._v8 = O.fp8_e4m3(self.v_full.float().numpy())
         return self._k8, self._v8
+
+    def reference_view(self, t, begin):
+        """This cache at context t as shard [begin, begin + t) of a sharded layer (oracle view)."""
+        k8, v8 = self.kv8()
+        return dict(cells=self.cells(t), begin=begin, context=t, sink=self.sink, local=self.local,
+                    k8=k8[:, :t], v8=v8[:, :t])
 
     def oracle(self, q, t, capacity=13056):
         qb = bits(q).reshape(16, 256)
