@@ -110,6 +110,8 @@ __device__ __forceinline__ int lower_bound_i32(const int32_t *a, int n, int x) {
   return lo;
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ void load_plane_row(const uint8_t *base, int row, uint4 (&r)[4]) {
   const uint4 *p = reinterpret_cast<const uint4 *>(base + (size_t)row * 64);
 #pragma unroll
@@ -288,6 +290,12 @@ __global__ void __launch_bounds__(256) k_assign(AssignArgs a, AppendArgs app, in
   const int tiles = a.nc >> 4;
   for (int tile = split * 8 + warp; tile < tiles; tile += a.split * 8) {
     const int rg = tile * 16 + g;
+    const int nxt = tile + a.split * 8;
+    if (nxt < tiles && t < 2) {  // the next tile's rows into L2 while this one computes
+      const int rn = nxt * 16 + g + 8 * t;
+      prefetch_l2(upper + (size_t)rn * 64);
+      prefetch_l2(lower + (size_t)rn * 64);
+    }
     uint4 ug[4], lg[4], u8[4], l8[4];
     load_plane_row(upper, rg, ug);
     load_plane_row(lower, rg, lg);

@@ -437,10 +437,11 @@ static int refresh_cells(Engine *e) {
   return SKV_OK;
 }
 
-// Centroid partitions of the assignment: enough CTAs to fill the GPU (about
-// 8 per SM over all cells and key groups), at least one 16-row tile per warp.
+// Centroid partitions of the assignment: one resident wave (2 CTAs per SM)
+// over all cells and key groups, but at least 16 (many key groups), and at
+// least one 16-row tile per warp.
 static int assign_split(int nc, int m, int n_cells) {
-  const int groups = (m + 3) / 4, fill = (1184 + n_cells * groups - 1) / (n_cells * groups);
+  const int groups = (m + 3) / 4, fill = std::max(16, (296 + n_cells * groups - 1) / (n_cells * groups));
   return std::max(1, std::min({ASSIGN_SPLIT, (nc / 16 + 7) / 8, fill}));
 }
 
