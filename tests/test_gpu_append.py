@@ -186,3 +186,29 @@ def test_append_nonfinite_key_counts_as_zero(ac, cuda):
             view = ac.views[g]
             want = O.assign_spill2(bits(k[g]), view["upper"], view["lower"], view["fine_scale"])[0]
             assert list(lab[g, ac.context]) == list(want), g
+
+
+def test_append_with_large_zones_and_per_head_nprobe(cuda):
+    """Sink 512 and an 8192-token local window (its lists assigned at upload
+    in 16 chunks of 512) with per-head nprobe overrides: after an append of
+    600 tokens the CSR, every token's lists and the decode equal the oracle's."""
+    ac = AppendCase(context=16384, total=16384 + 600, nprobe=128, seed=29, sink=512, local=8192)
+    probes = (128, 192, 160, 256)
+    cfg = SeoulKV4Config(debug=True, max_context=ac.total, nprobe=probes)
+    with SeoulKV4(device=cuda, k=ac.k, v=ac.v, index=ac.index, config=cfg) as attn:
+        attn.append(*ac.appended(ac.context, ac.total))
+        t = ac.total
+        _check_csr(ac, attn._engine, t)
+        _check_labels(ac, attn._engine, t)
+        q = ac.query(t, seed=4)
+        qb = bits(q).reshape(16, 256)
+        res = [O.run_cell(c, qb[4 * g:4 * g + 4]) for g, c in enumerate(ac.cells(t, nprobe=probes))]
+        out = attn.run(q).to_torch()
+        ids = attn.debug_snapshot()["selected_ids"].numpy()
+        k8, v8 = ac.kv8()
+        want = np.zeros((16, 256), np.uint16)
+        for j in range(16):
+            g, h = divmod(j, 4)
+            assert np.array_equal(ids[g, h], res[g]["final_ids"][h]), (g, h)
+            want[j] = O.attention(qb[j], k8[g], v8[g], O.attention_keys(t, ac.sink, ac.local, res[g]["final_ids"][h]))
+        _check_out(bits(out).reshape(16, 256), want)
