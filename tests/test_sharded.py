@@ -99,3 +99,17 @@ def test_two_gloo_ranks_agree_with_one_process(tmp_path):
     want = O.merge_shards(keys, ids, [sh["begin"] for sh in shards])
     assert np.array_equal(got[0], want)
     assert (want >= 0).all() and want.max() < total
+
+
+def test_sharded_grow_validation():
+    """ShardedSeoulKV4 rejects a bad growth allowance and mismatched zones
+    before it touches a device."""
+    from seoulkv_b200.sharded import ShardedSeoulKV4
+
+    plan = ShardPlan(8192, 1, 0)
+    case = ShardCase(plan)
+    for bad in (-1, 1.5, True):
+        with pytest.raises(ValueError, match="grow"):
+            ShardedSeoulKV4(device="cuda:0", k=case.k, v=case.v, index=case.index, plan=plan, grow=bad)
+    with pytest.raises(ValueError, match="zones"):
+        ShardedSeoulKV4(device="cuda:0", k=case.k, v=case.v, index=case.index, plan=ShardPlan(8192, 1, 0, local=128))
