@@ -143,9 +143,9 @@ int skv_output(void *handle, void *out, int32_t to_host);
  * query head, rank).  Synchronises. */
 int skv_debug_ids(void *handle, int32_t *out);
 
-/* Cache append (no counterpart in the reference, whose cache is static:
- * README.md "out of scope"; see the build path it would extend,
- * _index_build.py:22-59 and _codecs/keys.py:16-44).  Appends n_tokens
+/* Cache append (no counterpart in the reference, whose cache is static: its
+ * README.md:68-69 lists appends as out of scope; the build path this extends
+ * is src/seoulkv4/_index_build.py:22-59 and _codecs/keys.py:16-44).  Appends n_tokens
  * tokens to every slot: k and v are BF16 [n_slots][4][n_tokens][256]
  * (host memory, or device memory with on_device != 0).  Each new token gets
  * its key planes (with the build's per-dimension scales, codes clamped to
