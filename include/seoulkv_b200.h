@@ -310,7 +310,8 @@ int skv_shard_gids(void *handle, const int32_t **gids);
  *        [context][512] = K (256 B) | V (256 B) of one KV head
  *   ids  device int32 [n_slots][4][4][100] selected token ids (KV head,
  *        query head, rank); ids outside [0, context) are skipped
- *   out  device BF16 [n_slots][16][256]
+ *   out  device BF16 [n_slots][16][256]; a query head left with no key at
+ *        all (sink = local = 0 and every one of its ids skipped) gets zeros
  * Scratch is a fixed file-scope device array sized for SKV_NOALLOC_MAX_SLOTS
  * slots (about 1 MiB, held by every GPU that loads the library until the
  * process exits); larger n_slots is rejected with SKV_E_INVALID.  The first

@@ -52,7 +52,7 @@ def build(force: bool = False) -> Path:
     src = HERE / "skv_oracle.c"
     if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
         subprocess.check_call(
-            ["gcc", "-O2", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
+            ["gcc", "-O2", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math", "-fopenmp",
              "-std=c11", "-o", str(LIB_PATH), str(src), "-lm"]
         )
     return LIB_PATH
@@ -92,7 +92,14 @@ def lib():
         for name in ("skv_oracle_coarse", "skv_oracle_fine", "skv_oracle_pool",
                      "skv_oracle_stage15", "skv_oracle_stage16"):
             getattr(_lib, name).restype = ctypes.c_int
+        _lib.skv_oracle_set_threads.argtypes = [ctypes.c_int]
     return _lib
+
+
+def set_threads(n: int) -> None:
+    """Host threads of each cell's scoring loops (default 1; results do not
+    depend on it)."""
+    lib().skv_oracle_set_threads(int(n))
 
 
 def _ptr(a: np.ndarray) -> ctypes.c_void_p:

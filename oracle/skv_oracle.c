@@ -49,6 +49,12 @@
 #define D 256
 #define G 4
 
+/* Host threads of the per-centroid / per-token scoring loops (1 unless
+ * skv_oracle_set_threads raises it).  Each iteration writes only its own
+ * outputs, so results do not depend on the thread count. */
+static int g_threads = 1;
+void skv_oracle_set_threads(int n) { g_threads = n > 0 ? n : 1; }
+
 /* ------------------------------------------------------------------ bits */
 
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -186,8 +192,9 @@ static inline uint64_t rank_key(uint16_t score, int32_t pos) {
 int skv_oracle_coarse(const OracleCell *c, const OracleQuery *q, uint16_t *lo /* [4][nc] */,
                       uint16_t *hi, uint16_t *thresh /* [4] */, uint32_t *tags /* [nc] */) {
     const int nc = c->nc;
-    int32_t w[D];
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
     for (int i = 0; i < nc; ++i) {
+        int32_t w[D];
         const uint8_t *row = c->upper + (size_t)i * 64;
         for (int d = 0; d < D; ++d) w[d] = (row[d >> 2] >> (2 * (d & 3))) & 3;
         const float sc4 = c->coarse_scale4[i >> 5];
@@ -202,13 +209,15 @@ int skv_oracle_coarse(const OracleCell *c, const OracleQuery *q, uint16_t *lo /*
             hi[h * nc + i] = skv_oracle_bf16_rne(v + margin);
         }
     }
-    KeyIdx *items = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)nc);
+    KeyIdx *items_all = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)nc * G);
+#pragma omp parallel for schedule(static) num_threads(g_threads < G ? g_threads : G) if (g_threads > 1)
     for (int h = 0; h < G; ++h) {
+        KeyIdx *items = items_all + (size_t)h * nc;
         for (int i = 0; i < nc; ++i) { items[i].key = ord16(lo[h * nc + i]); items[i].idx = i; }
         qsort(items, (size_t)nc, sizeof(KeyIdx), by_key_desc);
         thresh[h] = lo[h * nc + items[c->nprobe - 1].idx];
     }
-    free(items);
+    free(items_all);
     int n = 0;
     for (int i = 0; i < nc; ++i) {
         uint32_t mask = 0;
@@ -227,9 +236,10 @@ int skv_oracle_coarse(const OracleCell *c, const OracleQuery *q, uint16_t *lo /*
  * survivors. */
 int skv_oracle_fine(const OracleCell *c, const OracleQuery *q, const uint32_t *tags, int ntags,
                     uint16_t *scores, int32_t *top, int32_t *selected) {
-    int32_t w[D];
     const int P = c->nprobe;
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
     for (int i = 0; i < ntags; ++i) {
+        int32_t w[D];
         const uint32_t cid = tags[i] & 0x0fffffffu, mask = tags[i] >> 28;
         const uint8_t *up = c->upper + (size_t)cid * 64, *lw = c->lower + (size_t)cid * 64;
         for (int d = 0; d < D; ++d) {
@@ -299,24 +309,28 @@ static inline int r4_at(const uint8_t *row, int d) { return (row[d >> 1] >> (4 *
  * positions ascending.  Returns |u15|. */
 int skv_oracle_stage15(const OracleCell *c, const OracleQuery *q, const int32_t *pool, int npool,
                        int m, uint16_t *scores, int32_t *top, int32_t *u15) {
-    int32_t w[D];
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
     for (int i = 0; i < npool; ++i) {
+        int32_t w[D];
         const uint8_t *row = c->prefix2 + (size_t)pool[i] * 64;
         for (int d = 0; d < D; ++d) w[d] = 2 * p2_at(row, d) - 3;
         for (int h = 0; h < G; ++h)
             scores[h * npool + i] = skv_oracle_bf16_rne(exact_dot(q->xb[h], q->sb[h], w));
     }
     const int k = m < npool ? m : npool;
-    KeyIdx *items = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)npool);
-    uint8_t *chosen = (uint8_t *)calloc((size_t)npool, 1);
+    KeyIdx *items_all = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)npool * G);
+#pragma omp parallel for schedule(static) num_threads(g_threads < G ? g_threads : G) if (g_threads > 1)
     for (int h = 0; h < G; ++h) {
+        KeyIdx *items = items_all + (size_t)h * npool;
         for (int i = 0; i < npool; ++i) { items[i].key = rank_key(scores[h * npool + i], i); items[i].idx = i; }
         top_k(items, npool, k, top + h * m);
-        for (int j = 0; j < k; ++j) chosen[top[h * m + j]] = 1;
     }
+    uint8_t *chosen = (uint8_t *)calloc((size_t)npool, 1);
+    for (int h = 0; h < G; ++h)
+        for (int j = 0; j < k; ++j) chosen[top[h * m + j]] = 1;
     int n = 0;
     for (int i = 0; i < npool; ++i) if (chosen[i]) u15[n++] = i;
-    free(items);
+    free(items_all);
     free(chosen);
     return n;
 }
@@ -328,8 +342,9 @@ int skv_oracle_stage15(const OracleCell *c, const OracleQuery *q, const int32_t 
 int skv_oracle_stage16(const OracleCell *c, const OracleQuery *q, const int32_t *pool,
                        const int32_t *u15, int nu, int m, uint16_t *scores, int32_t *top,
                        int32_t *cand) {
-    int32_t w[D];
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
     for (int u = 0; u < nu; ++u) {
+        int32_t w[D];
         const int t = pool[u15[u]];
         const uint8_t *p = c->prefix2 + (size_t)t * 64, *r = c->residual2 + (size_t)t * 64;
         for (int d = 0; d < D; ++d) w[d] = 2 * ((p2_at(p, d) << 2) | p2_at(r, d)) - 15;
@@ -337,16 +352,19 @@ int skv_oracle_stage16(const OracleCell *c, const OracleQuery *q, const int32_t 
             scores[h * nu + u] = skv_oracle_bf16_rne(exact_dot(q->xd[h], q->sd[h] + 4, w));
     }
     const int k = m < nu ? m : nu;
-    KeyIdx *items = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)nu);
-    uint8_t *chosen = (uint8_t *)calloc((size_t)nu, 1);
+    KeyIdx *items_all = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)(nu > 0 ? nu : 1) * G);
+#pragma omp parallel for schedule(static) num_threads(g_threads < G ? g_threads : G) if (g_threads > 1)
     for (int h = 0; h < G; ++h) {
+        KeyIdx *items = items_all + (size_t)h * nu;
         for (int u = 0; u < nu; ++u) { items[u].key = rank_key(scores[h * nu + u], u); items[u].idx = u; }
         top_k(items, nu, k, top + h * m);
-        for (int j = 0; j < k; ++j) chosen[top[h * m + j]] = 1;
     }
+    uint8_t *chosen = (uint8_t *)calloc((size_t)(nu > 0 ? nu : 1), 1);
+    for (int h = 0; h < G; ++h)
+        for (int j = 0; j < k; ++j) chosen[top[h * m + j]] = 1;
     int n = 0;
     for (int u = 0; u < nu; ++u) if (chosen[u]) cand[n++] = u;
-    free(items);
+    free(items_all);
     free(chosen);
     return n;
 }
@@ -358,8 +376,9 @@ int skv_oracle_stage16(const OracleCell *c, const OracleQuery *q, const int32_t 
 void skv_oracle_stage2(const OracleCell *c, const OracleQuery *q, const int32_t *pool,
                        const int32_t *u15, const int32_t *cand, int ncand, int k,
                        uint16_t *scores, int32_t *final_pos, int32_t *final_ids) {
-    int32_t w[D];
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
     for (int j = 0; j < ncand; ++j) {
+        int32_t w[D];
         const int t = pool[u15[cand[j]]];
         const uint8_t *p = c->prefix2 + (size_t)t * 64, *r = c->residual2 + (size_t)t * 64,
                       *r4 = c->residual4 + (size_t)t * 128;

@@ -184,7 +184,9 @@ __global__ void __launch_bounds__(256) k_attn_noalloc(const uint16_t *q, KvPtrs 
       L += s_part[sp][1] * e;
       O += s_part[sp][4 + tid] * e;
     }
-    out[((size_t)slot * 16 + g * 4 + h) * D + tid] = bf16_rne(O / L);
+    // a head with no key to attend (no dense zones and no selected id inside
+    // the context) gets zeros rather than 0/0
+    out[((size_t)slot * 16 + g * 4 + h) * D + tid] = L > 0.0f ? bf16_rne(O / L) : (uint16_t)0;
     __syncthreads();
   }
   if (tid == 0) arrive[cell] = 0;

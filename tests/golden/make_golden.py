@@ -38,7 +38,9 @@ import torch
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-REF = os.environ.get("SEOULKV_REFERENCE", "/root/reference/src")
+REF = os.environ.get("SEOULKV_REFERENCE")
+if not REF:
+    sys.exit("set SEOULKV_REFERENCE to the reference's source directory (the one holding seoulkv4/)")
 sys.path.insert(0, REF)
 
 from oracle import oracle as O  # noqa: E402

@@ -10,8 +10,9 @@ import torch
 from seoulkv_b200 import SeoulKV4Index, _codecs
 from tests.helpers import Case
 
-REF = os.environ.get("SEOULKV_REFERENCE", "/root/reference/src")
-HAVE_REF = os.path.isdir(os.path.join(REF, "seoulkv4"))
+# the reference's source directory (holding seoulkv4/), only from the environment
+REF = os.environ.get("SEOULKV_REFERENCE", "")
+HAVE_REF = bool(REF) and os.path.isdir(os.path.join(REF, "seoulkv4"))
 
 
 @pytest.fixture(scope="module")
