@@ -166,7 +166,9 @@ def headline_config(args) -> dict:
     """The config dict of the single-layer line (both arms print this one)."""
     return {"workload": "1 layer, 1 query token, T=131072, 4 KV / 16 Q heads, d=256, nprobe=384, "
                         "sink=128, local=256, top-100",
-            "context": args.context, "nprobe": args.nprobe, "l2": "flushed before every step",
+            "context": args.context, "nprobe": args.nprobe,
+            "l2": "flushed (256 MiB write) before every step; the layer's centroid planes sit in the persisting "
+                  "L2 set-aside (access-policy window), which the flush does not evict",
             "parallelism": "1 GPU"}
 
 
@@ -842,6 +844,17 @@ def main():
     eng.sync()  # status check of the last step
     value = total_us / (world * args.steps)
 
+    # the same kind of steps without the L2 window (centroid planes read from
+    # HBM after every flush), for comparison; the window is restored after
+    window_bytes = int(getattr(eng, "l2_resident_bytes", 0))
+    no_window = None
+    if window_bytes:
+        eng.set_l2_residency(False)
+        t_nw = _timed_steps(argparse.Namespace(warmup=args.warmup, steps=min(args.steps, 200)), device, flush, step)
+        eng.set_l2_residency(True)
+        no_window = {"mean_us": float(np.mean(t_nw)), "p50_us": float(np.median(t_nw)),
+                     "p99_us": float(np.percentile(t_nw, 99)), "steps": int(len(t_nw))}
+
     # per-kernel device times (non-graph launches, L2 flushed before each)
     prof = {}
     for _ in range(5):
@@ -867,7 +880,17 @@ def main():
     roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
             "traffic": None, "algorithmic_bytes": dom_bytes, "kernel_us": prof[dom],
-            "timing": "CUDA events around one non-graph launch, L2 flushed"}
+            "timing": "CUDA events around one non-graph launch, L2 flushed (normal lines)"}
+    if window_bytes and dom == "k_funnel":
+        # bytes the window serves from persisting L2: the coarse scan's upper
+        # plane (nc x 64 per cell) and the Fine rows of the survivors (128 of
+        # the 132 bytes charged per survivor)
+        nc = index.cells()[0]["centroids"].shape[0]
+        resident = 4 * nc * 64 + traffic["fine"] * 128.0 / 132.0
+        roof.update(l2_window_bytes=window_bytes, l2_resident_algorithmic_bytes=resident,
+                    hbm_algorithmic_bytes=dom_bytes - resident,
+                    hbm_achieved=(dom_bytes - resident) / (prof[dom] * 1e-6) / 1e9,
+                    hbm_frac=(dom_bytes - resident) / (prof[dom] * 1e-6) / 1e9 / peak)
     ncu_note = ROOT / "profiles" / "traffic_128k.json"
     if ncu_note.exists():
         try:
@@ -941,6 +964,10 @@ def main():
             "p50_us": float(np.percentile(per, 50)), "p99_us": float(np.percentile(per, 99)),
             "tokens_per_s": 1e6 / value,
             "roofline": roof, "kernel_us": prof, "phase_us": phases, "algorithmic_bytes_per_step": traffic,
+            "l2_window": {"resident_bytes": window_bytes,
+                          "what": "upper+lower centroid planes of the layer held in persisting L2 by an "
+                                  "access-policy window (the flush evicts normal lines only)",
+                          "without_window": no_window},
             "live_counts": {"survivors_max": st.survivors_max, "pool_min": st.pool_min, "pool_max": st.pool_max,
                             "union15_max": st.union15_max, "union16_max": st.union16_max},
             "parity": parity, "cpu_baseline": cpu_line, "e2e": e2e, "clocks": clk,

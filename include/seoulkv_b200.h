@@ -121,6 +121,22 @@ int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *str
  * be device-resident (SKV_E_STATE otherwise). */
 int skv_run(void *handle, void *stream);
 
+/* Keep the centroid planes (upper and lower, nc * 128 bytes per cell, all
+ * cells in one arena) resident in L2 across steps: the counterpart of the
+ * reference uploading its coarse centroid plane into on-chip SRAM
+ * (_upload(..., dram=False) in
+ * src/seoulkv4/_kernels/stage1_coarse/seoulkv4_coarse_score.py:120,195).
+ * enable != 0 puts an access-policy window (hits persisting) over the arena
+ * on the fused funnel's launch and raises this process's persisting-L2
+ * set-aside by the arena's size; enable == 0 removes the window and, when no
+ * engine of the process holds one any more, restores the set-aside the
+ * process had.  The set-aside is state of the calling process's CUDA
+ * context (it ends with the process).  *resident_bytes (if not NULL) gets
+ * the bytes now held resident: 0 on the staged path, or when the device's
+ * largest window or set-aside cannot hold the arena (then nothing changes).
+ * Waits for the engine's work; the step graphs are captured again. */
+int skv_set_l2_residency(void *handle, int32_t enable, size_t *resident_bytes);
+
 /* skv_bind_query + skv_run in one call (one host crossing per step). */
 int skv_step(void *handle, const uint16_t *q, int32_t on_device, void *stream);
 

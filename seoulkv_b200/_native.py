@@ -32,7 +32,7 @@ EXPORTS = (
     "skv_kernels_per_step", "skv_step_kernel_name", "skv_profile_phases", "skv_phase_name", "skv_profile_ctas", "skv_step", "skv_finish",
     "skv_shard_outputs", "skv_shard_merge", "skv_shard_attention", "skv_shard_combine",
     "skv_shard_setup", "skv_shard_connect", "skv_shard_ipc_handle_bytes", "skv_shard_gids",
-    "skv_append", "skv_context",
+    "skv_append", "skv_context", "skv_set_l2_residency",
 )
 
 SKV_FLAG_STAGED = 1
@@ -142,6 +142,7 @@ def load() -> ctypes.CDLL:
         lib.skv_append.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                    ctypes.c_int32, ctypes.c_void_p]
         lib.skv_context.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
+        lib.skv_set_l2_residency.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]
         _lib = lib
         return lib
 
@@ -288,6 +289,14 @@ class Engine:
         check(self.lib.skv_profile_step(self.handle, ctypes.c_void_p(stream or None), _ptr(ms), 64,
                                         ctypes.byref(n)), "skv_profile_step")
         return [(self.lib.skv_step_kernel_name(self.handle, i).decode(), float(ms[i])) for i in range(n.value)]
+
+    def set_l2_residency(self, enable: bool) -> int:
+        """Hold the centroid planes in the persisting part of L2 (or stop);
+        returns the bytes now resident (0: off, or they do not fit)."""
+        n = ctypes.c_size_t()
+        check(self.lib.skv_set_l2_residency(self.handle, int(bool(enable)), ctypes.byref(n)), "skv_set_l2_residency")
+        self.l2_resident_bytes = int(n.value)
+        return self.l2_resident_bytes
 
     def kernels_per_step(self) -> int:
         """Kernels one step of this engine launches (1 on the fused path)."""

@@ -158,6 +158,7 @@ class SeoulKV4:
             else:
                 kb, vb = _bits(k), _bits(v)
                 eng.upload_kv(0, kb.data_ptr(), vb.data_ptr(), False)
+            eng.set_l2_residency(self._config.l2_resident)
         except Exception:
             eng.close()
             raise
@@ -270,6 +271,7 @@ class SeoulKV4:
                 device_path="fused cluster kernel" if self._engine.fused else "staged kernels",
                 stage15_capacity=self._config.stage15_capacity,
                 graph_replay=True,
+                l2_resident_bytes=getattr(self._engine, "l2_resident_bytes", 0),
             )
         return meta
 

@@ -133,6 +133,7 @@ class SeoulKV4Batch:
                 else:
                     kb, vb = _bits(k), _bits(v)
                 eng.upload_kv(s, kb.data_ptr(), vb.data_ptr(), on_dev)
+            eng.set_l2_residency(self._config.l2_resident)
         except Exception:
             eng.close()
             raise

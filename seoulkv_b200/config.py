@@ -45,12 +45,17 @@ class SeoulKV4Config:
     instance without rebuilding the index.  ``max_context`` (None = the
     index's context: a static cache, as in the reference) is the context the
     cache may grow to by ``append``; device buffers are sized for it.
+    ``l2_resident`` keeps the index's centroid planes in the persisting part
+    of L2 across steps (the reference keeps its coarse centroid plane in
+    on-chip SRAM); it applies where the device's persisting set-aside can hold
+    them, and is a no-op otherwise.
     """
 
     stage15_capacity: int = 13056
     debug: bool = False
     nprobe: int | tuple[int, ...] | None = None
     max_context: int | None = None
+    l2_resident: bool = True
 
     def __post_init__(self):
         n = self.stage15_capacity
@@ -58,6 +63,8 @@ class SeoulKV4Config:
             raise ValueError("stage15_capacity must be a multiple of 768 in [12288, 24576]")
         if type(self.debug) is not bool:
             raise TypeError("debug must be a bool")
+        if type(self.l2_resident) is not bool:
+            raise TypeError("l2_resident must be a bool")
         if self.nprobe is not None:
             validate_nprobe(self.nprobe if type(self.nprobe) is int else tuple(self.nprobe), 512)
             if not isinstance(self.nprobe, int):

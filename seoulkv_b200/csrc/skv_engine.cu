@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -75,6 +76,13 @@ struct Engine {
   bool q_host = false;   // the bound query is in q_pinned
   bool host_io = false;  // the last launch was a host-I/O step (its output and counters are in pinned memory)
   bool fused = false;             // one cluster kernel per step (else the staged kernels)
+  // the centroid planes of every cell in one arena: cell c's upper plane at
+  // c * nc * 128, its lower plane right after it (what an L2 access-policy
+  // window covers, skv_set_l2_residency)
+  uint8_t *planes = nullptr;
+  size_t planes_bytes = 0;
+  cudaAccessPolicyWindow l2win{};  // num_bytes 0: no window
+  bool l2_resident = false;
   long long *phase_ts = nullptr;  // fused phase timestamps (skv_profile_phases)
   long long *cta_ts = nullptr;    // per-CTA entry/exit times (skv_profile_ctas)
   // sequence-sharded group over peer memory (skv_shard_setup / skv_shard_connect)
@@ -131,10 +139,66 @@ ShardLinkDev link_view(const Engine *e) {
   return L;
 }
 
+// The access-policy window the fused launches carry (null: none).
+const cudaAccessPolicyWindow *window_of(const Engine *e) {
+  return e->l2_resident && e->l2win.num_bytes ? &e->l2win : nullptr;
+}
+
+// Engines of this process holding an L2 window, per device: how many, the
+// plane bytes they hold, and the persisting set-aside the process had before
+// the first of them raised it (restored when the last one lets go).  The
+// set-aside is state of this process's CUDA context: it ends with the process
+// and changes no setting of the GPU.
+std::mutex g_l2_lock;
+constexpr int kL2Devices = 64;
+int g_l2_users[kL2Devices] = {};
+size_t g_l2_bytes[kL2Devices] = {};
+size_t g_l2_prev[kL2Devices] = {};
+
+void l2_release(Engine *e) {
+  std::lock_guard<std::mutex> lock(g_l2_lock);
+  const int dev = e->desc.device;
+  const size_t bytes = e->l2win.num_bytes;
+  e->l2_resident = false;
+  e->l2win = cudaAccessPolicyWindow{};
+  if (dev < 0 || dev >= kL2Devices || g_l2_users[dev] == 0) return;
+  --g_l2_users[dev];
+  g_l2_bytes[dev] -= std::min(bytes, g_l2_bytes[dev]);
+  cudaCtxResetPersistingL2Cache();  // lines marked persisting become normal (others re-mark on access)
+  cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g_l2_users[dev] ? g_l2_bytes[dev] : g_l2_prev[dev]);
+}
+
+// Hold the engine's centroid planes in the persisting part of L2; false when
+// the device offers no window or set-aside large enough for them.
+int l2_acquire(Engine *e, bool *ok) {
+  *ok = false;
+  const int dev = e->desc.device;
+  if (dev < 0 || dev >= kL2Devices) return SKV_OK;
+  int max_persist = 0, max_win = 0;
+  CK(cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, dev));
+  CK(cudaDeviceGetAttribute(&max_win, cudaDevAttrMaxAccessPolicyWindowSize, dev));
+  const size_t bytes = e->planes_bytes;
+  std::lock_guard<std::mutex> lock(g_l2_lock);
+  if (max_persist <= 0 || max_win <= 0 || bytes > (size_t)max_win || g_l2_bytes[dev] + bytes > (size_t)max_persist)
+    return SKV_OK;
+  if (g_l2_users[dev] == 0) CK(cudaDeviceGetLimit(&g_l2_prev[dev], cudaLimitPersistingL2CacheSize));
+  CK(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g_l2_bytes[dev] + bytes));
+  ++g_l2_users[dev];
+  g_l2_bytes[dev] += bytes;
+  e->l2win.base_ptr = e->planes;
+  e->l2win.num_bytes = bytes;
+  e->l2win.hitRatio = 1.0f;
+  e->l2win.hitProp = cudaAccessPropertyPersisting;
+  e->l2win.missProp = cudaAccessPropertyStreaming;
+  e->l2_resident = true;
+  *ok = true;
+  return SKV_OK;
+}
+
 // Enqueue one decode step of the engine's path; for a connected shard group
 // the global merge, attention and combine over peer memory follow.
 cudaError_t launch_step(const Engine *e, const Work &w, cudaStream_t st) {
-  cudaError_t r = e->fused ? launch_fused(w, st) : launch_funnel(w, st);
+  cudaError_t r = e->fused ? launch_fused(w, st, window_of(e)) : launch_funnel(w, st);
   if (r != cudaSuccess || !e->link.active) return r;
   // the fused kernel exchanges inside itself (Work::link); the staged path
   // runs the exchange kernels after its funnel
@@ -153,7 +217,8 @@ int dalloc(Engine *e, T **p, size_t count) {
 
 void free_cell(CellBufs &b, bool index, bool kv) {
   if (index) {
-    for (void *p : {(void *)b.upper, (void *)b.lower, (void *)b.coarse_scale4, (void *)b.fine_scale,
+    // (the upper and lower planes live in the engine's plane arena)
+    for (void *p : {(void *)b.coarse_scale4, (void *)b.fine_scale,
                     (void *)b.resid, (void *)b.offsets, (void *)b.values, (void *)b.mates, (void *)b.offsets2,
                     (void *)b.values2, (void *)b.mates2})
       if (p) cudaFree(p);
@@ -323,6 +388,8 @@ int skv_create(const SkvDesc *d, void **handle) {
   w.local = d->local;
   w.nc = d->nc;
   w.cap = d->stage15_capacity;
+  e->planes_bytes = (size_t)C * d->nc * 128;
+  TRY(cudaMalloc(reinterpret_cast<void **>(&e->planes), e->planes_bytes + 16) ? fail(SKV_E_CUDA, "plane arena") : 0);
   TRY(dalloc(e, &e->dcells, C));
   w.cells = e->dcells;
   uint16_t *q = nullptr;
@@ -416,7 +483,9 @@ void skv_destroy(void *handle) {
       if (p) cudaIpcCloseMemHandle(p);
   if (e->link.region) cudaFree(e->link.region);
   drop_graphs(e);
+  if (e->l2_resident) l2_release(e);
   for (auto &b : e->bufs) free_cell(b, true, true);
+  if (e->planes) cudaFree(e->planes);
   for (void *p : e->wkeys)
     if (p) cudaFree(p);
   if (e->kv_stage) cudaFree(e->kv_stage);
@@ -508,8 +577,10 @@ int skv_upload_index(void *handle, int32_t slot, const SkvCellView *cells) {
     CellBufs &b = e->bufs[cell];
     free_cell(b, true, false);
     int rc;
-    if ((rc = upload(&b.upper, v.upper, (size_t)nc * 64))) return rc;
-    if ((rc = upload(&b.lower, v.lower, (size_t)nc * 64))) return rc;
+    b.upper = e->planes + (size_t)cell * nc * 128;
+    b.lower = b.upper + (size_t)nc * 64;
+    CK(cudaMemcpy(b.upper, v.upper, (size_t)nc * 64, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(b.lower, v.lower, (size_t)nc * 64, cudaMemcpyHostToDevice));
     if ((rc = upload(&b.coarse_scale4, v.coarse_scale4, (size_t)nc / 32))) return rc;
     if ((rc = upload(&b.fine_scale, v.fine_scale, (size_t)nc / 32))) return rc;
     if ((rc = upload(&b.resid, v.resid_bf16, (size_t)nc))) return rc;
@@ -717,6 +788,28 @@ int skv_run(void *handle, void *stream) {
   e->host_io = host;
   CK(cudaEventRecord(e->done, st));
   e->ran = true;
+  return SKV_OK;
+}
+
+int skv_set_l2_residency(void *handle, int32_t enable, size_t *resident_bytes) {
+  Engine *e = as_engine(handle);
+  if (!e) return fail(SKV_E_INVALID, "null engine");
+  if (resident_bytes) *resident_bytes = 0;
+  int rc = sync_done(e);
+  if (rc) return rc;
+  if (!enable) {
+    if (e->l2_resident) {
+      l2_release(e);
+      drop_graphs(e);  // the step graphs are captured again without the window
+    }
+    return SKV_OK;
+  }
+  if (!e->l2_resident && e->fused) {
+    bool ok = false;
+    if ((rc = l2_acquire(e, &ok))) return rc;
+    if (ok) drop_graphs(e);  // captured again with the window on the funnel's launch
+  }
+  if (resident_bytes) *resident_bytes = e->l2_resident ? e->l2win.num_bytes : 0;
   return SKV_OK;
 }
 
@@ -1202,7 +1295,7 @@ int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_k
   e->host_io = false;
   if (e->fused) {
     cudaEventRecord(ev[0], st);
-    le = launch_fused(e->work, st);
+    le = launch_fused(e->work, st, window_of(e));
     cudaEventRecord(ev[1], st);
   } else {
     le = launch_funnel(e->work, st, ev.data());
@@ -1243,7 +1336,7 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
     w.shard_gids = e->link.gids;
   }
   e->host_io = false;
-  CK(launch_fused(w, st));  // (with a connected group, the kernel advances the step counter)
+  CK(launch_fused(w, st, window_of(e)));  // (with a connected group, the kernel advances the step counter)
   CK(cudaMemcpyAsync(ts.data(), e->phase_ts, ts.size() * sizeof(long long), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   CK(cudaEventRecord(e->done, st));
@@ -1283,7 +1376,7 @@ int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end
   CK(cudaEventCreate(&ev[1]));
   e->host_io = false;
   cudaEventRecord(ev[0], st);
-  cudaError_t le = launch_fused(w, st);
+  cudaError_t le = launch_fused(w, st, window_of(e));
   cudaEventRecord(ev[1], st);
   std::vector<long long> ts(nts, 0);
   cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(ev[1]) : le;

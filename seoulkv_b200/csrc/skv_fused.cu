@@ -1850,19 +1850,25 @@ cudaError_t prepare_fused_attributes() {
   return cudaFuncSetAttribute(k_funnel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
-cudaError_t launch_fused(const Work &w, cudaStream_t st) {
+cudaError_t launch_fused(const Work &w, cudaStream_t st, const cudaAccessPolicyWindow *win) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, w.n_cells, 1);
   cfg.blockDim = dim3(FT, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (win && win->num_bytes) {
+    // the centroid planes stay in the persisting part of L2 across steps
+    attr[1].id = cudaLaunchAttributeAccessPolicyWindow;
+    attr[1].val.accessPolicyWindow = *win;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, k_funnel, w);
 }
 

@@ -128,3 +128,72 @@ def test_large_attention_zones(cuda, monkeypatch, staged):
         got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
         err = np.abs(got - O.bf16_to_f32(ref_out).astype(np.float64))
         assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
+
+
+@pytest.fixture(scope="module")
+def headline():
+    """T=131072, nprobe 384, sink 128, local 256."""
+    return Case(context=131072, nprobe=384, seed=1000)
+
+
+@pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
+def test_headline_config_parity(cuda, monkeypatch, headline, staged):
+    """The benchmarked configuration itself: every stage bit-exact, ids
+    bit-exact and the output within tolerance, on three fresh queries."""
+    monkeypatch.setattr(_native, "FORCE_STAGED", staged)
+    case = headline
+    nc = case.index.cells()[0]["centroids"].shape[0]
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
+        for qseed in (1000 * 7919 + 3, 1000 * 7919 + 4, 1000 * 7919 + 5):
+            q = case.query(qseed)
+            y = attn.run(q).to_torch()
+            assert attn._engine.fused == (not staged)
+            res, ref_out = case.oracle(q)
+            _compare(attn._engine, res, nc, 13056)
+            ids = attn.debug_snapshot()["selected_ids"].numpy()
+            assert np.array_equal(ids, np.stack([r["final_ids"] for r in res])), "selected token ids"
+            got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
+            err = np.abs(got - O.bf16_to_f32(ref_out).astype(np.float64))
+            assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
+
+
+def test_l2_window_changes_nothing(cuda, headline):
+    """The centroid planes held in persisting L2 give the same bits as without
+    the window (and the window really is set on a B200)."""
+    case = headline
+    nc = case.index.cells()[0]["centroids"].shape[0]
+    outs = []
+    for resident in (True, False):
+        cfg = SeoulKV4Config(debug=True, l2_resident=resident)
+        with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
+            got = []
+            for qseed in (11, 12):
+                y = attn.run(case.query(qseed)).to_torch()
+                got.append((bits(y), attn.debug_snapshot()["selected_ids"].numpy()))
+            meta = attn.metadata()
+            if resident:
+                assert meta["l2_resident_bytes"] == 4 * nc * 128, meta["l2_resident_bytes"]
+            else:
+                assert meta["l2_resident_bytes"] == 0
+            outs.append(got)
+    for (ya, ia), (yb, ib) in zip(*outs):
+        assert np.array_equal(ya, yb) and np.array_equal(ia, ib)
+
+
+def test_above_the_fused_limit(cuda):
+    """T = 262,144 (nc = 65,440 > 32,768): the staged kernels carry it; every
+    stage bit-exact against the oracle."""
+    case = Case(context=262144, nprobe=384, seed=62)
+    nc = case.index.cells()[0]["centroids"].shape[0]
+    assert nc > 32768
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
+        for qseed in (1, 2):
+            q = case.query(qseed)
+            y = attn.run(q).to_torch()
+            res, ref_out = case.oracle(q)
+            _compare(attn._engine, res, nc, 13056)
+            ids = attn.debug_snapshot()["selected_ids"].numpy()
+            assert np.array_equal(ids, np.stack([r["final_ids"] for r in res])), "selected token ids"
+            got = O.bf16_to_f32(bits(y).reshape(16, 256)).astype(np.float64)
+            err = np.abs(got - O.bf16_to_f32(ref_out).astype(np.float64))
+            assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
