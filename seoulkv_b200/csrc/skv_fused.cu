@@ -786,24 +786,36 @@ __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, 
   }
   __syncthreads();
   mark(M_XLIST);
+  // every shard's list of this (cell, head) into shared memory in one pass of
+  // independent loads (the peers wrote them into this GPU's region), as
+  // 64-bit merge keys; the binary searches below then touch shared memory
+  // only (searching global memory made each search a chain of dependent
+  // memory round trips, one chain per other shard)
   const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
+  unsigned long long *mk = reinterpret_cast<unsigned long long *>(S.big + 4096);  // [n][TOPK]
+  static_assert(4096 + SHARD_MAX * TOPK * 8 <= BIG, "merge keys fit the staging area");
+  for (int c = tid; c < n * TOPK; c += FT) {
+    const int s = c / TOPK, r = c - s * TOPK;
+    const uint32_t key = __ldcv(&R->keys[s][ch][r]);
+    const int32_t id = __ldcv(&R->ids[s][ch][r]);
+    mk[c] = key ? merge_key(key, r, L.begin[s] + id) : 0ull;
+  }
+  __syncthreads();
   int32_t *gout = w.shard_gids + (size_t)ch * TOPK;
   int valid = 0;
   for (int c = tid; c < n * TOPK; c += FT) {
     const int s = c / TOPK, r = c - s * TOPK;
-    const uint32_t key = __ldcv(&R->keys[s][ch][r]);
-    if (!key) continue;
-    const int gid = L.begin[s] + __ldcv(&R->ids[s][ch][r]);
-    const unsigned long long kv = merge_key(key, r, gid);
+    const unsigned long long kv = mk[c];
+    if (!kv) continue;
+    const int gid = (int)(0xffffffffu - (uint32_t)(kv & 0xffffffffull));
     int rank = r;
     for (int s2 = 0; s2 < n; ++s2) {
       if (s2 == s) continue;
-      int lo = 0, hi = TOPK;  // first entry of list s2 not above kv
+      const unsigned long long *l2 = mk + s2 * TOPK;
+      int lo = 0, hi = TOPK;  // first entry of list s2 not above kv (zero keys end a list)
       while (lo < hi) {
         const int mid = (lo + hi) >> 1;
-        const uint32_t k2 = __ldcv(&R->keys[s2][ch][mid]);
-        const bool above = k2 && merge_key(k2, mid, L.begin[s2] + __ldcv(&R->ids[s2][ch][mid])) > kv;
-        if (above) lo = mid + 1; else hi = mid;
+        if (l2[mid] > kv) lo = mid + 1; else hi = mid;
       }
       rank += lo;
     }
@@ -1702,6 +1714,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   // enough for that split to be balanced); a warp's items go 32 at a time
   const int nwa = (CL - G) * FW;
   const bool early = dense <= nwa * 32;
+  __syncthreads();  // every warp is done with its Stage-II rows in the staging area (stg lies above them)
   if (early && rank >= G) {
     const int gwa = (rank - G) * FW + warp;
     const int na = gwa < dense ? (dense - gwa + nwa - 1) / nwa : 0;
