@@ -93,7 +93,22 @@ def lib():
                      "skv_oracle_stage15", "skv_oracle_stage16"):
             getattr(_lib, name).restype = ctypes.c_int
         _lib.skv_oracle_set_threads.argtypes = [ctypes.c_int]
+        _lib.skv_oracle_set_unflushed.argtypes = [ctypes.c_int]
+        _lib.skv_oracle_unflushed_dropped.restype = ctypes.c_longlong
     return _lib
+
+
+def set_unflushed(on: bool) -> None:
+    """Switch every scoring dot to the unflushed exact sum (all operand
+    elements, 128-bit integers, one FP32 rounding).  A measurement of the
+    canonical definition's flush of elements below 2^(E-22), not a second
+    definition: the engine follows the flushed one."""
+    lib().skv_oracle_set_unflushed(1 if on else 0)
+
+
+def unflushed_dropped() -> int:
+    """Operand elements the unflushed mode could not hold (spread > 86 bits)."""
+    return int(lib().skv_oracle_unflushed_dropped())
 
 
 def set_threads(n: int) -> None:

@@ -112,7 +112,21 @@ typedef struct {
     int64_t xa[G][D]; int32_t sa[G];   /* q        (coarse, fine)  */
     int64_t xb[G][D]; int32_t sb[G];   /* 16*q15   (stage 1.5)     */
     int64_t xd[G][D]; int32_t sd[G];   /* qs       (stage II); 16*qs for 1.6 */
+    /* the same operand rows before the flush (unflushed mode) */
+    float ra[G][D], rb[G][D], rd[G][D];
 } OracleQuery;
+
+/* Unflushed mode (a measurement of the flush, not the canonical definition):
+ * every operand element takes part in the exact sum, however small.  The
+ * sum is formed with 128-bit integers on the grid of the row's smallest
+ * element and rounded once to FP32.  A row whose elements span more than
+ * UNFLUSHED_SPAN bits of exponent (which no query of the tests comes near)
+ * drops the elements below that span, and g_unflushed_dropped counts them. */
+static int g_unflushed = 0;
+static long long g_unflushed_dropped = 0;
+#define UNFLUSHED_SPAN 86
+void skv_oracle_set_unflushed(int on) { g_unflushed = on != 0; g_unflushed_dropped = 0; }
+long long skv_oracle_unflushed_dropped(void) { return g_unflushed_dropped; }
 
 /* ------------------------------------------------------- query operands */
 
@@ -158,10 +172,60 @@ void skv_oracle_prepare_query(const uint16_t *q /* [4][256] bf16 */,
         exact_row(o->qb[h], o->xa[h], &o->sa[h]);
         exact_row(b, o->xb[h], &o->sb[h]);
         exact_row(d16, o->xd[h], &o->sd[h]);
+        memcpy(o->ra[h], o->qb[h], sizeof(float) * D);
+        memcpy(o->rb[h], b, sizeof(float) * D);
+        memcpy(o->rd[h], d16, sizeof(float) * D);
     }
 }
 
-static inline float exact_dot(const int64_t *X, int32_t shift, const int32_t *w) {
+/* sum_d row[d] * 2^e_add * w[d], exact, rounded once to FP32 (RNE); the
+ * unflushed mode's dot (see g_unflushed). */
+static float unflushed_dot(const float *row, int e_add, const int32_t *w) {
+    int kmax = INT32_MIN, kmin = INT32_MAX;
+    for (int d = 0; d < D; ++d)
+        if (row[d] != 0.0f) {
+            const int k = ilogbf(row[d]) - 23;   /* the element's lsb exponent (24-bit significand) */
+            if (k > kmax) kmax = k;
+            if (k < kmin) kmin = k;
+        }
+    if (kmax == INT32_MIN) return 0.0f;
+    if (kmax - kmin > UNFLUSHED_SPAN) kmin = kmax - UNFLUSHED_SPAN;
+    __int128 acc = 0;
+    for (int d = 0; d < D; ++d) {
+        if (row[d] == 0.0f) continue;
+        const int k = ilogbf(row[d]) - 23;
+        if (k < kmin) {
+#pragma omp atomic
+            ++g_unflushed_dropped;
+            continue;
+        }
+        /* row[d] = m * 2^k exactly, |m| < 2^24 */
+        const int64_t m = (int64_t)ldexp((double)row[d], -k);
+        acc += ((__int128)m << (k - kmin)) * w[d];
+    }
+    const int neg = acc < 0;
+    unsigned __int128 a = neg ? (unsigned __int128)(-acc) : (unsigned __int128)acc;
+    if (a == 0) return 0.0f;
+    int n = 0;
+    for (unsigned __int128 t = a; t; t >>= 1) ++n;
+    int e = kmin + e_add;
+    uint64_t mant;
+    if (n <= 24) {
+        mant = (uint64_t)a;
+    } else {
+        const int sh = n - 24;
+        mant = (uint64_t)(a >> sh);
+        const unsigned __int128 rem = a & (((unsigned __int128)1 << sh) - 1);
+        const unsigned __int128 half = (unsigned __int128)1 << (sh - 1);
+        if (rem > half || (rem == half && (mant & 1))) ++mant;
+        e += sh;
+    }
+    const float f = ldexpf((float)mant, e);   /* mant <= 2^24: exact */
+    return neg ? -f : f;
+}
+
+static inline float exact_dot(const int64_t *X, int32_t shift, const float *row, int e_add, const int32_t *w) {
+    if (g_unflushed) return unflushed_dot(row, e_add, w);
     int64_t acc = 0;
     for (int d = 0; d < D; ++d) acc += X[d] * (int64_t)w[d];
     return (float)ldexp((double)acc, shift);
@@ -200,7 +264,7 @@ int skv_oracle_coarse(const OracleCell *c, const OracleQuery *q, uint16_t *lo /*
         const float sc4 = c->coarse_scale4[i >> 5];
         const float r = bf16f(c->resid_bf16[i]);
         for (int h = 0; h < G; ++h) {
-            float dot = exact_dot(q->xa[h], q->sa[h], w);
+            float dot = exact_dot(q->xa[h], q->sa[h], q->ra[h], 0, w);
             float corr = 3.0f * q->qsum[h];
             float centered = 2.0f * dot - corr;
             float v = centered * sc4;
@@ -249,7 +313,7 @@ int skv_oracle_fine(const OracleCell *c, const OracleQuery *q, const uint32_t *t
         const float fs = c->fine_scale[cid >> 5];
         for (int h = 0; h < G; ++h) {
             if (!((mask >> h) & 1)) { scores[h * ntags + i] = 0xff80u; continue; }
-            float dot = exact_dot(q->xa[h], q->sa[h], w);
+            float dot = exact_dot(q->xa[h], q->sa[h], q->ra[h], 0, w);
             scores[h * ntags + i] = skv_oracle_bf16_rne(dot * fs);
         }
     }
@@ -315,7 +379,7 @@ int skv_oracle_stage15(const OracleCell *c, const OracleQuery *q, const int32_t 
         const uint8_t *row = c->prefix2 + (size_t)pool[i] * 64;
         for (int d = 0; d < D; ++d) w[d] = 2 * p2_at(row, d) - 3;
         for (int h = 0; h < G; ++h)
-            scores[h * npool + i] = skv_oracle_bf16_rne(exact_dot(q->xb[h], q->sb[h], w));
+            scores[h * npool + i] = skv_oracle_bf16_rne(exact_dot(q->xb[h], q->sb[h], q->rb[h], 0, w));
     }
     const int k = m < npool ? m : npool;
     KeyIdx *items_all = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)npool * G);
@@ -349,7 +413,7 @@ int skv_oracle_stage16(const OracleCell *c, const OracleQuery *q, const int32_t 
         const uint8_t *p = c->prefix2 + (size_t)t * 64, *r = c->residual2 + (size_t)t * 64;
         for (int d = 0; d < D; ++d) w[d] = 2 * ((p2_at(p, d) << 2) | p2_at(r, d)) - 15;
         for (int h = 0; h < G; ++h)   /* operand 16*qs: same integers, shift + 4 */
-            scores[h * nu + u] = skv_oracle_bf16_rne(exact_dot(q->xd[h], q->sd[h] + 4, w));
+            scores[h * nu + u] = skv_oracle_bf16_rne(exact_dot(q->xd[h], q->sd[h] + 4, q->rd[h], 4, w));
     }
     const int k = m < nu ? m : nu;
     KeyIdx *items_all = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)(nu > 0 ? nu : 1) * G);
@@ -387,7 +451,7 @@ void skv_oracle_stage2(const OracleCell *c, const OracleQuery *q, const int32_t 
             w[d] = 2 * code8 - 255;
         }
         for (int h = 0; h < G; ++h)
-            scores[h * ncand + j] = skv_oracle_bf16_rne(exact_dot(q->xd[h], q->sd[h], w));
+            scores[h * ncand + j] = skv_oracle_bf16_rne(exact_dot(q->xd[h], q->sd[h], q->rd[h], 0, w));
     }
     KeyIdx *items = (KeyIdx *)malloc(sizeof(KeyIdx) * (size_t)ncand);
     for (int h = 0; h < G; ++h) {

@@ -140,10 +140,12 @@ def midrise4(x: torch.Tensor) -> torch.Tensor:
 
 
 def to_csr(labels: torch.Tensor, nc: int):
-    """CSR of spill lists: offsets [nc+1] int32, values [2R] local token ids (token order)."""
-    flat = labels.reshape(-1).cpu()
-    tokens = torch.arange(labels.shape[0]).repeat_interleave(labels.shape[1])
+    """CSR of spill lists: offsets [nc+1] int32, values [2R] local token ids
+    (token order), on the labels' device (integer sort and scan: the same
+    lists on the host and the GPU)."""
+    flat = labels.reshape(-1)
+    tokens = torch.arange(labels.shape[0], device=flat.device).repeat_interleave(labels.shape[1])
     order = torch.argsort(flat, stable=True)
     counts = torch.bincount(flat, minlength=nc)
-    offsets = torch.cat([torch.zeros(1, dtype=torch.long), counts.cumsum(0)])
+    offsets = torch.cat([torch.zeros(1, dtype=torch.long, device=flat.device), counts.cumsum(0)])
     return offsets.int(), tokens[order].int()

@@ -50,19 +50,30 @@ def unpack2(packed: torch.Tensor) -> torch.Tensor:
 
 
 def coarse_metadata(source: torch.Tensor, upper: torch.Tensor, scale: torch.Tensor) -> dict:
-    """Two-bit centroid operands and the residual norm used by the coarse interval."""
+    """Two-bit centroid operands and the residual norm used by the coarse interval.
+
+    The norm is a float32 reduction whose rounding depends on the summation
+    order, so it is always taken on the host (the reference's own order):
+    a device encode sends the [nc, 256] residuals over and reduces them here."""
     odd = 2 * unpack2(upper).float() - 3
     full = scale.float()[:, None] * odd / 4
     return {
         "coarse2": full.half(),
         "coarse_odd": odd.bfloat16(),
-        "coarse_residual_norm": (source.float() - full).norm(dim=-1).half(),
+        "coarse_residual_norm": (source.float() - full).cpu().norm(dim=-1).half(),
     }
 
 
 def encode_group_scale_cell(cell: dict) -> dict:
-    """Quantise a cell's FP16 centroids and remap its CSR lists (query-free)."""
+    """Quantise a cell's FP16 centroids and remap its CSR lists (query-free).
+
+    Runs on the device that holds the centroids (a CUDA build encodes on the
+    GPU: every step is elementwise, a stable sort, an integer scan, or an
+    exact max, so the codes, planes, scales and lists are the bytes the host
+    computes; the residual norm's float32 sum is taken on the host, see
+    coarse_metadata); the returned cell holds CPU tensors."""
     original = cell.get("coarse_centroids", cell["centroids"])
+    dev = original.device
     x = original.float()
     nc, d = x.shape
     if d != 256 or nc % GROUP:
@@ -78,23 +89,22 @@ def encode_group_scale_cell(cell: dict) -> dict:
     odd = (2 * code.float() - 15).bfloat16()
     decoded = (scale[:, None] * odd.float() / 16).half()
     levels = (
-        (group_scale[:, None, None] * (2 * torch.arange(16).float()[None, None] - 15) / 16)
+        (group_scale[:, None, None] * (2 * torch.arange(16, device=dev).float()[None, None] - 15) / 16)
         .expand(-1, GROUP, -1)
         .reshape(nc, 16)
         .half()
     )
     upper, lower = pack2(code >> 2), pack2(code & 3)
 
-    offsets = cell["offsets"].long()
+    offsets = cell["offsets"].to(dev).long()
     lengths = offsets[1:] - offsets[:-1]
-    owner = torch.repeat_interleave(torch.arange(nc), lengths)
+    owner = torch.repeat_interleave(torch.arange(nc, device=dev), lengths)
     rank = torch.empty_like(order)
-    rank[order] = torch.arange(nc)
+    rank[order] = torch.arange(nc, device=dev)
     posting_order = torch.argsort(rank[owner], stable=True)
-    new_offsets = torch.cat((torch.zeros(1, dtype=torch.long), lengths[order].cumsum(0)))
+    new_offsets = torch.cat((torch.zeros(1, dtype=torch.long, device=dev), lengths[order].cumsum(0)))
     group_fine_scale = (group_scale / 16).half()
-    out = dict(cell)
-    out.update(
+    fields = dict(
         coarse_centroids=x.to(original.dtype),
         centroids=decoded.bfloat16(),
         upper=upper,
@@ -106,12 +116,14 @@ def encode_group_scale_cell(cell: dict) -> dict:
         levels=levels,
         centroid_codec=CENTROID_CODEC,
         offsets=new_offsets.to(cell["offsets"].dtype),
-        values=cell["values"][posting_order],
+        values=cell["values"].to(dev)[posting_order],
         max_codec_error=float((x - decoded.float()).abs().max()),
         group_scale_size=GROUP,
         summary_codec=CODEC,
         **coarse_metadata(x, upper, scale),
     )
+    out = dict(cell)
+    out.update({k: v.cpu() if isinstance(v, torch.Tensor) else v for k, v in fields.items()})
     return out
 
 

@@ -96,6 +96,13 @@ struct SelRes {
   uint32_t pf, kr, th, flags;
 };
 
+// Profiling marks of one CTA (thread 0): buffer, count, time base.
+struct MarkState {
+  long long *ts;  // null unless this CTA records
+  int n;
+  int global;     // global-timer ns (comparable across SMs) instead of SM clocks
+};
+
 struct FusedSmem {
   uint32_t frag[3 * FRAG_ROW];     // int8 digit fragments of the three operand rows
   uint32_t hist[4 * 256];          // this CTA's selection histogram (4 heads x 256 bins)
@@ -115,6 +122,7 @@ struct FusedSmem {
   float qscal[8];
   long long sxsum[3][4];           // sum over d of X_d per operand row and head
   int round, status, n_win, pad_;
+  MarkState ms;                    // profiling marks (thread 0)
   CellDev cell;                    // this cell's descriptor (read once from global)
   alignas(16) union {
     struct { uint16_t lo[4][PER_MAX]; uint16_t hi[4][PER_MAX]; } c;   // P1-P3
@@ -157,15 +165,22 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
+// The mark buffer and count live in shared memory (FusedSmem::ms, set by
+// thread 0 at entry) and only thread 0 records, so an unprofiled step pays one
+// branch on the thread index per mark and nothing is held in registers or
+// local memory across the phases.  (A marker object passed by reference to
+// the out-of-line phases lived in local memory, and every thread read it back
+// at every mark: ~4 us per step at 128K.)
 struct Marker {
-  long long *ts;
-  int n;
-  bool global;  // global-timer ns (comparable across SMs) instead of SM clocks
-  __device__ __forceinline__ void operator()(int tag) {
-    if (ts && n < FUSED_MARKS) {
-      ts[2 * n] = tag;
-      ts[2 * n + 1] = global ? (long long)global_ns() : clock64();
-      ++n;
+  MarkState *st;
+  __device__ __forceinline__ void operator()(int tag) const {
+    if (threadIdx.x == 0 && st->ts) {
+      const int k = st->n;
+      if (k < FUSED_MARKS) {
+        st->ts[2 * k] = tag;
+        st->ts[2 * k + 1] = st->global ? (long long)global_ns() : clock64();
+        st->n = k + 1;
+      }
     }
   }
 };
@@ -501,7 +516,8 @@ __device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t 
 // the keys a global K-th largest key would; S.ctl.own[h] marks the CTA whose
 // threshold is the cluster's K-th largest key.
 __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, int nbits, bool exact, int kind,
-                                            int q0, Marker &mark, bool pre = false) {
+                                            int q0, bool pre = false) {
+  const Marker mark{&S.ms};
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = (int)cluster_rank();
   int ph_in = S.ph_in, ph_res = S.ph_res;  // (read by every thread before the barrier below)
@@ -760,7 +776,8 @@ __device__ __forceinline__ unsigned long long merge_key(uint32_t key, int r, int
 }
 
 __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, int h, const uint32_t *fkeys,
-                                         const int32_t *fids, Marker &mark) {
+                                         const int32_t *fids) {
+  const Marker mark{&S.ms};
   const ShardLinkDev &L = *w.link;
   const int tid = threadIdx.x, n = L.n_shards, ch = cell * G + h;
   const uint32_t epoch = *L.epoch + 1;
@@ -832,6 +849,7 @@ __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, 
 __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
+  const unsigned long long t_entry = global_ns();  // (CTA entry stamp of skv_profile_ctas)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, t = lane & 3;
   const int hA = t >> 1, hB = 2 + hA;
   const int rank = (int)cluster_rank();
@@ -844,7 +862,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   const int per = ((nc + CL * 32 - 1) / (CL * 32)) * 32;
   const int r0 = min(nc, rank * per), r1 = min(nc, r0 + per), nrows = r1 - r0;
   const uint32_t P = (uint32_t)c.nprobe;
-  if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank)] = (long long)global_ns();
+  if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank)] = (long long)t_entry;
   // marks: SM clocks of CTA 0 of cell 0 (Work::phase_ts), or global-timer
   // marks of every CTA of cell 0 after the entry/exit stamps (Work::cta_ts)
   long long *mts = nullptr;
@@ -852,7 +870,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (w.phase_ts) mts = rank == 0 ? w.phase_ts : nullptr;
     else if (w.cta_ts) mts = w.cta_ts + 2 * (size_t)w.n_cells * CL + (size_t)rank * 2 * FUSED_MARKS;
   }
-  Marker mark{mts, 0, !w.phase_ts};
+  if (tid == 0) S.ms = MarkState{mts, 0, !w.phase_ts};  // (read and written by thread 0 only)
+  const Marker mark{&S.ms};
   int *counts = w.counts + cell * NCOUNT;
   mark(M_START);
 
@@ -1008,7 +1027,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     const Pow2 scA = pow2s(S.shift[R_Q][hA]), scB = pow2s(S.shift[R_Q][hB]);
     const float qnA = S.qscal[hA], qnB = S.qscal[hB], c3A = S.qscal[4 + hA], c3B = S.qscal[4 + hB];
     const int tiles = nrows >> 4;
-    if (mark.ts && tiles > 0) {
+    if (tid == 0 && S.ms.ts && tiles > 0) {
       mbar_wait(&S.mbar[(tiles * 16 - 1) / SLICE_CHUNK], 0);
       mark(M_SLICE);
     }
@@ -1043,7 +1062,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   // ---------------------------------------------------------------- P2
   cluster_wait();
   {
-    cluster_select(S, nrows, P, 16, true, KEY_COARSE, 0, mark, true);
+    cluster_select(S, nrows, P, 16, true, KEY_COARSE, 0, true);
   }
   uint32_t tco[4];
 #pragma unroll
@@ -1153,7 +1172,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // ---------------------------------------------------------------- P5
   {
-    cluster_select(S, nsh, P, 32, false, KEY_FINE, 0, mark);
+    cluster_select(S, nsh, P, 32, false, KEY_FINE, 0);
   }
   mark(M_FSEL);
   uint32_t st = 0;
@@ -1164,7 +1183,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       tf[h] = S.ctl.th[h];
       if (tf[h] == 0u) { tf[h] = 0xffffffffu; st |= ST_FINE_SHORT; }
     }
-    if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_FINE * G + tid] = tf[tid];
+    if (tid < 4 && S.ctl.own[tid])
+      w.thr[(size_t)cell * 16 + T_FINE * G + tid] = S.ctl.th[tid] ? S.ctl.th[tid] : 0xffffffffu;
     uint32_t *selbits = w.selbits + (size_t)cell * (nc >> 5);
     for (int k = tid; k < nsh; k += FT) {
       bool s = false;
@@ -1377,7 +1397,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // ---------------------------------------------------------------- P8
   {
-    cluster_select(S, m15, (uint32_t)min(UNION15, n15), 32, false, KEY_S15, q0, mark);
+    cluster_select(S, m15, (uint32_t)min(UNION15, n15), 32, false, KEY_S15, q0);
   }
   mark(M_S15SEL);
   int nu;
@@ -1385,7 +1405,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     uint32_t tu[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) tu[h] = S.ctl.th[h] ? S.ctl.th[h] : 0xffffffffu;
-    if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_S15 * G + tid] = tu[tid];
+    if (tid < 4 && S.ctl.own[tid])
+      w.thr[(size_t)cell * 16 + T_S15 * G + tid] = S.ctl.th[tid] ? S.ctl.th[tid] : 0xffffffffu;
     const int i0 = tid * 2;
     int f[2], cnt = 0;
 #pragma unroll
@@ -1453,7 +1474,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // ---------------------------------------------------------------- P9
   {
-    cluster_select(S, m15, (uint32_t)min(M16, nu_all), 32, false, KEY_S16, q0, mark);
+    cluster_select(S, m15, (uint32_t)min(M16, nu_all), 32, false, KEY_S16, q0);
   }
   mark(M_S16SEL);
   int ncl;
@@ -1461,7 +1482,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     uint32_t tc[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) tc[h] = S.ctl.th[h] ? S.ctl.th[h] : 0xffffffffu;
-    if (tid < 4 && S.ctl.own[tid]) w.thr[(size_t)cell * 16 + T_S16 * G + tid] = tc[tid];
+    if (tid < 4 && S.ctl.own[tid])
+      w.thr[(size_t)cell * 16 + T_S16 * G + tid] = S.ctl.th[tid] ? S.ctl.th[tid] : 0xffffffffu;
     const int i0 = tid * 2;
     int f[2], cnt = 0;
 #pragma unroll
@@ -1613,7 +1635,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       wtok[tid] = 0;
     }
     if (w.link) {
-      shard_lists(w, S, cell, h, fkeys, fids, mark);
+      shard_lists(w, S, cell, h, fkeys, fids);
     } else {
       // head h's winners, in rank order, into every CTA's S.win[h]
       __syncthreads();

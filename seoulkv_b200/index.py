@@ -197,8 +197,9 @@ def build_cell(k: torch.Tensor, *, p: int, lam: float, seed: int, r0: int, r1: i
     x = _clustering._normalise(x)
     centroids, labels, stats = _clustering.build_ivf(x, nc, seed)
     offsets, values = _clustering.to_csr(labels, nc)
+    # the codec runs where the clustering ran (the GPU for a CUDA build)
     cell = _codecs.encode_group_scale_cell(dict(
-        centroids=_clustering.midrise4(centroids).half().cpu(),
+        centroids=_clustering.midrise4(centroids).half(),
         offsets=offsets,
         values=values + r0,
         context=len(k), r0=r0, r1=r1, spill=2, p=int(p), lam=float(lam), seed=int(seed),
