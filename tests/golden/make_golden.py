@@ -16,7 +16,9 @@ everything that *can* run here:
 * query operands come from the reference's ``query_prepare.reference``;
 * for each query, the oracle's Fine survivors/scores are fed to the
   reference's ``tree_top_p`` and ``distributed_union_reference``, its
-  selected clusters to ``encounter_union`` / ``expand_lists``, and its
+  selected clusters to ``encounter_union`` / ``expand_lists``, its Stage-1.5
+  scores (split over the reference's six pool shards) to the score-only
+  ``merge_tree_reference`` of the 6->3->2->1 frontier merge, and its
   Stage-1.5 frontiers to ``source_union_reference``; their outputs are stored;
 * the group-scale centroid codec and the posting-mate map of the reference
   are stored for a small input and for the fixture index.
@@ -66,6 +68,7 @@ def main():
     from seoulkv4._codecs.keys import _stage15_key_codec, encode_planes
     from seoulkv4._kernels.common.seoulkv4_cluster_blocks import encounter_union, posting_mates
     from seoulkv4._kernels.query_prepare.host import reference as qp_reference
+    from seoulkv4._kernels.stage15.seoulkv4_stage15_tree_merge import merge_tree_reference
     from seoulkv4._kernels.stage15.seoulkv4_stage15_union import source_union_reference
     from seoulkv4._kernels.stage1_fine.seoulkv4_fine_native_select import distributed_union_reference
     from seoulkv4._kernels.stage1_fine.seoulkv4_fine_parallel import schedule, tree_top_p
@@ -163,6 +166,21 @@ def main():
             pool = encounter_union(c, sel)
             data[f"q{qi}_{g}_ref_pool"] = pool.numpy().astype(np.int32)
             data[f"q{qi}_{g}_ref_expand_lists"] = expand_lists(c, sel).numpy().astype(np.int32)
+            # Stage-1.5 frontier: each of the six pool shards (24 workers of
+            # 32-position chunks, four per shard) ranks its own scores, and
+            # the reference's tree merges the six rows into the top 2048
+            npool = len(r["pool"])
+            chunks = (npool + 31) // 32
+            frontier = []
+            for h in range(4):
+                sc = O.ord16(r["s15_scores"][h]).astype(np.int64)
+                rows = []
+                for sh in range(6):
+                    lo = (chunks * (4 * sh) // 24) * 32
+                    hi = min((chunks * (4 * sh + 4) // 24) * 32, npool)
+                    rows.append(sorted(sc[lo:hi].tolist(), reverse=True)[:2048])
+                frontier.append(merge_tree_reference(rows, k=2048))
+            data[f"q{qi}_{g}_ref_s15_frontier"] = np.asarray(frontier, dtype=np.uint16)
             by_source, parts = source_union_reference(
                 [row[:1600] for row in r["s15_top"].tolist()], 13056, 6, 1600)
             data[f"q{qi}_{g}_ref_s15_union"] = np.asarray([x for p in parts for x in p], dtype=np.int32)

@@ -70,6 +70,20 @@ def test_pool_matches_encounter_union(gold, runs):
             assert np.array_equal(np.sort(r["pool"]), gold.z[f"q{qi}_{g}_ref_expand_lists"])
 
 
+def test_stage15_frontier_matches_reference_tree_merge(gold, runs):
+    """The reference ranks Stage-1.5 per pool shard and merges the six
+    shards' rows in a 6->3->2->1 tree into a 2048-score frontier
+    (``merge_tree_reference``, score only), whose first 1600 scores enter the
+    union.  The oracle's top-1600 per head has exactly those scores."""
+    for qi, res in enumerate(runs):
+        for g, r in enumerate(res):
+            want = gold.z[f"q{qi}_{g}_ref_s15_frontier"]
+            for h in range(4):
+                top = r["s15_top"][h]
+                got = np.sort(O.ord16(r["s15_scores"][h][top]))[::-1]
+                assert np.array_equal(got, want[h][:len(top)]), (qi, g, h)
+
+
 def test_stage15_union_matches_source_union(gold, runs):
     for qi, res in enumerate(runs):
         for g, r in enumerate(res):
