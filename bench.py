@@ -367,12 +367,19 @@ def run_sharded(args, world, rank, local, device):
     torch.cuda.synchronize(device)
     clocks.start()
     time.sleep(0.3)
+    # every host enqueues ahead of its device (a short device-side sleep
+    # first, no garbage collection meanwhile), so that the GPUs run their
+    # steps back to back and meet at each step's list exchange, as a decode
+    # loop does; otherwise each step would also carry the hosts' launch skew
+    gc.disable()
+    torch.cuda._sleep(int(2e7))
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
         sh.run(q_dev[args.warmup + i])
         ends[i].record(stream)
     torch.cuda.synchronize(device)
+    gc.enable()
     dist.barrier()
     clk = clocks.stop()
     per = np.array([a.elapsed_time(b) for a, b in zip(starts, ends)]) * 1e3  # µs
@@ -389,18 +396,29 @@ def run_sharded(args, world, rank, local, device):
     fun_all = torch.empty(world, dtype=torch.float64, device=device)
     dist.all_gather_into_tensor(fun_all, torch.tensor([float(np.median(fun))], dtype=torch.float64, device=device))
     shard_funnel_us = [round(float(x), 1) for x in fun_all.cpu()]
-    # phase marks of one whole group step (all ranks together; fused path only)
+    # phase marks of one whole group step on every rank (fused path only):
+    # the profiled step follows two back-to-back steps, so the ranks meet as
+    # in the timed loop; "shard_list_exchange" is the wait for the other
+    # shards' top-100 lists, "attn_items" the attention over the merged
+    # winners (records of other shards read over NVLink)
     phases = None
     if sh.attn._engine.fused and args.transport == "p2p":
         mhz = (clk or {}).get("sm_mhz") or 1965.0
         acc = {}
-        for _ in range(3):
-            flush.zero_()
+        for rep in range(3):
             torch.cuda.synchronize(device)
             dist.barrier()
+            torch.cuda._sleep(int(2e6))
+            for j in range(2):
+                flush.zero_()
+                sh.run(q_dev[j])
+            flush.zero_()
             for name, cyc in sh.attn._engine.profile_phases(stream.cuda_stream):
                 acc[name] = acc.get(name, 0.0) + cyc / 3
-        phases = {n: round(v / mhz, 2) for n, v in acc.items()}
+        mine = {n: round(v / mhz, 2) for n, v in acc.items()}
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+        phases = {f"rank{r}": every[r] for r in range(world)}
 
     # parity: this shard's funnel vs the CPU restatement (ids bit-exact); the
     # merge vs the restated merge rule on the gathered lists; one output on

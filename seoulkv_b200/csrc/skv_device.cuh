@@ -57,6 +57,10 @@ struct ShardRegion {
   float part[SHARD_MAX][SHARD_CELLS][G][PART];            // [source shard][cell][head][m, l, 0, 0, o]
   uint32_t flag_lists[SHARD_MAX][SHARD_CELLS * G];        // epoch of each source's (cell, head) list
   uint32_t flag_parts[SHARD_MAX][SHARD_CELLS];            // epoch of each source's cell partials
+  // the fused kernel's lists: one 8-byte entry per rank carrying its own
+  // step tag, [tag 8 | score 16 | 0 8 | shard-local id 32], so a reader
+  // needs no flag and the writer no fence; double-buffered by step parity
+  unsigned long long ll[2][SHARD_MAX][SHARD_CELLS * G][TOPK];
 };
 
 // Kernel-side view of a connected group.
@@ -81,6 +85,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 // Waits until flag[s * stride] >= epoch for every shard s; false on timeout.
 __device__ __forceinline__ bool wait_flags(const uint32_t *flag, int stride, int n_shards, uint32_t epoch) {
   for (int s = 0; s < n_shards; ++s) {

@@ -775,49 +775,60 @@ __device__ __forceinline__ unsigned long long merge_key(uint32_t key, int r, int
          (unsigned long long)(0xffffffffu - (uint32_t)gid);
 }
 
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The exchange and merge of head h's list (CTA h of the cell's cluster).
+// Each entry travels as one naturally aligned 8-byte store (single-copy
+// atomic, over NVLink too) that carries the step's tag, so a reader polls the
+// entries themselves: no flag, no system-scope fence, one one-way trip.  The
+// tag is the step counter's low byte and the buffer alternates with the
+// step's parity; a shard can only overwrite a buffer after the whole group
+// finished the step before (each shard's step ends after its own merge,
+// which read every shard's entries).  The merged winners go to every CTA's
+// S.win[h] by asynchronous stores (and to Work::shard_gids for the caller).
 __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, int h, const uint32_t *fkeys,
                                          const int32_t *fids) {
   const Marker mark{&S.ms};
   const ShardLinkDev &L = *w.link;
   const int tid = threadIdx.x, n = L.n_shards, ch = cell * G + h;
   const uint32_t epoch = *L.epoch + 1;
+  const unsigned long long tag = (unsigned long long)(epoch & 0xffu) << 56;
+  const int par = (int)(epoch & 1u);
   __syncthreads();  // this head's keys and ids are written
   for (int i = tid; i < TOPK; i += FT) {
-    const uint32_t k = fkeys[i];
-    const int32_t id = fids[i];
-    for (int p = 0; p < n; ++p) {
-      ShardRegion *R = reinterpret_cast<ShardRegion *>(L.peer[p]);
-      R->keys[L.rank][ch][i] = k;
-      R->ids[L.rank][ch][i] = id;
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    // cumulative: orders the CTA's pushes (before the barrier) before the flags
-    __threadfence_system();
+    const unsigned long long v = tag | ((unsigned long long)(fkeys[i] >> 16) << 40) | (uint32_t)fids[i];
     for (int p = 0; p < n; ++p)
-      st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_lists[L.rank][ch], epoch);
-    const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
-    if (!wait_flags(&mine->flag_lists[0][ch], SHARD_CELLS * G, n, epoch))
-      atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
+      st_relaxed_sys_u64(&reinterpret_cast<ShardRegion *>(L.peer[p])->ll[par][L.rank][ch][i], v);
   }
-  __syncthreads();
-  mark(M_XLIST);
-  // every shard's list of this (cell, head) into shared memory in one pass of
-  // independent loads (the peers wrote them into this GPU's region), as
-  // 64-bit merge keys; the binary searches below then touch shared memory
-  // only (searching global memory made each search a chain of dependent
-  // memory round trips, one chain per other shard)
+  // every shard's list of this (cell, head) into shared memory as 64-bit
+  // merge keys, each entry polled (bounded) until it carries this step's tag;
+  // the binary searches below then touch shared memory only
   const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
   unsigned long long *mk = reinterpret_cast<unsigned long long *>(S.big + 4096);  // [n][TOPK]
   static_assert(4096 + SHARD_MAX * TOPK * 8 <= BIG, "merge keys fit the staging area");
+  bool late = false;
   for (int c = tid; c < n * TOPK; c += FT) {
     const int s = c / TOPK, r = c - s * TOPK;
-    const uint32_t key = __ldcv(&R->keys[s][ch][r]);
-    const int32_t id = __ldcv(&R->ids[s][ch][r]);
-    mk[c] = key ? merge_key(key, r, L.begin[s] + id) : 0ull;
+    const unsigned long long *src = &R->ll[par][s][ch][r];
+    unsigned long long v = ld_relaxed_sys_u64(src);
+    for (long long polls = 0; (v & 0xff00000000000000ull) != tag; ++polls) {
+      if (polls > SHARD_WAIT_POLLS) { late = true; break; }
+      __nanosleep(64);
+      v = ld_relaxed_sys_u64(src);
+    }
+    const uint32_t score = (uint32_t)(v >> 40) & 0xffffu;
+    mk[c] = score ? merge_key(score << 16, r, L.begin[s] + (int32_t)(uint32_t)v) : 0ull;
   }
+  if (late) atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
   __syncthreads();
+  mark(M_XLIST);
   int32_t *gout = w.shard_gids + (size_t)ch * TOPK;
   int valid = 0;
   for (int c = tid; c < n * TOPK; c += FT) {
@@ -836,12 +847,21 @@ __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, 
       }
       rank += lo;
     }
-    if (rank < TOPK) gout[rank] = gid;
+    if (rank < TOPK) {
+      gout[rank] = gid;
+      for (int d = 0; d < CL; ++d)
+        st_async_b32(remote(&S.win[h][rank], (uint32_t)d), remote(&S.mb_win, (uint32_t)d), (uint32_t)gid);
+    }
     ++valid;
   }
   int total;
   block_exclusive_scan(valid, &total);
-  for (int i = total + tid; i < TOPK; i += FT) gout[i] = -1;  // fewer than 100 candidates in the group
+  // fewer than 100 candidates in the group: the remaining ranks are -1
+  for (int i = total + tid; i < TOPK; i += FT) {
+    gout[i] = -1;
+    for (int d = 0; d < CL; ++d)
+      st_async_b32(remote(&S.win[h][i], (uint32_t)d), remote(&S.mb_win, (uint32_t)d), 0xffffffffu);
+  }
 }
 
 // ------------------------------------------------------------ the kernel
@@ -1745,12 +1765,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       fold(nb, lane < nb ? dense_tok(gwa + (c0 + lane) * nwa) : 0, -1);
     }
   }
-  if (Lk) {
-    cluster_sync();  // the group's global winners are complete in global memory
-  } else {
-    if (tid == 0) mbar_expect_tx(&S.mb_win, G * TOPK * 4);
-    mbar_wait_cluster(&S.mb_win, 0u, &S.status);
-  }
+  // the step's winners (the group's merged ones when sequence-sharded) in S.win
+  if (tid == 0) mbar_expect_tx(&S.mb_win, G * TOPK * 4);
+  mbar_wait_cluster(&S.mb_win, 0u, &S.status);
   mark(M_S2SEL);
   {
     // the winners over all warps (and the dense zones too when they were
@@ -1769,14 +1786,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         } else {
           const int r = it - dense;
           my_head = r / TOPK;
-          if (Lk) {
-            // sharded: the group's global winners (-2: fewer than 100 in the group)
-            const int gid = __ldcg(w.shard_gids + (size_t)cell * G * TOPK + r);
-            if (gid >= 0) my_tok = gid;
-            else my_head = -2;
-          } else {
-            my_tok = S.win[r / TOPK][r - (r / TOPK) * TOPK];
-          }
+          my_tok = S.win[r / TOPK][r - (r / TOPK) * TOPK];
+          if (my_tok < 0) { my_tok = 0; my_head = -2; }  // sharded: fewer than 100 in the group
         }
       }
       fold(nb, my_tok, my_head);

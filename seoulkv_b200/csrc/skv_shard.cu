@@ -245,8 +245,12 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_shard_merge_p2p(ShardLinkDev 
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence_system();  // cumulative over the CTA's pushes
-    for (int p = 0; p < n; ++p) st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_lists[L.rank][ch], epoch);
+    // one release fence (cumulative over the CTA's pushes, which the barrier
+    // above ordered before it), then the flags as relaxed stores: a fence per
+    // flag (release stores) or a sequentially consistent fence costs several
+    // microseconds more per exchange
+    fence_acq_rel_sys();
+    for (int p = 0; p < n; ++p) st_relaxed_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_lists[L.rank][ch], epoch);
     const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
     s_ok = wait_flags(&mine->flag_lists[0][ch], SHARD_CELLS * G, n, epoch);
     if (!s_ok) atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
@@ -288,8 +292,8 @@ __global__ void __launch_bounds__(256) k_shard_combine_p2p(ShardLinkDev L, const
   }
   __syncthreads();
   if (d == 0) {
-    __threadfence_system();  // cumulative over the CTA's pushes
-    for (int p = 0; p < n; ++p) st_release_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_parts[L.rank][cell], epoch);
+    fence_acq_rel_sys();  // one release fence, cumulative over the CTA's pushes
+    for (int p = 0; p < n; ++p) st_relaxed_sys(&reinterpret_cast<ShardRegion *>(L.peer[p])->flag_parts[L.rank][cell], epoch);
     const ShardRegion *mine = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
     s_ok = wait_flags(&mine->flag_parts[0][cell], SHARD_CELLS, n, epoch);
     if (!s_ok) atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
