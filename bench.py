@@ -873,6 +873,23 @@ def main():
         no_window = {"mean_us": float(np.mean(t_nw)), "p50_us": float(np.median(t_nw)),
                      "p99_us": float(np.percentile(t_nw, 99)), "steps": int(len(t_nw))}
 
+    # the same kind of steps on a second instance of the layer without the
+    # lead cluster (the fused launch's extra cluster that runs a small
+    # synthetic cell ahead of the real cells, bringing the kernel's
+    # instructions into L2 before they need them), for comparison
+    no_lead = None
+    if eng.fused:
+        attn2 = SeoulKV4(device=device, k=k, v=v, index=index, config=SeoulKV4Config(debug=True, lead_cluster=False))
+        attn2.run(qs_host[0])
+        attn2.synchronize()
+        eng2 = attn2._engine
+        t_nl = _timed_steps(argparse.Namespace(warmup=args.warmup, steps=min(args.steps, 200)), device, flush,
+                            lambda i: eng2.step(qbits[i].data_ptr(), True, stream.cuda_stream))
+        eng2.sync()
+        attn2.close()
+        no_lead = {"mean_us": float(np.mean(t_nl)), "p50_us": float(np.median(t_nl)),
+                   "p99_us": float(np.percentile(t_nl, 99)), "steps": int(len(t_nl))}
+
     # per-kernel device times (non-graph launches, L2 flushed before each)
     prof = {}
     for _ in range(5):
@@ -986,6 +1003,11 @@ def main():
                           "what": "upper+lower centroid planes of the layer held in persisting L2 by an "
                                   "access-policy window (the flush evicts normal lines only)",
                           "without_window": no_window},
+            "lead_cluster": {"on": bool(eng.fused),
+                             "what": "one extra 16-CTA cluster per fused launch decodes a small synthetic cell "
+                                     "ahead of the real cells, so the kernel's instructions are in L2 when they "
+                                     "reach them (the flush evicts them before every step)",
+                             "without_lead": no_lead},
             "live_counts": {"survivors_max": st.survivors_max, "pool_min": st.pool_min, "pool_max": st.pool_max,
                             "union15_max": st.union15_max, "union16_max": st.union16_max},
             "parity": parity, "cpu_baseline": cpu_line, "e2e": e2e, "clocks": clk,

@@ -52,6 +52,13 @@ extern "C" {
 /* SkvDesc.flags */
 #define SKV_FLAG_STAGED 1         /* run the 14-kernel staged path even where the
                                      single-kernel cluster path applies      */
+#define SKV_FLAG_NO_LEAD 2        /* fused path without its lead cluster: one
+                                     extra 16-CTA cluster in every launch that
+                                     decodes a small built-in synthetic cell,
+                                     runs ahead of the real cells and so brings
+                                     the kernel's instructions into L2 before
+                                     they need them (results do not depend on
+                                     it; off only to measure it)             */
 
 typedef struct SkvDesc {
     int32_t n_slots;          /* independent caches decoded per run        */
@@ -215,6 +222,9 @@ int skv_context(void *handle, int32_t *context);
 #define SKV_STAGE_MATES 17      /* int32 per cell offsets[nc] mates, cell after cell     */
 #define SKV_STAGE_LABELS 18     /* int32 [4][T][2] spill-2 lists of tokens from the first local window on
                                    (engines with appends; -1 below the window)     */
+#define SKV_STAGE_LEAD_COUNTS 19 /* int32 [NCOUNT = 8] counters of the lead cluster's synthetic
+                                   cell (SKV_FLAG_NO_LEAD): tags, pool, selected, postings, status,
+                                   union, candidates; slot is ignored (must be valid) */
 int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
                    size_t *written);
 

@@ -23,7 +23,7 @@ SKV_E_CAPACITY = -3
 
 STAGE = dict(counts=0, thresh=1, tags=2, selected=3, pool=4, u15=5, cand=6, final_pos=7, lohi=8,
              prefix2=9, residual2=10, residual4=11, kv8=12, key_scale=13, final_keys=14, offsets=15,
-             values=16, mates=17, labels=18)
+             values=16, mates=17, labels=18, lead_counts=19)
 
 EXPORTS = (
     "skv_last_error", "skv_version", "skv_create", "skv_destroy", "skv_upload_index",
@@ -36,6 +36,7 @@ EXPORTS = (
 )
 
 SKV_FLAG_STAGED = 1
+SKV_FLAG_NO_LEAD = 2
 # Engines created without an explicit ``staged=`` use the staged (14-kernel)
 # path when this is true; tests flip it to run both paths through the API.
 FORCE_STAGED = False
@@ -168,14 +169,16 @@ class Engine:
     """One engine instance: ``n_slots`` caches x 4 KV heads on one CUDA device."""
 
     def __init__(self, *, n_slots: int, context: int, sink: int, local: int, nc: int,
-                 capacity: int, device: int, staged: bool | None = None, max_context: int = 0):
+                 capacity: int, device: int, staged: bool | None = None, max_context: int = 0,
+                 lead: bool = True):
         self.lib = load()
         self.n_slots, self.context, self.nc, self.capacity = n_slots, context, nc, capacity
         self.sink, self.local, self.device = sink, local, device
         self.max_context = max_context or context
         staged = FORCE_STAGED if staged is None else staged
         desc = SkvDesc(n_slots=n_slots, context=context, sink=sink, local=local, nc=nc,
-                       stage15_capacity=capacity, device=device, flags=SKV_FLAG_STAGED if staged else 0,
+                       stage15_capacity=capacity, device=device,
+                       flags=(SKV_FLAG_STAGED if staged else 0) | (0 if lead else SKV_FLAG_NO_LEAD),
                        max_context=max_context)
         h = ctypes.c_void_p()
         check(self.lib.skv_create(ctypes.byref(desc), ctypes.byref(h)), "skv_create")

@@ -148,7 +148,8 @@ class SeoulKV4:
             raise ValueError("all four index cells must have the same centroid count")
         eng = _native.Engine(n_slots=1, context=zones.context, sink=zones.sink, local=zones.local,
                              nc=nc, capacity=self._config.stage15_capacity, device=self._device_index,
-                             max_context=self._max_context if self._max_context > zones.context else 0)
+                             max_context=self._max_context if self._max_context > zones.context else 0,
+                             lead=self._config.lead_cluster)
         try:
             eng.upload_index(0, [device_view(c, p) for c, p in zip(cells, self._nprobe)])
             k, v = self._host_kv

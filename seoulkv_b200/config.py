@@ -48,7 +48,10 @@ class SeoulKV4Config:
     ``l2_resident`` keeps the index's centroid planes in the persisting part
     of L2 across steps (the reference keeps its coarse centroid plane in
     on-chip SRAM); it applies where the device's persisting set-aside can hold
-    them, and is a no-op otherwise.
+    them, and is a no-op otherwise.  ``lead_cluster`` adds to every fused
+    launch one cluster that decodes a small synthetic cell ahead of the real
+    ones, so that the kernel's instructions are in L2 when the real cells
+    reach them; results do not depend on it (off only to measure it).
     """
 
     stage15_capacity: int = 13056
@@ -56,6 +59,7 @@ class SeoulKV4Config:
     nprobe: int | tuple[int, ...] | None = None
     max_context: int | None = None
     l2_resident: bool = True
+    lead_cluster: bool = True
 
     def __post_init__(self):
         n = self.stage15_capacity
@@ -65,6 +69,8 @@ class SeoulKV4Config:
             raise TypeError("debug must be a bool")
         if type(self.l2_resident) is not bool:
             raise TypeError("l2_resident must be a bool")
+        if type(self.lead_cluster) is not bool:
+            raise TypeError("lead_cluster must be a bool")
         if self.nprobe is not None:
             validate_nprobe(self.nprobe if type(self.nprobe) is int else tuple(self.nprobe), 512)
             if not isinstance(self.nprobe, int):

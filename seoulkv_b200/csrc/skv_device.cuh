@@ -114,9 +114,10 @@ struct CellDev {
   const uint8_t *residual4;          // [T][128]
   const float *key_scale;            // [256]
   const uint8_t *kv8;                // [T][512] FP8 e4m3 [K | V]
+  const uint16_t *q;                 // the lead cell's own query [4][256] (null: the slot's query)
   int32_t nc, nprobe;
   float lam;
-  int32_t pad;
+  int32_t context;                   // the lead cell's own context (0: the engine's)
 };
 
 // Workspace: one base pointer per buffer, indexed by cell inside kernels.
@@ -124,6 +125,7 @@ struct CellDev {
 // a step clears them again for the next one.
 struct Work {
   int n_cells, n_slots, T, sink, local, nc, cap;
+  int lead;                 // 1: the fused launch carries the lead cluster (cell n_cells, launched first)
   int chunks_nc;            // ceil(nc / CHUNK)
   int chunks_surv;          // ceil(nc / SCHUNK)
   int chunks_pool;          // ceil(cap / CHUNK)

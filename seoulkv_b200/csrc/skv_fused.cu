@@ -873,16 +873,22 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, t = lane & 3;
   const int hA = t >> 1, hB = 2 + hA;
   const int rank = (int)cluster_rank();
-  const int cell = blockIdx.y, slot = cell >> 2, g = cell & 3;
+  // the lead cluster (launched first: blockIdx.y 0) decodes the engine's
+  // small synthetic cell n_cells; its outputs are never read
+  const int cell = w.lead ? (blockIdx.y == 0 ? w.n_cells : (int)blockIdx.y - 1) : (int)blockIdx.y;
+  const bool lead = cell == w.n_cells, timed = w.cta_ts && !lead;
+  const int slot = cell >> 2, g = cell & 3;
   if (tid < (int)(sizeof(CellDev) / 4))
     reinterpret_cast<uint32_t *>(&S.cell)[tid] = reinterpret_cast<const uint32_t *>(w.cells + cell)[tid];
   __syncthreads();
   const CellDev &c = S.cell;
-  const int nc = w.nc, cap = w.cap;
+  // nc bounds this cell's loops (the lead cell's is small); ncs is the
+  // workspace's per-cell stride
+  const int nc = c.nc, ncs = w.nc, cap = w.cap;
   const int per = ((nc + CL * 32 - 1) / (CL * 32)) * 32;
   const int r0 = min(nc, rank * per), r1 = min(nc, r0 + per), nrows = r1 - r0;
   const uint32_t P = (uint32_t)c.nprobe;
-  if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank)] = (long long)t_entry;
+  if (timed && tid == 0) w.cta_ts[2 * (cell * CL + rank)] = (long long)t_entry;
   // marks: SM clocks of CTA 0 of cell 0 (Work::phase_ts), or global-timer
   // marks of every CTA of cell 0 after the entry/exit stamps (Work::cta_ts)
   long long *mts = nullptr;
@@ -901,7 +907,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   // the generic source pointers and would otherwise serialise the loads)
   {
     static_assert(PER_MAX == 4 * FT && 4 * D == 2 * FT && PER_MAX / 32 <= FT && D <= FT, "load shapes");
-    const uint16_t *qsrc = w.q + ((size_t)slot * 16 + g * 4) * D;
+    const uint16_t *qsrc = c.q ? c.q : w.q + ((size_t)slot * 16 + g * 4) * D;
     uint16_t qv[2], rv[4];
     int ov[5];
     float ks = 0.0f, s4 = 0.0f, fs[2];
@@ -950,7 +956,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 #pragma unroll
     for (int k = 0; k < 2; ++k) S.fsc[tid + k * FT] = fs[k];
     // the slice's selected-cluster bits, set by whichever CTA scores a survivor (P5)
-    if (tid < (nrows >> 5)) w.selbits[(size_t)cell * (nc >> 5) + (r0 >> 5) + tid] = 0u;
+    if (tid < (nrows >> 5)) w.selbits[(size_t)cell * (ncs >> 5) + (r0 >> 5) + tid] = 0u;
   }
   for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0u;  // (P1 adds the coarse first round)
   __syncthreads();
@@ -1051,7 +1057,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       mbar_wait(&S.mbar[(tiles * 16 - 1) / SLICE_CHUNK], 0);
       mark(M_SLICE);
     }
-    uint16_t *glo = w.lo + (size_t)cell * G * nc, *ghi = w.hi + (size_t)cell * G * nc;
+    uint16_t *glo = w.lo + (size_t)cell * G * ncs, *ghi = w.hi + (size_t)cell * G * ncs;
     for (int tile = warp; tile < tiles; tile += FW) {
       if (!mbar_wait(&S.mbar[(tile * 16) / SLICE_CHUNK], 0)) atomicOr(reinterpret_cast<unsigned *>(&S.status), ST_TIMEOUT);
       long long dsum[2];
@@ -1071,8 +1077,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         S.b.c.lo[h][lr] = lo;
         atomicAdd(&S.hist[h * 256 + (lo >> 8)], 1u);  // the coarse selection's first round
         S.b.c.hi[h][lr] = hi;
-        glo[(size_t)h * nc + row] = lo;
-        ghi[(size_t)h * nc + row] = hi;
+        glo[(size_t)h * ncs + row] = lo;
+        ghi[(size_t)h * ncs + row] = hi;
       }
     }
   }
@@ -1140,7 +1146,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   for (int k = tid; k < nsurv; k += FT) {
     const int lr = S.sidx[k], p = surv_base + k, d = p / L;
     const uint32_t m = S.smask[k];
-    w.tags[(size_t)cell * nc + p] = (uint32_t)(r0 + lr) | (m << 28);
+    w.tags[(size_t)cell * ncs + p] = (uint32_t)(r0 + lr) | (m << 28);
     st_async_b32(remote(&S.shin[p - d * L], (uint32_t)d), remote(&S.mb_sh, (uint32_t)d), (uint32_t)(r0 + lr) | (m << 16));
   }
   if (tid == 0) mbar_expect_tx(&S.mb_sh, (uint32_t)nsh * 4u);
@@ -1205,7 +1211,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     }
     if (tid < 4 && S.ctl.own[tid])
       w.thr[(size_t)cell * 16 + T_FINE * G + tid] = S.ctl.th[tid] ? S.ctl.th[tid] : 0xffffffffu;
-    uint32_t *selbits = w.selbits + (size_t)cell * (nc >> 5);
+    uint32_t *selbits = w.selbits + (size_t)cell * (ncs >> 5);
     for (int k = tid; k < nsh; k += FT) {
       bool s = false;
 #pragma unroll
@@ -1285,7 +1291,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   int nkept = 0;
   {
     int *klist = reinterpret_cast<int *>(S.big);
-    const uint32_t *selbits = w.selbits + (size_t)cell * (nc >> 5);
+    const uint32_t *selbits = w.selbits + (size_t)cell * (ncs >> 5);
     for (int p0 = 0; p0 < npost; p0 += FT * 4) {
       int jj[4], cid[4], mate[4], tok[4], keep[4];
       if (p0 == 0) {
@@ -1654,7 +1660,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       fkeys[tid] = 0u;
       wtok[tid] = 0;
     }
-    if (w.link) {
+    if (w.link && !lead) {
       shard_lists(w, S, cell, h, fkeys, fids);
     } else {
       // head h's winners, in rank order, into every CTA's S.win[h]
@@ -1669,8 +1675,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   }
   // --------------------------------------------------------------- P13
   // (the block closes after the combine below)
-  const ShardLinkDev *Lk = w.link;
-  const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local, T = Lk ? Lk->total : context_of(w);
+  const ShardLinkDev *Lk = lead ? nullptr : w.link;
+  const int sink = Lk ? Lk->sink : w.sink, local = Lk ? Lk->local : w.local;
+  const int T = Lk ? Lk->total : (c.context ? c.context : context_of(w));
   const int dense = sink + local;
   const float qscale = 0.0625f * 1.4426950408889634f;  // 1/sqrt(256), log2(e)
   float qv[G][8];
@@ -1859,13 +1866,13 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         L += ls[r] * e;
         O += os[r] * e;
       }
-      w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
+      if (!lead) w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
     }
   }
   mark(M_ATTN);
   if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
   cluster_sync();  // no CTA leaves while its shared memory may still be read
-  if (w.link && rank == 0 && tid == 0) {
+  if (w.link && !lead && rank == 0 && tid == 0) {
     // the last cluster of the step to finish advances the group's step
     // counter (every cluster read it in P12, before this barrier)
     const ShardLinkDev *Lk = w.link;
@@ -1874,7 +1881,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       *Lk->epoch += 1u;
     }
   }
-  if (w.cta_ts && tid == 0) w.cta_ts[2 * (cell * CL + rank) + 1] = (long long)global_ns();
+  if (timed && tid == 0) w.cta_ts[2 * (cell * CL + rank) + 1] = (long long)global_ns();
 }
 
 const char *const kMarkNames[M_NTAGS] = {
@@ -1898,7 +1905,7 @@ cudaError_t prepare_fused_attributes() {
 
 cudaError_t launch_fused(const Work &w, cudaStream_t st, const cudaAccessPolicyWindow *win) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(CL, w.n_cells, 1);
+  cfg.gridDim = dim3(CL, w.n_cells + w.lead, 1);
   cfg.blockDim = dim3(FT, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
