@@ -105,7 +105,8 @@ struct MarkState {
 
 struct FusedSmem {
   uint32_t frag[3 * FRAG_ROW];     // int8 digit fragments of the three operand rows
-  uint32_t hist[4 * 256];          // this CTA's selection histogram (4 heads x 256 bins)
+  uint32_t hist[4 * 256];          // selection histogram: word 128 h + b / 2 holds bins b, b + 1 of head h as
+                                   // 16-bit counts (the cluster selections); 256 plain bins (P12)
   alignas(16) uint32_t tab[CL][128];  // CTA h < 4: each source CTA's counts of head h's bins (16-bit pairs)
   uint32_t sum[256];               // CTA h < 4: head h's bins summed over the cluster
   alignas(16) SelRes res[4];       // the owners' results of the latest selection round
@@ -401,8 +402,20 @@ __device__ __forceinline__ uint32_t select_key(const FusedSmem &S, int kind, int
   }
 }
 
+// One count in bin b (0..255) of head h of a selection histogram: bins b and
+// b + 1 (b even) share a word as 16-bit counts (a CTA holds at most 2048 keys
+// per head), the layout the histogram is pushed in.
+__device__ __forceinline__ void hist_add(uint32_t *hist, int h, uint32_t b) {
+  atomicAdd(&hist[h * 128 + (b >> 1)], 1u << ((b & 1u) << 4));
+}
+
 // One radix-histogram pass over this CTA's keys of `KIND`: keys with
-// (key & mk[h]) == pf[h] add one to bin h*256 + digit (bits sh..sh+7).
+// (key & mk[h]) == pf[h] add one to bin digit (bits sh..sh+7) of head h.
+// Zero keys (a survivor position without head h, a pool position outside
+// the union) are not counted: they lie below every real key, so the K-th
+// largest key is the same whenever K real keys exist, and otherwise no bin
+// is found and the threshold is 0 either way (the step's failure status);
+// counting them only piled atomics onto bin 0.
 // One shared-memory atomic per key: measured on B200 with BF16-like keys
 // crowded into a few bins, this is faster than run-length counting in
 // registers or per-warp aggregation (the atomic unit combines lanes of one
@@ -418,8 +431,8 @@ __device__ __forceinline__ void hist_pass(uint32_t *hist, const FusedSmem &S, in
       for (int h = 0; h < 4; ++h) {
         const uint32_t two = *reinterpret_cast<const uint32_t *>(&S.b.c.lo[h][i]);
         const uint32_t v0 = two << 16, v1 = two & 0xffff0000u;
-        if ((v0 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v0 >> sh) & 255u)], 1u);
-        if ((v1 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v1 >> sh) & 255u)], 1u);
+        if ((v0 & mk[h]) == pf[h]) hist_add(hist, h, (v0 >> sh) & 255u);
+        if ((v1 & mk[h]) == pf[h]) hist_add(hist, h, (v1 >> sh) & 255u);
       }
     }
   } else {
@@ -444,8 +457,8 @@ __device__ __forceinline__ void hist_pass(uint32_t *hist, const FusedSmem &S, in
           v0 = (fl & 0xffu) ? (sc << 16) | (0xffffu - (uint32_t)(q0 + i)) : 0u;
           v1 = (fl >> 8) ? (sc & 0xffff0000u) | (0xffffu - (uint32_t)(q0 + i + 1)) : 0u;
         }
-        if ((v0 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v0 >> sh) & 255u)], 1u);
-        if (two && (v1 & mk[h]) == pf[h]) atomicAdd(&hist[h * 256 + ((v1 >> sh) & 255u)], 1u);
+        if (v0 && (v0 & mk[h]) == pf[h]) hist_add(hist, h, (v0 >> sh) & 255u);
+        if (two && v1 && (v1 & mk[h]) == pf[h]) hist_add(hist, h, (v1 >> sh) & 255u);
       }
     }
   }
@@ -486,8 +499,8 @@ __device__ __forceinline__ bool warp_find_regs(const uint32_t (&c)[8], uint32_t 
 
 // K-th largest of the cluster's keys (select_key of `kind`) for each of the
 // four heads; nbits (16 or 32) top bits of the 32-bit keys are significant.
-// With `pre`, S.hist already holds this CTA's first-round histogram (all
-// keys, built while the keys were computed).
+// With `pre`, S.hist already holds this CTA's first-round histogram (its
+// non-zero keys, counted while the keys were computed).
 // On return S.ctl.th[h] holds a threshold: the keys >= it, over the whole
 // cluster, are
 //   exact (16 bits):  those >= the K-th largest key;
@@ -530,7 +543,7 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     S.ctl.own[tid] = rank == 0;
   }
   if (!pre)
-    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0;
+    for (int e = tid; e < 4 * 128; e += FT) S.hist[e] = 0;
   __syncthreads();
   for (int sh = 24; sh >= 16; sh -= 8) {
     int live[4], nlive = 0;
@@ -556,17 +569,16 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     }
     __syncthreads();
     mark(M_HIST);
-    // this CTA's counts (< 2^16: nloc <= 2048) of each live head to its owner
-    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+    // this CTA's counts of each live head (16-bit pairs, as counted) to the
+    // head's owner; each word is read and then cleared for the next round by
+    // the one thread that pushes it
     const int sh_h = tid >> 5, sj = tid & 31;
     if (tid < 128 && live[sh_h]) {
-      const uint32_t *c = S.hist + sh_h * 256 + 8 * sj;
-      pk = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
-    }
-    __syncthreads();  // counts read
-    if (tid < 128 && live[sh_h])
+      uint4 *hp = reinterpret_cast<uint4 *>(S.hist + sh_h * 128 + 4 * sj);
+      const uint4 pk = *hp;
       st_async_v4(remote(&S.tab[rank][4 * sj], (uint32_t)sh_h), remote(&S.mb_in, (uint32_t)sh_h), pk);
-    for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0u;  // the next round's histogram
+      *hp = make_uint4(0u, 0u, 0u, 0u);
+    }
     if (rank < 4 && live[rank]) {
       // owner of head h = rank
       const int h = rank;
@@ -668,6 +680,10 @@ __device__ __noinline__ void cluster_select(FusedSmem &S, int nloc, uint32_t K, 
     S.ph_in = ph_in;
     S.ph_res = ph_res;
   }
+  // a clear histogram for the next selection's first round, which the next
+  // scoring phase may build on the way (heads done before any round still
+  // hold a prebuilt first round)
+  for (int e = tid; e < 4 * 128; e += FT) S.hist[e] = 0u;
   __syncthreads();
 }
 
@@ -958,7 +974,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     // the slice's selected-cluster bits, set by whichever CTA scores a survivor (P5)
     if (tid < (nrows >> 5)) w.selbits[(size_t)cell * (ncs >> 5) + (r0 >> 5) + tid] = 0u;
   }
-  for (int e = tid; e < 4 * 256; e += FT) S.hist[e] = 0u;  // (P1 adds the coarse first round)
+  for (int e = tid; e < 4 * 128; e += FT) S.hist[e] = 0u;  // (P1 adds the coarse first round)
   __syncthreads();
   mark(M_ISSUE);
   static_assert(FW == 16, "12 operand-row warps + 4 norm warps");
@@ -1075,7 +1091,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         const uint16_t lo = (uint16_t)ord16(bf16_score(__fsub_rn(v, margin)));
         const uint16_t hi = (uint16_t)ord16(bf16_score(__fadd_rn(v, margin)));
         S.b.c.lo[h][lr] = lo;
-        atomicAdd(&S.hist[h * 256 + (lo >> 8)], 1u);  // the coarse selection's first round
+        hist_add(S.hist, h, lo >> 8u);  // the coarse selection's first round
         S.b.c.hi[h][lr] = hi;
         glo[(size_t)h * ncs + row] = lo;
         ghi[(size_t)h * ncs + row] = hi;
@@ -1188,6 +1204,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
             if ((mk >> h) & 1)
               key = ord_fused(bf16_score(__fmul_rn(exact_to_float(dsum[kk], kk ? scB : scA), fs)), (uint32_t)pos);
             S.b.fkey[h][k] = key;
+            if (key) hist_add(S.hist, h, key >> 24);  // the Fine selection's first round
           }
         }
       }
@@ -1198,7 +1215,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // ---------------------------------------------------------------- P5
   {
-    cluster_select(S, nsh, P, 32, false, KEY_FINE, 0);
+    cluster_select(S, nsh, P, 32, false, KEY_FINE, 0, true);
   }
   mark(M_FSEL);
   uint32_t st = 0;
@@ -1388,8 +1405,11 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
           const int row = (t & 1) ? r8 : rg;
           if (row < nb) {
 #pragma unroll
-            for (int k = 0; k < 2; ++k)
-              S.b.p.sc15[k ? hB : hA][b0 + row] = (uint16_t)ord16(bf16_score(exact_to_float(dsum[k], k ? scB : scA)));
+            for (int k = 0; k < 2; ++k) {
+              const uint32_t sc = ord16(bf16_score(exact_to_float(dsum[k], k ? scB : scA)));
+              S.b.p.sc15[k ? hB : hA][b0 + row] = (uint16_t)sc;
+              hist_add(S.hist, k ? hB : hA, sc >> 8);  // the Stage-1.5 selection's first round
+            }
           }
         }
       }
@@ -1423,7 +1443,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
 
   // ---------------------------------------------------------------- P8
   {
-    cluster_select(S, m15, (uint32_t)min(UNION15, n15), 32, false, KEY_S15, q0);
+    cluster_select(S, m15, (uint32_t)min(UNION15, n15), 32, false, KEY_S15, q0, true);
   }
   mark(M_S15SEL);
   int nu;
