@@ -52,6 +52,11 @@ extern "C" {
 /* SkvDesc.flags */
 #define SKV_FLAG_STAGED 1         /* run the 14-kernel staged path even where the
                                      single-kernel cluster path applies      */
+#define SKV_FLAG_TRACE 4          /* the fused path writes every stage's intermediates
+                                     (coarse bounds, survivor tags, selected clusters,
+                                     pool, unions) for skv_read_stage; without it
+                                     only the counters, thresholds and final ranks
+                                     are written (the staged path always writes them) */
 #define SKV_FLAG_NO_LEAD 2        /* fused path without its lead cluster: one
                                      extra 16-CTA cluster in every launch that
                                      decodes a small built-in synthetic cell,

@@ -37,6 +37,7 @@ EXPORTS = (
 
 SKV_FLAG_STAGED = 1
 SKV_FLAG_NO_LEAD = 2
+SKV_FLAG_TRACE = 4
 # Engines created without an explicit ``staged=`` use the staged (14-kernel)
 # path when this is true; tests flip it to run both paths through the API.
 FORCE_STAGED = False
@@ -170,7 +171,7 @@ class Engine:
 
     def __init__(self, *, n_slots: int, context: int, sink: int, local: int, nc: int,
                  capacity: int, device: int, staged: bool | None = None, max_context: int = 0,
-                 lead: bool = True):
+                 lead: bool = True, trace: bool = False):
         self.lib = load()
         self.n_slots, self.context, self.nc, self.capacity = n_slots, context, nc, capacity
         self.sink, self.local, self.device = sink, local, device
@@ -178,7 +179,8 @@ class Engine:
         staged = FORCE_STAGED if staged is None else staged
         desc = SkvDesc(n_slots=n_slots, context=context, sink=sink, local=local, nc=nc,
                        stage15_capacity=capacity, device=device,
-                       flags=(SKV_FLAG_STAGED if staged else 0) | (0 if lead else SKV_FLAG_NO_LEAD),
+                       flags=(SKV_FLAG_STAGED if staged else 0) | (0 if lead else SKV_FLAG_NO_LEAD)
+                       | (SKV_FLAG_TRACE if trace else 0),
                        max_context=max_context)
         h = ctypes.c_void_p()
         check(self.lib.skv_create(ctypes.byref(desc), ctypes.byref(h)), "skv_create")

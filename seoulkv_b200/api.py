@@ -149,7 +149,7 @@ class SeoulKV4:
         eng = _native.Engine(n_slots=1, context=zones.context, sink=zones.sink, local=zones.local,
                              nc=nc, capacity=self._config.stage15_capacity, device=self._device_index,
                              max_context=self._max_context if self._max_context > zones.context else 0,
-                             lead=self._config.lead_cluster)
+                             lead=self._config.lead_cluster, trace=self._config.trace_stages)
         try:
             eng.upload_index(0, [device_view(c, p) for c, p in zip(cells, self._nprobe)])
             k, v = self._host_kv

@@ -124,7 +124,7 @@ class SeoulKV4Batch:
         eng = _native.Engine(n_slots=self.n, context=context, sink=sink, local=local, nc=self._nc,
                              capacity=self._config.stage15_capacity, device=self._device_index,
                              max_context=self._max_context if self._max_context > context else 0,
-                             lead=self._config.lead_cluster)
+                             lead=self._config.lead_cluster, trace=self._config.trace_stages)
         try:
             for s, (k, v, index) in enumerate(self._caches):
                 eng.upload_index(s, [device_view(c, p) for c, p in zip(index.cells(), self._nprobe[s])])

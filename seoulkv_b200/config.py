@@ -52,6 +52,9 @@ class SeoulKV4Config:
     launch one cluster that decodes a small synthetic cell ahead of the real
     ones, so that the kernel's instructions are in L2 when the real cells
     reach them; results do not depend on it (off only to measure it).
+    ``trace_stages`` makes the single-kernel path also write every stage's
+    intermediates (coarse bounds, survivor tags, selected clusters, pool,
+    unions) for stage-by-stage inspection; decoding does not need them.
     """
 
     stage15_capacity: int = 13056
@@ -60,6 +63,7 @@ class SeoulKV4Config:
     max_context: int | None = None
     l2_resident: bool = True
     lead_cluster: bool = True
+    trace_stages: bool = False
 
     def __post_init__(self):
         n = self.stage15_capacity
@@ -71,6 +75,8 @@ class SeoulKV4Config:
             raise TypeError("l2_resident must be a bool")
         if type(self.lead_cluster) is not bool:
             raise TypeError("lead_cluster must be a bool")
+        if type(self.trace_stages) is not bool:
+            raise TypeError("trace_stages must be a bool")
         if self.nprobe is not None:
             validate_nprobe(self.nprobe if type(self.nprobe) is int else tuple(self.nprobe), 512)
             if not isinstance(self.nprobe, int):

@@ -126,6 +126,7 @@ struct CellDev {
 struct Work {
   int n_cells, n_slots, T, sink, local, nc, cap;
   int lead;                 // 1: the fused launch carries the lead cluster (cell n_cells, launched first)
+  int trace;                // 1: the fused kernel writes every stage's intermediates (SKV_FLAG_TRACE)
   int chunks_nc;            // ceil(nc / CHUNK)
   int chunks_surv;          // ceil(nc / SCHUNK)
   int chunks_pool;          // ceil(cap / CHUNK)

@@ -556,6 +556,7 @@ int skv_create(const SkvDesc *d, void **handle) {
   w.phase_ts = nullptr;
   w.cta_ts = nullptr;
   e->fused = !(d->flags & SKV_FLAG_STAGED) && fused_supported(w);
+  w.trace = (d->flags & SKV_FLAG_TRACE) ? 1 : 0;
   if (e->fused) TRY(prepare_fused_attributes() ? fail(SKV_E_CUDA, "fused kernel attributes") : 0);
   // (the lead cell's buffers use the workspace's per-cell strides: nc >= 512)
   if (e->fused && !(d->flags & SKV_FLAG_NO_LEAD) && d->nc >= 512) TRY(build_lead_cell(e));
@@ -1119,6 +1120,10 @@ int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t 
   const Work &w = e->work;
   const void *src = nullptr;
   size_t n = 0;
+  if (e->fused && !w.trace &&
+      (which == SKV_STAGE_LOHI || which == SKV_STAGE_TAGS || which == SKV_STAGE_SELECTED ||
+       which == SKV_STAGE_POOL || which == SKV_STAGE_U15 || which == SKV_STAGE_CAND))
+    return fail(SKV_E_STATE, "this stage's intermediates need an engine created with SKV_FLAG_TRACE");
   switch (which) {
     case SKV_STAGE_COUNTS: src = w.counts + c0 * NCOUNT; n = G * NCOUNT * 4; break;
     case SKV_STAGE_LEAD_COUNTS:

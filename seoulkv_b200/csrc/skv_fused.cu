@@ -1093,8 +1093,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         S.b.c.lo[h][lr] = lo;
         hist_add(S.hist, h, lo >> 8u);  // the coarse selection's first round
         S.b.c.hi[h][lr] = hi;
-        glo[(size_t)h * ncs + row] = lo;
-        ghi[(size_t)h * ncs + row] = hi;
+        if (w.trace) {
+          glo[(size_t)h * ncs + row] = lo;
+          ghi[(size_t)h * ncs + row] = hi;
+        }
       }
     }
   }
@@ -1162,7 +1164,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   for (int k = tid; k < nsurv; k += FT) {
     const int lr = S.sidx[k], p = surv_base + k, d = p / L;
     const uint32_t m = S.smask[k];
-    w.tags[(size_t)cell * ncs + p] = (uint32_t)(r0 + lr) | (m << 28);
+    if (w.trace) w.tags[(size_t)cell * ncs + p] = (uint32_t)(r0 + lr) | (m << 28);
     st_async_b32(remote(&S.shin[p - d * L], (uint32_t)d), remote(&S.mb_sh, (uint32_t)d), (uint32_t)(r0 + lr) | (m << 16));
   }
   if (tid == 0) mbar_expect_tx(&S.mb_sh, (uint32_t)nsh * 4u);
@@ -1183,7 +1185,30 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         const uint8_t *src = (part < 4 ? c.upper : c.lower) + (size_t)cid * 64 + (part & 3) * 16;
         cp16(S.big + rr * STRIDE_FINE + part * 16, src);
       }
+      // the share's CSR ranges travel with the rows (P5 lists the selected
+      // clusters from them without a dependent global load): start into
+      // S.offs, length into S.resid (both free since P3; a length that does
+      // not fit 16 bits is marked 0xffff and read again in P5)
+      static_assert(BATCH_FINE <= 2 * FT, "two share survivors per thread");
+      int cb[2] = {0, 0}, ce[2] = {0, 0};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = tid + j * FT;
+        if (k < nb) {
+          const int cid = (int)(S.shin[b0 + k] & 0xffffu);
+          cb[j] = __ldg(c.offsets + cid);
+          ce[j] = __ldg(c.offsets + cid + 1);
+        }
+      }
       cp_wait_all();
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = tid + j * FT;
+        if (k < nb) {
+          S.offs[b0 + k] = cb[j];
+          S.resid[b0 + k] = (uint16_t)min(ce[j] - cb[j], 0xffff);
+        }
+      }
       __syncthreads();
       if (b0 == 0) mark(M_FGATHER);
       const int tiles = (nb + 15) >> 4;
@@ -1258,8 +1283,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       len[j] = 0;
       if (f[j]) {
         const int cid = (int)(S.shin[i0 + j] & 0xffffu);
-        const int b = __ldg(c.offsets + cid);
-        len[j] = __ldg(c.offsets + cid + 1) - b;
+        const int b = S.offs[i0 + j];  // (P4)
+        len[j] = S.resid[i0 + j] < 0xffffu ? (int)S.resid[i0 + j] : __ldg(c.offsets + cid + 1) - b;
         S.b.s.slist[r] = (uint16_t)cid;
         S.b.s.soff[r] = b;
         psum += len[j];
@@ -1300,8 +1325,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   }
   exchange_wait(S);
   const int sel_base = before(S, 0, rank), nsel_all = total(S, 0), npost_all = total(S, 1);
-  for (int k = tid; k < nsel; k += FT)
-    if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = S.b.s.slist[k];
+  if (w.trace)
+    for (int k = tid; k < nsel; k += FT)
+      if (sel_base + k < SEL_MAX) w.sel[(size_t)cell * SEL_MAX + sel_base + k] = S.b.s.slist[k];
   mark(M_SELX);
 
   // ---------------------------------------------------------------- P6
@@ -1353,7 +1379,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     int32_t *pool = w.pool + (size_t)cell * cap;
     for (int k = tid; k < nkept && k < KMAX; k += FT) {
       const int p = kept_base + k;
-      if (p < cap) pool[p] = klist[k];
+      if (w.trace && p < cap) pool[p] = klist[k];
       if (p < n15) {
         const int d = p / pc;
         st_async_b32(remote(&S.b.p.tok[p - d * pc], (uint32_t)d), remote(&S.mb_pool, (uint32_t)d), (uint32_t)klist[k]);
@@ -1507,7 +1533,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   }
   exchange_wait(S);
   const int u_base = before(S, 0, rank), nu_all = min(total(S, 0), U15_MAX);
-  for (int i = tid; i < m15; i += FT) {
+  for (int i = tid; i < m15 && w.trace; i += FT) {
     if (!S.b.p.flag[i]) continue;
     const int u = u_base + S.b.p.urank[i];
     if (u < U15_MAX) {
@@ -1576,7 +1602,7 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     const int cr = c_base + k;
     if (cr >= CAND_MAX) break;
     const int i = S.b.p.clist[k];
-    w.cand[(size_t)cell * CAND_MAX + cr] = u_base + S.b.p.urank[i];
+    if (w.trace) w.cand[(size_t)cell * CAND_MAX + cr] = u_base + S.b.p.urank[i];
     prefetch_l2_bulk(c.kv8 + (size_t)S.b.p.tok[i] * REC, REC);  // for attention should it win
   }
   {

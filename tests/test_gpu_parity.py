@@ -55,7 +55,7 @@ def _compare(eng, res, nc, capacity):
 
 
 def test_funnel_parity_and_output(case, cuda, path):
-    cfg = SeoulKV4Config(debug=True)
+    cfg = SeoulKV4Config(debug=True, trace_stages=True)
     with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
         attn.run(case.query(100))
         assert attn._engine.fused == (path == "fused")
@@ -97,7 +97,7 @@ def test_parity_sweep(cuda, monkeypatch, context, nprobe, capacity, staged):
     per-head nprobe and capacities."""
     monkeypatch.setattr(_native, "FORCE_STAGED", staged)
     case = Case(context=context, nprobe=64, seed=61)
-    cfg = SeoulKV4Config(debug=True, nprobe=nprobe, stage15_capacity=capacity)
+    cfg = SeoulKV4Config(debug=True, nprobe=nprobe, stage15_capacity=capacity, trace_stages=True)
     per_head = [nprobe] * 4 if isinstance(nprobe, int) else list(nprobe)
     with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
         for qseed in (1, 2):
@@ -143,7 +143,8 @@ def test_headline_config_parity(cuda, monkeypatch, headline, staged):
     monkeypatch.setattr(_native, "FORCE_STAGED", staged)
     case = headline
     nc = case.index.cells()[0]["centroids"].shape[0]
-    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
+    cfg = SeoulKV4Config(debug=True, trace_stages=True)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
         for qseed in (1000 * 7919 + 3, 1000 * 7919 + 4, 1000 * 7919 + 5):
             q = case.query(qseed)
             y = attn.run(q).to_torch()
@@ -186,7 +187,8 @@ def test_above_the_fused_limit(cuda):
     case = Case(context=262144, nprobe=384, seed=62)
     nc = case.index.cells()[0]["centroids"].shape[0]
     assert nc > 32768
-    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=SeoulKV4Config(debug=True)) as attn:
+    cfg = SeoulKV4Config(debug=True, trace_stages=True)
+    with SeoulKV4(device=cuda, k=case.k, v=case.v, index=case.index, config=cfg) as attn:
         for qseed in (1, 2):
             q = case.query(qseed)
             y = attn.run(q).to_torch()
