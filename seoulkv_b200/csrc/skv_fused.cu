@@ -1603,7 +1603,6 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (cr >= CAND_MAX) break;
     const int i = S.b.p.clist[k];
     if (w.trace) w.cand[(size_t)cell * CAND_MAX + cr] = u_base + S.b.p.urank[i];
-    prefetch_l2_bulk(c.kv8 + (size_t)S.b.p.tok[i] * REC, REC);  // for attention should it win
   }
   {
     BFrag F;
