@@ -139,7 +139,7 @@ struct FusedSmem {
   } b;
   float sx[4 * D];                 // the cell's four query rows (FP32 of BF16)
   float kscale[D];                 // per-dimension key scales
-  int offs[PER_MAX + 1];           // CSR offsets of the slice's clusters
+  int offs[PER_MAX + 1];           // CSR start of each Fine share survivor's list (P4 -> P5)
   uint16_t resid[PER_MAX];         // residual norms of the slice (BF16)
   float scale4[PER_MAX / 32];
   float fsc[CL * PER_MAX / 32];    // the cell's Fine scales (one per 32 centroids)
@@ -925,15 +925,12 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     static_assert(PER_MAX == 4 * FT && 4 * D == 2 * FT && PER_MAX / 32 <= FT && D <= FT, "load shapes");
     const uint16_t *qsrc = c.q ? c.q : w.q + ((size_t)slot * 16 + g * 4) * D;
     uint16_t qv[2], rv[4];
-    int ov[5];
     float ks = 0.0f, s4 = 0.0f, fs[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) qv[k] = qsrc[tid + k * FT];
     if (tid < D) ks = c.key_scale[tid];
 #pragma unroll
     for (int k = 0; k < 4; ++k) rv[k] = tid + k * FT < nrows ? c.resid[r0 + tid + k * FT] : (uint16_t)0;
-#pragma unroll
-    for (int k = 0; k < 5; ++k) ov[k] = tid + k * FT <= nrows ? c.offsets[r0 + tid + k * FT] : 0;
     if (tid < (nrows >> 5)) s4 = c.coarse_scale4[(r0 >> 5) + tid];
 #pragma unroll
     for (int k = 0; k < 2; ++k) fs[k] = tid + k * FT < (nc >> 5) ? c.fine_scale[tid + k * FT] : 0.0f;
@@ -965,9 +962,6 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     if (tid < D) S.kscale[tid] = ks;
 #pragma unroll
     for (int k = 0; k < 4; ++k) S.resid[tid + k * FT] = rv[k];
-#pragma unroll
-    for (int k = 0; k < 5; ++k)
-      if (tid + k * FT <= PER_MAX) S.offs[tid + k * FT] = ov[k];
     if (tid < PER_MAX / 32) S.scale4[tid] = s4;
 #pragma unroll
     for (int k = 0; k < 2; ++k) S.fsc[tid + k * FT] = fs[k];
@@ -1140,19 +1134,6 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       }
   }
   exchange_send(S, nsurv, 0, 0, 0);
-  // posting lists a survivor would bring into the pool (into L2), while the
-  // survivor counts travel
-  for (int k = tid; k < nsurv; k += FT) {
-    const int lr = S.sidx[k], b = S.offs[lr], e = S.offs[lr + 1];
-    if (e > b) {
-      prefetch_l2(c.values + b);
-      prefetch_l2(c.mates + b);
-      if (((b * 4) >> 7) != (((e - 1) * 4) >> 7)) {
-        prefetch_l2(c.values + e - 1);
-        prefetch_l2(c.mates + e - 1);
-      }
-    }
-  }
   exchange_wait(S);
   const int surv_base = before(S, 0, rank), nsurv_all = total(S, 0);
   // The Fine work is balanced over the cluster: CTA r scores the survivors at
@@ -1187,8 +1168,8 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
       }
       // the share's CSR ranges travel with the rows (P5 lists the selected
       // clusters from them without a dependent global load): start into
-      // S.offs, length into S.resid (both free since P3; a length that does
-      // not fit 16 bits is marked 0xffff and read again in P5)
+      // S.offs, length into S.resid (free since P1; a length that does not
+      // fit 16 bits is marked 0xffff and read again in P5)
       static_assert(BATCH_FINE <= 2 * FT, "two share survivors per thread");
       int cb[2] = {0, 0}, ce[2] = {0, 0};
 #pragma unroll
@@ -1262,6 +1243,18 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         const uint32_t cid = S.shin[k] & 0xffffu;
         S.shin[k] |= 1u << 24;
         atomicOr(selbits + (cid >> 5), 1u << (cid & 31));
+        // the cluster's postings and mates into L2 for P6 (only selected
+        // clusters: prefetching every survivor's lists read ~2 MB per step
+        // that no stage used)
+        const int b = S.offs[k], n = S.resid[k];
+        if (n > 0) {
+          prefetch_l2(c.values + b);
+          prefetch_l2(c.mates + b);
+          if (((b * 4) >> 7) != (((b + n - 1) * 4) >> 7)) {
+            prefetch_l2(c.values + b + n - 1);
+            prefetch_l2(c.mates + b + n - 1);
+          }
+        }
       }
     }
     __syncthreads();  // selected flags complete
