@@ -75,6 +75,7 @@ struct Engine {
   cudaGraph_t graph_host = nullptr;
   cudaGraphExec_t exec_host = nullptr;
   bool q_host = false;   // the bound query is in q_pinned
+  const uint16_t *q_bound = nullptr;  // fused path: the caller's device query, read in place by the kernel
   bool host_io = false;  // the last launch was a host-I/O step (its output and counters are in pinned memory)
   bool fused = false;             // one cluster kernel per step (else the staged kernels)
   // the centroid planes of every cell in one arena: cell c's upper plane at
@@ -138,6 +139,14 @@ ShardLinkDev link_view(const Engine *e) {
   L.epoch = e->link.epoch;
   L.exits = e->link.epoch + 1;
   return L;
+}
+
+// The engine's Work as a launch sees it: on the fused path a device-resident
+// query is read where the caller keeps it (no copy into the engine).
+Work view_work(const Engine *e) {
+  Work w = e->work;
+  if (e->q_bound) w.q = e->q_bound;
+  return w;
 }
 
 // The access-policy window the fused launches carry (null: none).
@@ -811,10 +820,19 @@ int skv_bind_query(void *handle, const uint16_t *q, int32_t on_device, void *str
   const size_t bytes = (size_t)e->desc.n_slots * 16 * D * sizeof(uint16_t);
   uint16_t *dq = const_cast<uint16_t *>(e->work.q);
   if (on_device) {
-    CK(cudaMemcpyAsync(dq, q, bytes, cudaMemcpyDeviceToDevice, st));
+    // the fused kernel reads the caller's query in place, in stream order
+    // (the caller keeps the buffer unchanged until the run has executed, as
+    // for any stream-ordered input); the staged kernels take a copy
+    if (e->fused) {
+      e->q_bound = q;
+    } else {
+      CK(cudaMemcpyAsync(dq, q, bytes, cudaMemcpyDeviceToDevice, st));
+      e->q_bound = nullptr;
+    }
     e->q_host = false;
     return SKV_OK;
   }
+  e->q_bound = nullptr;
   // the pinned staging buffer may still feed the previous host-I/O step;
   // the next skv_run copies it in as the first node of its graph
   if (e->q_pending) CK(cudaEventSynchronize(e->q_copied));
@@ -839,7 +857,7 @@ int skv_run(void *handle, void *stream) {
     // be on the device (a host query's pinned staging copy is not capturable
     // as a step of the caller's graph)
     if (e->q_host) return fail(SKV_E_STATE, "a captured run needs a device-resident query");
-    Work w = e->work;
+    Work w = view_work(e);
     if (e->link.active) {
       w.link = e->link.dev;
       w.shard_gids = e->link.gids;
@@ -849,6 +867,19 @@ int skv_run(void *handle, void *stream) {
     return SKV_OK;
   }
   const bool host = e->q_host;
+  if (!host && e->q_bound) {
+    // fused path, device query: one kernel launch, reading the query in place
+    Work w = view_work(e);
+    if (e->link.active) {
+      w.link = e->link.dev;
+      w.shard_gids = e->link.gids;
+    }
+    CK(launch_step(e, w, st));
+    e->host_io = false;
+    CK(cudaEventRecord(e->done, st));
+    e->ran = true;
+    return SKV_OK;
+  }
   cudaGraphExec_t &exec = host ? e->exec_host : e->exec;
   if (!exec) {
     CK(cudaStreamSynchronize(e->stream));
@@ -1268,7 +1299,7 @@ int skv_shard_attention(void *handle, const int32_t *gids, int32_t token_begin, 
   int rc = ready(e);
   if (rc) return rc;
   CK(cudaSetDevice(e->desc.device));
-  CK(launch_shard_attention(e->work, gids, token_begin, partials, static_cast<cudaStream_t>(stream)));
+  CK(launch_shard_attention(view_work(e), gids, token_begin, partials, static_cast<cudaStream_t>(stream)));
   e->host_io = false;
   return SKV_OK;
 }
@@ -1399,10 +1430,10 @@ int skv_profile_step(void *handle, void *stream, float *kernel_ms, int32_t max_k
   e->host_io = false;
   if (e->fused) {
     cudaEventRecord(ev[0], st);
-    le = launch_fused(e->work, st, window_of(e));
+    le = launch_fused(view_work(e), st, window_of(e));
     cudaEventRecord(ev[1], st);
   } else {
-    le = launch_funnel(e->work, st, ev.data());
+    le = launch_funnel(view_work(e), st, ev.data());
   }
   cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(ev[nk]) : le;
   const int n = std::min<int>(nk, max_kernels);
@@ -1433,7 +1464,7 @@ int skv_profile_phases(void *handle, void *stream, int32_t *tags, double *cycles
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   std::vector<long long> ts(2 * FUSED_MARKS, -1);
   CK(cudaMemcpyAsync(e->phase_ts, ts.data(), ts.size() * sizeof(long long), cudaMemcpyHostToDevice, st));
-  Work w = e->work;
+  Work w = view_work(e);
   w.phase_ts = e->phase_ts;
   if (e->link.active) {  // a connected shard group: every shard must profile this step together
     w.link = e->link.dev;
@@ -1473,7 +1504,7 @@ int skv_profile_ctas(void *handle, void *stream, int64_t *start_ns, int64_t *end
     if (rc) return rc;
   }
   CK(cudaMemsetAsync(e->cta_ts, 0xff, nts * sizeof(long long), st));  // unused marks read as tag -1
-  Work w = e->work;
+  Work w = view_work(e);
   w.cta_ts = e->cta_ts;
   cudaEvent_t ev[2];
   CK(cudaEventCreate(&ev[0]));
