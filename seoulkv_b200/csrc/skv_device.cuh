@@ -165,6 +165,9 @@ struct Work {
   uint32_t *arrive;         // [cell] attention partitions finished (step)
   uint32_t *hist;           // [cell][4 stages][4 heads][4096] first-pass histograms (step)
   uint16_t *out;            // [n_slots][16][256] BF16
+  uint16_t *out_host;       // fused host-I/O step: the output also goes straight to mapped pinned memory (or null)
+  int32_t *counts_host;     // ... and each cell's counters after its last barrier (or null)
+  uint16_t *q_store;        // ... and the query, read from mapped memory, is mirrored here for later kernels (or null)
   long long *phase_ts;      // [FUSED_MARKS][2] (tag, SM clock) marks of cell 0, or null
   long long *cta_ts;        // [cell][16][2] global timer (ns) at CTA entry and exit, then [16][FUSED_MARKS][2]
                             // (tag, ns) phase marks of cell 0's CTAs (fused), or null

@@ -69,6 +69,8 @@ struct Engine {
   // graph itself, which also copies the output and the counters back into
   // pinned host memory, so that a step costs one launch and one wait
   uint8_t *io_pinned = nullptr;    // output then counters (one copy back per host-I/O step)
+  uint16_t *q_pinned_dev = nullptr;  // device views of the mapped pinned buffers (fused host-I/O steps)
+  uint8_t *io_pinned_dev = nullptr;
   uint16_t *out_pinned = nullptr;  // views into io_pinned
   int32_t *counts_pinned = nullptr;
   size_t io_bytes = 0;
@@ -463,14 +465,18 @@ int skv_create(const SkvDesc *d, void **handle) {
   TRY(cudaEventCreateWithFlags(&e->q_copied, cudaEventDisableTiming) ? fail(SKV_E_CUDA, "event") : 0);
   TRY(cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming) ? fail(SKV_E_CUDA, "event") : 0);
   TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->q_pinned), (size_t)d->n_slots * 16 * D * 2,
-                    cudaHostAllocDefault) ? fail(SKV_E_CUDA, "pinned query buffer") : 0);
+                    cudaHostAllocMapped) ? fail(SKV_E_CUDA, "pinned query buffer") : 0);
+  TRY(cudaHostGetDevicePointer(reinterpret_cast<void **>(&e->q_pinned_dev), e->q_pinned, 0)
+          ? fail(SKV_E_CUDA, "mapped query buffer") : 0);
   // the output and the counters live in one device block (and one pinned
   // mirror), so that a host-I/O step copies them back in one transfer
   const size_t out_bytes = (size_t)d->n_slots * 16 * D * 2;
   e->io_bytes = out_bytes + (size_t)d->n_slots * G * NCOUNT * 4;
-  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->io_pinned), e->io_bytes, cudaHostAllocDefault)
+  TRY(cudaHostAlloc(reinterpret_cast<void **>(&e->io_pinned), e->io_bytes, cudaHostAllocMapped)
           ? fail(SKV_E_CUDA, "pinned output buffer")
           : 0);
+  TRY(cudaHostGetDevicePointer(reinterpret_cast<void **>(&e->io_pinned_dev), e->io_pinned, 0)
+          ? fail(SKV_E_CUDA, "mapped output buffer") : 0);
   e->out_pinned = reinterpret_cast<uint16_t *>(e->io_pinned);
   e->counts_pinned = reinterpret_cast<int32_t *>(e->io_pinned + out_bytes);
   TRY(prepare_funnel_attributes() ? fail(SKV_E_CUDA, "kernel attributes") : 0);
@@ -876,6 +882,27 @@ int skv_run(void *handle, void *stream) {
     }
     CK(launch_step(e, w, st));
     e->host_io = false;
+    CK(cudaEventRecord(e->done, st));
+    e->ran = true;
+    return SKV_OK;
+  }
+  if (host && e->fused) {
+    // fused path, host query: one kernel launch that reads the query from
+    // the mapped pinned buffer and writes the output and counters back into
+    // mapped pinned memory (no copy nodes around it)
+    Work w = e->work;
+    w.q = e->q_pinned_dev;
+    w.out_host = reinterpret_cast<uint16_t *>(e->io_pinned_dev);
+    w.counts_host = reinterpret_cast<int32_t *>(e->io_pinned_dev + (size_t)e->desc.n_slots * 16 * D * 2);
+    w.q_store = const_cast<uint16_t *>(e->work.q);
+    if (e->link.active) {
+      w.link = e->link.dev;
+      w.shard_gids = e->link.gids;
+    }
+    CK(launch_step(e, w, st));
+    CK(cudaEventRecord(e->q_copied, st));
+    e->q_pending = true;
+    e->host_io = true;
     CK(cudaEventRecord(e->done, st));
     e->ran = true;
     return SKV_OK;

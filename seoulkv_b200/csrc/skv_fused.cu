@@ -928,6 +928,9 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
     float ks = 0.0f, s4 = 0.0f, fs[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) qv[k] = qsrc[tid + k * FT];
+    if (w.q_store && rank == 0 && !lead)  // (host-I/O step: kernels after this one read the device copy)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) w.q_store[((size_t)slot * 16 + g * 4) * D + tid + k * FT] = qv[k];
     if (tid < D) ks = c.key_scale[tid];
 #pragma unroll
     for (int k = 0; k < 4; ++k) rv[k] = tid + k * FT < nrows ? c.resid[r0 + tid + k * FT] : (uint16_t)0;
@@ -1904,12 +1907,23 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
         L += ls[r] * e;
         O += os[r] * e;
       }
-      if (!lead) w.out[((size_t)slot * 16 + g * 4 + h) * D + d] = bf16_rne(O / L);
+      if (!lead) {
+        // (a host-I/O step also writes the mapped pinned copy; the device
+        // output stays current for borrowed device views)
+        const size_t o = ((size_t)slot * 16 + g * 4 + h) * D + d;
+        const uint16_t y = bf16_rne(O / L);
+        w.out[o] = y;
+        if (w.out_host) w.out_host[o] = y;
+      }
     }
   }
   mark(M_ATTN);
   if (tid == 0 && S.status) atomicOr(reinterpret_cast<unsigned *>(counts + C_STATUS), (unsigned)S.status);
   cluster_sync();  // no CTA leaves while its shared memory may still be read
+  // host-I/O step: the cell's counters (every CTA's status is in by now) to
+  // mapped pinned memory, plain stores
+  if (w.counts_host && !lead && rank == 0 && tid < NCOUNT)
+    w.counts_host[(size_t)cell * NCOUNT + tid] = __ldcg(counts + tid);
   if (w.link && !lead && rank == 0 && tid == 0) {
     // the last cluster of the step to finish advances the group's step
     // counter (every cluster read it in P12, before this barrier)
