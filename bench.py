@@ -504,14 +504,16 @@ def _timed_steps(args, device, flush, step_fn):
     each step on the current stream; returns the per-step times (us)."""
     stream = torch.cuda.current_stream(device)
     for i in range(args.warmup):
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         step_fn(i)
     torch.cuda.synchronize(device)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     gc.disable()
     torch.cuda._sleep(int(2e7))  # the host enqueues ahead of the device
     for i in range(args.steps):
-        flush.zero_()
+        if flush is not None:  # (None: steps back to back, L2 warm)
+            flush.zero_()
         ev[i][0].record(stream)
         step_fn(args.warmup + i)
         ev[i][1].record(stream)
@@ -873,6 +875,13 @@ def main():
         no_window = {"mean_us": float(np.mean(t_nw)), "p50_us": float(np.median(t_nw)),
                      "p99_us": float(np.percentile(t_nw, 99)), "steps": int(len(t_nw))}
 
+    # steady state: the same steps back to back without the L2 flush (a decode
+    # loop that revisits this layer finds its code and recent rows in L2)
+    t_w = _timed_steps(argparse.Namespace(warmup=args.warmup, steps=min(args.steps, 200)), device, None, step)
+    l2_warm = {"mean_us": float(np.mean(t_w)), "p50_us": float(np.median(t_w)),
+               "p99_us": float(np.percentile(t_w, 99)), "steps": int(len(t_w)),
+               "what": "steps back to back without the L2 flush (steady state); value flushes before every step"}
+
     # the same kind of steps on a second instance of the layer without the
     # lead cluster (the fused launch's extra cluster that runs a small
     # synthetic cell ahead of the real cells, bringing the kernel's
@@ -1003,6 +1012,7 @@ def main():
                           "what": "upper+lower centroid planes of the layer held in persisting L2 by an "
                                   "access-policy window (the flush evicts normal lines only)",
                           "without_window": no_window},
+            "l2_warm": l2_warm,
             "lead_cluster": {"on": bool(eng.fused),
                              "what": "one extra 16-CTA cluster per fused launch decodes a small synthetic cell "
                                      "ahead of the real cells, so the kernel's instructions are in L2 when they "

@@ -206,7 +206,9 @@ int skv_context(void *handle, int32_t *context);
 
 /* Intermediate buffers of the last run, for diagnostics and parity tests.
  * `which` selects one of SKV_STAGE_*; copies at most `bytes` bytes of the
- * given slot's four cells (cell-major) and returns the byte count in *written. */
+ * given slot's four cells (cell-major) and returns the byte count in *written.
+ * On the fused path TAGS, SELECTED, POOL, U15, CAND and LOHI are written only
+ * by an engine created with SKV_FLAG_TRACE (SKV_E_STATE otherwise). */
 #define SKV_STAGE_COUNTS 0      /* int32 [4][8]: ntags,nsel,npool,nu15,ncand,status,0,0 */
 #define SKV_STAGE_THRESH 1      /* uint16 [4][4] coarse thresholds (BF16 bits) */
 #define SKV_STAGE_TAGS 2        /* uint32 [4][nc] survivor tags                */
@@ -227,9 +229,10 @@ int skv_context(void *handle, int32_t *context);
 #define SKV_STAGE_MATES 17      /* int32 per cell offsets[nc] mates, cell after cell     */
 #define SKV_STAGE_LABELS 18     /* int32 [4][T][2] spill-2 lists of tokens from the first local window on
                                    (engines with appends; -1 below the window)     */
-#define SKV_STAGE_LEAD_COUNTS 19 /* int32 [NCOUNT = 8] counters of the lead cluster's synthetic
-                                   cell (SKV_FLAG_NO_LEAD): tags, pool, selected, postings, status,
-                                   union, candidates; slot is ignored (must be valid) */
+#define SKV_STAGE_LEAD_COUNTS 19 /* int32 [8] counters of the lead cluster's synthetic cell
+                                   (see SKV_FLAG_NO_LEAD), in the order of SKV_STAGE_COUNTS:
+                                   ntags, nsel, npool, nu15, ncand, status, postings, 0;
+                                   slot is ignored (must be valid) */
 int skv_read_stage(void *handle, int32_t slot, int32_t which, void *dst, size_t bytes,
                    size_t *written);
 

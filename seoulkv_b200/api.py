@@ -176,11 +176,15 @@ class SeoulKV4:
             self._engine = self._initialize()
             self._host_kv = None
         eng = self._engine
+        # (a contiguous BF16 Q is passed as it is: the engine takes its bytes)
         if q.device.type == "cuda":
-            qd = _bits(q.to(f"cuda:{self._device_index}"))
+            if q.device.index != self._device_index:
+                q = q.to(f"cuda:{self._device_index}")
+            qd = q if q.is_contiguous() else q.contiguous()
             eng.step(qd.data_ptr(), True, self._stream())
         else:
-            eng.step(_bits(q).data_ptr(), False, self._stream())
+            qh = q if q.is_contiguous() else q.contiguous()
+            eng.step(qh.data_ptr(), False, self._stream())
         self._generation += 1
         if first:
             # the reference's first run checks the live pool against capacity

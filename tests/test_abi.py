@@ -32,6 +32,19 @@ def test_library_exports_every_declared_symbol():
     assert lib.skv_kernel_name(0) != b""
 
 
+def test_flag_and_stage_constants_match_the_header():
+    """The Python binding's flag bits and stage ids are the header's."""
+    text = HEADER.read_text()
+    defs = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define\s+(SKV_\w+)\s+(\d+)", text)}
+    assert defs["SKV_FLAG_STAGED"] == _native.SKV_FLAG_STAGED
+    assert defs["SKV_FLAG_NO_LEAD"] == _native.SKV_FLAG_NO_LEAD
+    assert defs["SKV_FLAG_TRACE"] == _native.SKV_FLAG_TRACE
+    assert len({_native.SKV_FLAG_STAGED, _native.SKV_FLAG_NO_LEAD, _native.SKV_FLAG_TRACE}) == 3
+    stage = {k[len("SKV_STAGE_"):].lower(): v for k, v in defs.items() if k.startswith("SKV_STAGE_")}
+    for name, v in _native.STAGE.items():
+        assert stage.get(name) == v, name
+
+
 def test_create_rejects_bad_descriptors():
     lib = _native.load()
     import ctypes

@@ -26,6 +26,11 @@ def test_config_validation():
     assert SeoulKV4Config(nprobe=[16, 32, 48, 64]).nprobe == (16, 32, 48, 64)
     with pytest.raises(Exception):
         SeoulKV4Config().debug = True  # frozen
+    cfg = SeoulKV4Config()
+    assert cfg.l2_resident and cfg.lead_cluster and not cfg.trace_stages
+    for field in ("l2_resident", "lead_cluster", "trace_stages"):
+        with pytest.raises(TypeError):
+            SeoulKV4Config(**{field: 1})
 
 
 def test_nprobe_rules():
