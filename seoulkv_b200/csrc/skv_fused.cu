@@ -40,18 +40,25 @@
 // result (and, in the last round of a 32-bit selection, each CTA's share of
 // the tied keys) back; see cluster_select.
 //
-// Every intermediate the staged path exposes (lo/hi, thresholds, survivor
-// tags, selected clusters, pool, unions, final ranks and ids, counters) is
-// written to the same Work buffers in the same format, so both paths are
-// checked by the same stage-by-stage parity tests.
+// With Work::trace, every intermediate the staged path exposes (lo/hi,
+// survivor tags, selected clusters, pool, unions) is also written to the same
+// Work buffers in the same format, so both paths are checked by the same
+// stage-by-stage parity tests; thresholds, final ranks and ids and the
+// counters are always written.
+//
+// The lead cluster (Work::lead): the launch carries one more cluster,
+// blockIdx.y 0, that decodes the engine's small synthetic cell (index
+// n_cells) through the same phases.  Its work is a few percent of a real
+// cell's, so it runs ahead and its instruction fetches bring the kernel's
+// code into L2 before the real cells execute it; its outputs are never read.
 //
 // Waits: every wait on another CTA is a bounded poll of an mbarrier phase
 // (XWAIT_POLLS) that records ST_TIMEOUT in the cell's status and returns
-// instead of waiting on; the coarse-slice copies likewise (WAIT_POLLS).  The
-// cluster barriers left (the start, the sequence-sharded exchanges and the
-// end, where no CTA may leave while its shared memory can still be read) are
-// reached by all threads of all CTAs: control flow is uniform by
-// construction.
+// instead of waiting on; the coarse-slice copies likewise (WAIT_POLLS), and
+// the sequence-sharded list entries (SHARD_WAIT_POLLS).  The cluster
+// barriers left (the start and the end, where no CTA may leave while its
+// shared memory can still be read) are reached by all threads of all CTAs:
+// control flow is uniform by construction.
 #include <cuda_fp8.h>
 
 #include "skv_device.cuh"
