@@ -3,7 +3,12 @@
 Run in a checkout that has the reference package available (its ``src``
 directory on ``sys.path``, e.g. ``SEOULKV_REFERENCE=/path/to/reference/src``)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py                      # golden_t8192.npz
+    python tests/golden/make_golden.py --context 6400 --kv-seed 29 --nprobe 96 \
+        --sink 64 --local 512 --q-seeds 401,402,403          # golden_t6400.npz
+
+(the second one is the reference's smallest context, with other zones and
+another probe budget).
 
 The reference's decode path needs a Tenstorrent board, so the fixtures pin
 everything that *can* run here:
@@ -49,9 +54,20 @@ from oracle import oracle as O  # noqa: E402
 from seoulkv_b200 import synthetic  # noqa: E402
 from seoulkv_b200.index import device_view  # noqa: E402
 
-OUT = Path(__file__).resolve().parent / "golden_t8192.npz"
-CONTEXT, KV_SEED, NPROBE = 8192, 17, 128
-Q_SEEDS = (301, 302, 303)
+HERE = Path(__file__).resolve().parent
+
+
+def parse():
+    import argparse
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--context", type=int, default=8192)
+    p.add_argument("--kv-seed", type=int, default=17)
+    p.add_argument("--nprobe", type=int, default=128)
+    p.add_argument("--sink", type=int, default=128)
+    p.add_argument("--local", type=int, default=256)
+    p.add_argument("--q-seeds", default="301,302,303")
+    return p.parse_args()
 
 
 def sha(a) -> str:
@@ -63,6 +79,10 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 
 def main():
+    args = parse()
+    CONTEXT, KV_SEED, NPROBE, SINK, LOCAL = args.context, args.kv_seed, args.nprobe, args.sink, args.local
+    Q_SEEDS = tuple(int(x) for x in args.q_seeds.split(","))
+    OUT = HERE / f"golden_t{CONTEXT}.npz"
     from seoulkv4 import SeoulKV4Index as RefIndex
     from seoulkv4._codecs.index import encode_group_scale_cell, expand_lists
     from seoulkv4._codecs.keys import _stage15_key_codec, encode_planes
@@ -74,10 +94,10 @@ def main():
     from seoulkv4._kernels.stage1_fine.seoulkv4_fine_parallel import schedule, tree_top_p
 
     k, v, mixes = synthetic.make_kv(CONTEXT, seed=KV_SEED)
-    ref_index = RefIndex.build(k, v, sink=128, local=256, nprobe=NPROBE)
+    ref_index = RefIndex.build(k, v, sink=SINK, local=LOCAL, nprobe=NPROBE)
     cells = ref_index._cells
     data, meta = {}, {"context": CONTEXT, "kv_seed": KV_SEED, "nprobe": NPROBE, "q_seeds": list(Q_SEEDS),
-                      "sink": 128, "local": 256, "key_hashes": [c["key_hash"] for c in cells], "cells": []}
+                      "sink": SINK, "local": LOCAL, "key_hashes": [c["key_hash"] for c in cells], "cells": []}
     for g, c in enumerate(cells):
         for name in ("upper", "lower", "scale", "group_fine_scale", "coarse_residual_norm", "offsets", "values"):
             t = c[name]
@@ -145,7 +165,7 @@ def main():
         out = np.zeros((16, 256), np.uint16)
         for j in range(16):
             g, h = divmod(j, 4)
-            out[j] = O.attention(qb[j], k8[g], v8[g], O.attention_keys(CONTEXT, 128, 256, res[g]["final_ids"][h]))
+            out[j] = O.attention(qb[j], k8[g], v8[g], O.attention_keys(CONTEXT, SINK, LOCAL, res[g]["final_ids"][h]))
         data[f"q{qi}_final_ids"] = np.stack([r["final_ids"] for r in res])
         data[f"q{qi}_out"] = out
 

@@ -86,19 +86,24 @@ class ShardCase(Case):
 
 # ------------------------------------------------------------ golden data
 
-GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "golden_t8192.npz"
+GOLDEN_DIR = __import__("pathlib").Path(__file__).resolve().parent / "golden"
+GOLDEN = GOLDEN_DIR / "golden_t8192.npz"
+# every fixture tests/golden/make_golden.py wrote: the default one and the
+# reference's smallest context with other zones and another probe budget
+GOLDEN_FILES = ("golden_t8192.npz", "golden_t6400.npz")
 
 
 class Golden:
     """The reference-built fixture (tests/golden/make_golden.py) + regenerated K/V."""
 
-    def __init__(self):
+    def __init__(self, name: str = "golden_t8192.npz"):
         import json
 
-        z = np.load(GOLDEN, allow_pickle=False)
+        z = np.load(GOLDEN_DIR / name, allow_pickle=False)
         self.z = {k: z[k] for k in z.files}
         self.meta = json.loads(str(self.z["metadata"]))
         self.context = self.meta["context"]
+        self.sink, self.local = self.meta["sink"], self.meta["local"]
         self.k, self.v, self.mixes = synthetic.make_kv(self.context, seed=self.meta["kv_seed"])
         self.queries = [synthetic.make_query(self.context, self.mixes, seed=s) for s in self.meta["q_seeds"]]
 

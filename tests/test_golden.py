@@ -13,12 +13,12 @@ import torch
 from oracle import oracle as O
 from seoulkv_b200 import _codecs
 from seoulkv_b200.index import posting_mates
-from tests.helpers import Golden, bits
+from tests.helpers import GOLDEN_FILES, Golden, bits
 
 
-@pytest.fixture(scope="module")
-def gold():
-    return Golden()
+@pytest.fixture(scope="module", params=GOLDEN_FILES)
+def gold(request):
+    return Golden(request.param)
 
 
 @pytest.fixture(scope="module")

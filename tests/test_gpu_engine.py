@@ -7,7 +7,7 @@ import torch
 from oracle import oracle as O
 from seoulkv_b200 import _native
 from seoulkv_b200.index import device_view
-from tests.helpers import Case, Golden, bits
+from tests.helpers import GOLDEN_FILES, Case, Golden, bits
 
 pytestmark = pytest.mark.gpu
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
@@ -35,16 +35,16 @@ def _check_out(got_bits, want_bits):
     assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
 
 
-@pytest.fixture(scope="module")
-def gold():
-    return Golden()
+@pytest.fixture(scope="module", params=GOLDEN_FILES)
+def gold(request):
+    return Golden(request.param)
 
 
 @pytest.mark.parametrize("staged", [False, True], ids=["fused", "staged"])
 def test_reference_built_index(gold, cuda, staged):
     """Engine on the index the reference itself built: ids equal the pinned oracle."""
     views = gold.views()
-    eng = _engine(1, gold.context, views[0]["nc"], staged=staged)
+    eng = _engine(1, gold.context, views[0]["nc"], sink=gold.sink, local=gold.local, staged=staged)
     try:
         eng.upload_index(0, views)
         _upload_kv(eng, 0, gold.k, gold.v)
@@ -59,7 +59,7 @@ def test_reference_built_index(gold, cuda, staged):
 def test_upload_codec_and_fp8_records(gold, cuda):
     views = gold.views()
     T = gold.context
-    eng = _engine(1, T, views[0]["nc"])
+    eng = _engine(1, T, views[0]["nc"], sink=gold.sink, local=gold.local)
     try:
         eng.upload_index(0, views)
         _upload_kv(eng, 0, gold.k, gold.v)
