@@ -490,7 +490,12 @@ def run_sharded(args, world, rank, local, device):
                     "timing": "host wall clock of run(pinned Q) + host readback, each step after an L2 flush "
                               "and a barrier (value) or back to back with L2 warm (l2_warm_value); mean, max over ranks"},
             "clocks": clk,
-            "gpu_launches": (sh.attn._engine.kernels_per_step() + (4 if args.transport == "p2p" else 3))
+            # our kernels per step on each GPU: the funnel (one fused kernel, which
+            # also exchanges and merges over peer memory, or the 14 staged ones
+            # plus merge, attention, combine and step-counter kernels), or, with
+            # the NCCL transport, the funnel plus merge, attention and combine
+            "gpu_launches": (sh.attn._engine.kernels_per_step()
+                             + ((0 if sh.attn._engine.fused else 4) if args.transport == "p2p" else 3))
                             * args.steps * world,
         }
         print(json.dumps(line), flush=True)
