@@ -367,12 +367,14 @@ def run_sharded(args, world, rank, local, device):
     torch.cuda.synchronize(device)
     clocks.start()
     time.sleep(0.3)
-    # every host enqueues ahead of its device (a short device-side sleep
-    # first, no garbage collection meanwhile), so that the GPUs run their
-    # steps back to back and meet at each step's list exchange, as a decode
-    # loop does; otherwise each step would also carry the hosts' launch skew
+    # every host enqueues ahead of its device (a device-side sleep long
+    # enough for the host to queue the whole timed loop, ~150 us of host time
+    # per step at most; no garbage collection meanwhile), so that the GPUs
+    # run their steps back to back and meet at each step's list exchange, as
+    # a decode loop does; otherwise a step would also carry the hosts' launch
+    # skew and any pause of one host would stall every GPU at the exchange
     gc.disable()
-    torch.cuda._sleep(int(2e7))
+    torch.cuda._sleep(int(2e7 + args.steps * 150e-6 * 2.0e9))
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
