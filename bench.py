@@ -320,7 +320,8 @@ def run_reference(args):
         qs = [synthetic.make_query(args.context, mixes, seed=query_seed(HEADLINE_SEED, i))
               for i in range(warm + steps)]
         config = headline_config(args)
-        sample = f"{steps} decode steps of the 128K layer (fresh Q each; C restatement of the reference funnel)"
+        sample = (f"{steps} decode steps of the {args.context}-token layer (fresh Q each; "
+                  "C restatement of the reference funnel)")
     lat, _ = cpu_latencies(shards, qs, warm, steps)
     us = float(np.median(lat))
     line = {
@@ -979,7 +980,7 @@ def main():
     err = np.abs(O.bf16_to_f32(out).astype(np.float64) - O.bf16_to_f32(ref_out).astype(np.float64))
     parity = {"ids_bit_exact": bool(np.array_equal(ids, gids)), "out_max_abs": float(err.max()),
               "out_mean_abs": float(err.mean()), "tolerance": [2e-2, 2e-3], "step": "last timed step"}
-    cpu_line = cpu_baseline_line(lat, f"the first {n_cpu} timed queries of this 128K layer, one step at a time "
+    cpu_line = cpu_baseline_line(lat, f"the first {n_cpu} timed queries of this {args.context}-token layer, one step at a time "
                                       "(C restatement of the reference funnel)")
 
     # end to end through the public API: pinned host Q -> run -> to_torch.
