@@ -20,10 +20,16 @@ Steps 2-4 are CUDA kernels behind the C ABI.  Two transports move the lists
 and partials between GPUs:
 
 * ``"p2p"`` (default with more than one shard): every GPU maps its peers'
-  exchange regions once (CUDA IPC handles swapped over the process group);
-  the merge and combine kernels write straight into the peers' memory over
-  NVLink and wait (bounded) on per-step flags, so a whole step -- funnel,
-  merge, attention, combine -- is one CUDA graph with no host round trip;
+  exchange regions and FP8 records once (CUDA IPC handles swapped over the
+  process group).  On the fused path the whole step is one launch of the
+  funnel kernel: each head's top-100 goes to every peer as tagged 8-byte
+  entries (the step counter's low byte, polled with a bound, no flag), every
+  GPU merges the lists itself and attends over the global winners and the
+  dense zones, reading the records that other shards own over NVLink, so
+  steps 3-4 need no exchange of partials.  On the staged path (shards above
+  the fused kernel's limits) separate merge, attention and combine kernels
+  write into the peers' memory and wait (bounded) on per-step flags, all in
+  one CUDA graph with no host round trip;
 * ``"nccl"``: two ``torch.distributed`` all-gathers between separate
   merge / attention / combine launches.
 """
