@@ -225,13 +225,17 @@ class Engine:
 
     def step(self, q_ptr: int, on_device: bool, stream: int = 0) -> None:
         """bind_query + run in one call."""
-        check(self.lib.skv_step(self.handle, ctypes.c_void_p(q_ptr), int(on_device),
-                                ctypes.c_void_p(stream or None)), "skv_step")
+        # (the argtypes convert the integers: no ctypes objects on the per-step path)
+        check(self.lib.skv_step(self.handle, q_ptr, on_device, stream or None), "skv_step")
 
     def finish(self, out: np.ndarray | None) -> None:
         """Wait for the last step; copy its output into `out` (uint16 [n_slots, 16, 256]) if given.
         Raises NativeError (SKV_E_CAPACITY) when a live count left its range."""
         check(self.lib.skv_finish(self.handle, None if out is None else _ptr(out), None), "skv_finish")
+
+    def finish_to(self, out_ptr: int) -> None:
+        """``finish`` into host memory at ``out_ptr`` (BF16 [n_slots, 16, 256], C order)."""
+        check(self.lib.skv_finish(self.handle, out_ptr, None), "skv_finish")
 
     def sync(self) -> None:
         check(self.lib.skv_sync(self.handle), "skv_sync")

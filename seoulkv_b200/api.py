@@ -17,6 +17,17 @@ from seoulkv_b200.config import (
 from seoulkv_b200.index import SeoulKV4Index, device_view
 from seoulkv_b200.result import DecodeResult
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _current_stream(device_index: int) -> int:
+    """The cudaStream_t of PyTorch's current stream on the device (the raw
+    handle without a Stream object once PyTorch's CUDA state is initialised:
+    this is on every decode step's host path)."""
+    if _raw_stream is None or not torch.cuda.is_initialized():
+        return torch.cuda.current_stream(device_index).cuda_stream
+    return _raw_stream(device_index)
+
 
 def _cuda_index(device) -> int:
     if device is None:
@@ -138,7 +149,7 @@ class SeoulKV4:
             raise ValueError("expected BF16 Q [1,1,16,256]")
 
     def _stream(self) -> int:
-        return torch.cuda.current_stream(self._device_index).cuda_stream
+        return _current_stream(self._device_index)
 
     def _initialize(self):
         zones = self._index.zones

@@ -19,11 +19,10 @@ from __future__ import annotations
 
 from typing import Sequence
 
-import numpy as np
 import torch
 
 from seoulkv_b200 import _native
-from seoulkv_b200.api import _bits, _check_append, _cuda_index, _enqueue_append, _max_context
+from seoulkv_b200.api import _bits, _check_append, _cuda_index, _current_stream, _enqueue_append, _max_context
 from seoulkv_b200.config import MAX_CONTEXT, MIN_CONTEXT, N_HEADS, N_KV_HEADS, SeoulKV4Config, validate_nprobe
 from seoulkv_b200.index import SeoulKV4Index, device_view
 from seoulkv_b200.result import _DeviceBuffer
@@ -45,12 +44,12 @@ class BatchResult:
     def to_torch(self) -> torch.Tensor:
         """Synchronise and copy the outputs into a CPU BF16 tensor [n, 1, 16, 256]."""
         o = self._live()
-        out = np.empty((o.n, N_HEADS, 256), dtype=np.uint16)
+        y = torch.empty((o.n, 1, N_HEADS, 256), dtype=torch.bfloat16)
         try:
-            o._engine.finish(out)  # wait, status check and output copy in one native call
+            o._engine.finish_to(y.data_ptr())  # wait, status check and output copy in one native call
         except _native.NativeError as exc:
             raise RuntimeError(str(exc)) from exc
-        return torch.from_numpy(out.view(np.int16)).view(torch.bfloat16).reshape(o.n, 1, N_HEADS, 256)
+        return y
 
     @property
     def device_tensor(self) -> torch.Tensor:
@@ -117,7 +116,7 @@ class SeoulKV4Batch:
             raise RuntimeError("SeoulKV4Batch is closed")
 
     def _stream(self) -> int:
-        return torch.cuda.current_stream(self._device_index).cuda_stream
+        return _current_stream(self._device_index)
 
     def _initialize(self) -> _native.Engine:
         context, sink, local = self._zones
