@@ -29,7 +29,6 @@ the fixtures under ``tests/golden`` (see ``tests/golden/make_golden.py``).
 from __future__ import annotations
 
 import ctypes
-import os
 import subprocess
 from pathlib import Path
 
