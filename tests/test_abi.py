@@ -63,3 +63,56 @@ def test_no_gpu_fails_loudly():
     with pytest.raises(_native.NativeError) as exc:
         _native.Engine(n_slots=1, context=8192, sink=128, local=256, nc=1952, capacity=13056, device=0)
     assert exc.value.code == -2
+
+
+C_CONSUMER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "seoulkv_b200.h"
+
+int main(void) {
+  SkvDesc d;
+  void *h = NULL;
+  memset(&d, 0, sizeof d);
+  d.n_slots = 0;  /* invalid: rejected before any CUDA call */
+  d.context = 8192; d.sink = 128; d.local = 256; d.nc = 1952; d.stage15_capacity = 13056;
+  int rc = skv_create(&d, &h);
+  const char *msg = skv_last_error();
+  printf("%d %s|%s\n", rc, h == NULL ? "null" : "set", msg ? msg : "");
+  return rc == SKV_E_INVALID && h == NULL && msg && msg[0] ? 0 : 1;
+}
+"""
+
+
+def test_header_compiles_as_c_and_cxx(tmp_path):
+    """The boundary header is plain C (what cgo, JNI or a C++ runtime includes)."""
+    import shutil
+    import subprocess
+
+    for cc, std in (("gcc", "-std=c99"), ("g++", "-std=c++17")):
+        if not shutil.which(cc):
+            pytest.skip(f"{cc} not found")
+        src = tmp_path / ("h.c" if cc == "gcc" else "h.cc")
+        src.write_text('#include "seoulkv_b200.h"\nint main(void) { return sizeof(SkvDesc) == 0; }\n')
+        r = subprocess.run([cc, std, "-Wall", "-Werror", "-pedantic", "-fsyntax-only", f"-I{HEADER.parent}",
+                            str(src)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+
+
+def test_c_program_links_and_gets_the_error_contract(tmp_path):
+    """A plain C program linked against the library: a bad descriptor gives
+    SKV_E_INVALID, no handle and a message from skv_last_error()."""
+    import shutil
+    import subprocess
+
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not found")
+    lib = Path(_native.load()._name)
+    src, exe = tmp_path / "consumer.c", tmp_path / "consumer"
+    src.write_text(C_CONSUMER)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{HEADER.parent}", str(src), str(lib),
+                        f"-Wl,-rpath,{lib.parent}", "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, (run.stdout, run.stderr)
+    assert run.stdout.startswith(f"{-1} null|")
