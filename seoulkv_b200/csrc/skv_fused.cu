@@ -1839,7 +1839,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
           const int r = it - dense;
           my_head = r / TOPK;
           my_tok = S.win[r / TOPK][r - (r / TOPK) * TOPK];
-          if (my_tok < 0) { my_tok = 0; my_head = -2; }  // sharded: fewer than 100 in the group
+          // -1: fewer than 100 in the group (sharded); any other value outside
+          // the layer only after a wait for the winners ran out (ST_TIMEOUT,
+          // S.win not written this step): no record is read for either
+          if ((unsigned)my_tok >= (unsigned)T) { my_tok = 0; my_head = -2; }
         }
       }
       fold(nb, my_tok, my_head);
