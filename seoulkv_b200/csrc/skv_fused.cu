@@ -54,8 +54,9 @@
 //
 // Waits: every wait on another CTA is a bounded poll of an mbarrier phase
 // (XWAIT_POLLS) that records ST_TIMEOUT in the cell's status and returns
-// instead of waiting on; the coarse-slice copies likewise (WAIT_POLLS), and
-// the sequence-sharded list entries (SHARD_WAIT_POLLS).  The cluster
+// instead of waiting on; the coarse-slice copies likewise (WAIT_POLLS); the
+// sequence-sharded list entries and, in a linked cell, the merged winners
+// are bounded on the global timer (SHARD_LIST_NS, WIN_WAIT_NS).  The cluster
 // barriers left (the start and the end, where no CTA may leave while its
 // shared memory can still be read) are reached by all threads of all CTAs:
 // control flow is uniform by construction.
@@ -77,6 +78,14 @@ constexpr int POS_MAX = 1024;                     // pool positions per CTA
 constexpr int BIG = PER_MAX * 64;                 // staging area (128 KB)
 constexpr long long WAIT_POLLS = 1 << 20;         // mbarrier polls before giving up (slice copies)
 constexpr long long XWAIT_POLLS = 1 << 16;        // polls before giving up on other CTAs' pushes
+// Timed bounds (global timer) of the sequence-sharded step: an owner CTA
+// waits at most SHARD_LIST_NS for the other shards' lists, and every CTA of a
+// linked cell waits for the merged winners up to WIN_WAIT_NS from the start of
+// its own wait, longer than any owner can take; so a late or missing shard
+// ends the step with ST_TIMEOUT, and every push a CTA is sent still lands
+// before that CTA stops waiting for it.
+constexpr unsigned long long SHARD_LIST_NS = 2000000000ull;
+constexpr unsigned long long WIN_WAIT_NS = 3000000000ull;
 
 // Row strides (bytes) of gathered rows in the staging area: 16 bytes of
 // padding keep the 8-byte fragment loads of a warp on distinct banks.
@@ -280,6 +289,18 @@ __device__ __noinline__ void mbar_wait_cluster(void *bar, uint32_t parity, int *
   const uint32_t a = smem_addr(bar);
   for (long long i = 0; i < XWAIT_POLLS; ++i)
     if (mbar_try_cluster(a, parity)) return;
+  atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
+}
+// As mbar_wait_cluster, bounded by the global timer (and, should the timer
+// stall, by 2^32 polls) instead of XWAIT_POLLS polls.
+__device__ __noinline__ void mbar_wait_cluster_until(void *bar, uint32_t parity, int *status,
+                                                     unsigned long long deadline) {
+  const uint32_t a = smem_addr(bar);
+  for (long long it = 0; it < (1ll << 26); ++it) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_cluster(a, parity)) return;
+    if (global_ns() > deadline) break;
+  }
   atomicOr(reinterpret_cast<unsigned *>(status), ST_TIMEOUT);
 }
 // Asynchronous 16-byte store into a CTA's shared memory (dst, from remote());
@@ -833,13 +854,19 @@ __device__ __noinline__ void shard_lists(const Work &w, FusedSmem &S, int cell, 
   const ShardRegion *R = reinterpret_cast<const ShardRegion *>(L.peer[L.rank]);
   unsigned long long *mk = reinterpret_cast<unsigned long long *>(S.big + 4096);  // [n][TOPK]
   static_assert(4096 + SHARD_MAX * TOPK * 8 <= BIG, "merge keys fit the staging area");
+  // (bounded by SHARD_LIST_NS on the global timer, checked every 64 polls,
+  // and by SHARD_WAIT_POLLS polls; once late, a thread stops polling)
+  const unsigned long long deadline = global_ns() + SHARD_LIST_NS;
   bool late = false;
   for (int c = tid; c < n * TOPK; c += FT) {
     const int s = c / TOPK, r = c - s * TOPK;
     const unsigned long long *src = &R->ll[par][s][ch][r];
     unsigned long long v = ld_relaxed_sys_u64(src);
     for (long long polls = 0; (v & 0xff00000000000000ull) != tag; ++polls) {
-      if (polls > SHARD_WAIT_POLLS) { late = true; break; }
+      if (late || polls > SHARD_WAIT_POLLS || ((polls & 63) == 63 && global_ns() > deadline)) {
+        late = true;
+        break;
+      }
       __nanosleep(64);
       v = ld_relaxed_sys_u64(src);
     }
@@ -1819,7 +1846,10 @@ __global__ void __launch_bounds__(FT, 1) k_funnel(Work w) {
   }
   // the step's winners (the group's merged ones when sequence-sharded) in S.win
   if (tid == 0) mbar_expect_tx(&S.mb_win, G * TOPK * 4);
-  mbar_wait_cluster(&S.mb_win, 0u, &S.status);
+  if (Lk)
+    mbar_wait_cluster_until(&S.mb_win, 0u, &S.status, global_ns() + WIN_WAIT_NS);
+  else
+    mbar_wait_cluster(&S.mb_win, 0u, &S.status);
   mark(M_S2SEL);
   {
     // the winners over all warps (and the dense zones too when they were
