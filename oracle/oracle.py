@@ -93,6 +93,7 @@ def lib():
             getattr(_lib, name).restype = ctypes.c_int
         _lib.skv_oracle_set_threads.argtypes = [ctypes.c_int]
         _lib.skv_oracle_set_unflushed.argtypes = [ctypes.c_int]
+        _lib.skv_oracle_set_tie_high.argtypes = [ctypes.c_int]
         _lib.skv_oracle_unflushed_dropped.restype = ctypes.c_longlong
     return _lib
 
@@ -103,6 +104,14 @@ def set_unflushed(on: bool) -> None:
     canonical definition's flush of elements below 2^(E-22), not a second
     definition: the engine follows the flushed one."""
     lib().skv_oracle_set_unflushed(1 if on else 0)
+
+
+def set_tie_high(on: bool) -> None:
+    """Break equal Stage-1.5, 1.6 and II scores toward the higher position
+    instead of the lower one.  A measurement of the unpinned tie order (the
+    reference leaves it to its TT top-k library), not a second definition:
+    the engine follows the lower-position rule."""
+    lib().skv_oracle_set_tie_high(1 if on else 0)
 
 
 def unflushed_dropped() -> int:

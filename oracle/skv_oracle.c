@@ -246,8 +246,17 @@ static void top_k(KeyIdx *items, int n, int k, int32_t *out) {
     for (int i = 0; i < k; ++i) out[i] = items[i].idx;
 }
 
+/* Tie order of the Stage-1.5, 1.6 and II selections: equal scores go to the
+ * lower position (the canonical rule); with g_tie_high set, to the higher
+ * one.  The switch measures how much the unpinned tie order of the
+ * reference's TT top-k can move the selected ids and the output; the engine
+ * follows the canonical rule. */
+static int g_tie_high = 0;
+void skv_oracle_set_tie_high(int on) { g_tie_high = on != 0; }
+
 static inline uint64_t rank_key(uint16_t score, int32_t pos) {
-    return ((uint64_t)ord16(score) << 32) | (uint64_t)(0xffffffffu - (uint32_t)pos);
+    const uint32_t low = g_tie_high ? (uint32_t)pos : 0xffffffffu - (uint32_t)pos;
+    return ((uint64_t)ord16(score) << 32) | (uint64_t)low;
 }
 
 /* ---------------------------------------------------------------- coarse */
