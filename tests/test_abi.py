@@ -107,7 +107,8 @@ def test_c_program_links_and_gets_the_error_contract(tmp_path):
 
     if not shutil.which("gcc"):
         pytest.skip("gcc not found")
-    lib = Path(_native.load()._name)
+    _native.load()  # (builds the library first when it is stale)
+    lib = _native.library_path()
     src, exe = tmp_path / "consumer.c", tmp_path / "consumer"
     src.write_text(C_CONSUMER)
     r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{HEADER.parent}", str(src), str(lib),
