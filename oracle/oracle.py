@@ -94,6 +94,7 @@ def lib():
         _lib.skv_oracle_set_threads.argtypes = [ctypes.c_int]
         _lib.skv_oracle_set_unflushed.argtypes = [ctypes.c_int]
         _lib.skv_oracle_set_tie_high.argtypes = [ctypes.c_int]
+        _lib.skv_oracle_set_fp32_accumulation.argtypes = [ctypes.c_int]
         _lib.skv_oracle_unflushed_dropped.restype = ctypes.c_longlong
     return _lib
 
@@ -104,6 +105,14 @@ def set_unflushed(on: bool) -> None:
     canonical definition's flush of elements below 2^(E-22), not a second
     definition: the engine follows the flushed one."""
     lib().skv_oracle_set_unflushed(1 if on else 0)
+
+
+def set_fp32_accumulation(on: bool) -> None:
+    """Sum every scoring dot in FP32 in dimension order (a rounding after
+    every add) instead of exactly.  A measurement of the unpinned
+    accumulation of the reference's TT FPU, not a second definition: the
+    engine follows the exact sum."""
+    lib().skv_oracle_set_fp32_accumulation(1 if on else 0)
 
 
 def set_tie_high(on: bool) -> None:

@@ -224,7 +224,25 @@ static float unflushed_dot(const float *row, int e_add, const int32_t *w) {
     return neg ? -f : f;
 }
 
+/* FP32-accumulation mode (a measurement, not the canonical definition): the
+ * dot is summed in FP32 in dimension order, rounding after every add, as a
+ * float pipeline without exact accumulation would; the products themselves
+ * (an 8-bit significand times an integer below 2^9) are exact in FP32. */
+static int g_fp32_acc = 0;
+void skv_oracle_set_fp32_accumulation(int on) { g_fp32_acc = on != 0; }
+
+static float fp32_dot(const float *row, int e_add, const int32_t *w) {
+    const float scale = ldexpf(1.0f, e_add);
+    float acc = 0.0f;
+    for (int d = 0; d < D; ++d) {
+        const float p = row[d] * scale * (float)w[d];
+        acc = acc + p;
+    }
+    return acc;
+}
+
 static inline float exact_dot(const int64_t *X, int32_t shift, const float *row, int e_add, const int32_t *w) {
+    if (g_fp32_acc) return fp32_dot(row, e_add, w);
     if (g_unflushed) return unflushed_dot(row, e_add, w);
     int64_t acc = 0;
     for (int d = 0; d < D; ++d) acc += X[d] * (int64_t)w[d];
