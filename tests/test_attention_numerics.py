@@ -17,9 +17,8 @@ import pytest
 import torch
 
 from oracle import oracle as O
-from tests.helpers import Case, bits
+from tests.helpers import bits
 
-T, NPROBE = 131072, 384
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
 
 
@@ -51,9 +50,9 @@ def _attend(q_bits, kk, vv):
 
 
 @pytest.fixture(scope="module")
-def case():
+def case(headline_case):
     O.set_threads(8)
-    yield Case(context=T, nprobe=NPROBE, seed=1000, components=256)
+    yield headline_case
     O.set_threads(1)
 
 

@@ -19,16 +19,13 @@ import pytest
 import torch
 
 from oracle import oracle as O
-from tests.helpers import Case, bits
-
-T, NPROBE = 131072, 384
+from tests.helpers import bits
 
 
 @pytest.fixture(scope="module")
-def layer():
+def layer(headline_case):
     O.set_threads(8)
-    case = Case(context=T, nprobe=NPROBE, seed=1000, components=256)
-    yield case
+    yield headline_case
     O.set_unflushed(False)
     O.set_threads(1)
 

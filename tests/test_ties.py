@@ -15,15 +15,15 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests.helpers import Case, bits
+from tests.helpers import bits
 
-T, NPROBE, QUERIES = 131072, 384, 12
+QUERIES = 12
 
 
 @pytest.fixture(scope="module")
-def case():
+def case(headline_case):
     O.set_threads(8)
-    yield Case(context=T, nprobe=NPROBE, seed=1000, components=256)
+    yield headline_case
     O.set_tie_high(False)
     O.set_threads(1)
 
