@@ -1,6 +1,6 @@
 """Build the in-tree CUDA library (sm_100a) with nvcc.
 
-``python -m seoulkv_b200._build`` (or ``__graft_entry__.build()``) compiles
+``python seoulkv_b200/_build.py [--force] [-v]`` (or ``__graft_entry__.build()``) compiles
 ``csrc/*.cu`` into ``seoulkv_b200/_lib/libseoulkv_b200.so``.  The library is
 built in the source tree so it travels with the repository to a GPU host.
 """
